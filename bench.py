@@ -1,0 +1,284 @@
+"""Benchmark of the B200 quantizer: Gweights/s quantized to IQ2_XXS and IQ1_M at 1/8 of a B200 box (one GPU).
+
+Workload (the metric's own configuration): the MoE expert tensor of 384 experts x 2048 x 7168
+stored as MXFP4, sharded 48 experts a GPU (1/8 of the box). A step re-quantizes this GPU's 48 experts from their
+MXFP4 bytes to IQ2_XXS and to IQ1_M, each expert with its own imatrix row; the source is decoded inside the
+quantize kernels. Inputs are seeded synthetic data with the config's distributions (workloads.config2); 374 MB of
+MXFP4 a GPU, larger than the 126 MB L2, so every step streams its input from HBM.
+
+  value  device-resident: source and imatrix already in HBM, the kernels timed with CUDA events on their stream
+  e2e    the same step through the host C ABI (gpuq_requantize_batch) from pinned host memory: host->device copies,
+         kernels and device->host copies inside the timed region (timed on the host around the synchronous call)
+Multi-GPU (torchrun, one rank a GPU): each rank takes its own 48 experts, no collective on the data path
+("scaling": "weak"); rank times are combined by max. `--impl reference` times the reference's own CPU code
+(trench-gguf's block functions compiled for the host, oracle/_ref) on a bounded sample with every host core.
+"""
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "trench-gguf_b200")
+sys.path.insert(0, PKG)
+
+EXPERTS_PER_GPU, ROWS, COLS = 48, 2048, 7168
+TYPES = {"iq2_xxs": 16, "iq1_m": 29, "iq1_s": 19, "iq2_xs": 17, "iq2_s": 22}
+METRIC = "Gweights/s quantized (IQ2_XXS, IQ1_M) at 1/8 B200, byte-identical to ggml"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--types", default="iq2_xxs,iq1_m")
+    ap.add_argument("--experts", type=int, default=EXPERTS_PER_GPU)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    return ap.parse_args()
+
+
+def load_ops():
+    p = os.path.join(PKG, "op_counts.json")
+    return json.load(open(p)) if os.path.exists(p) else {}
+
+
+class Clocks:
+    """nvidia-smi sampled every 200 ms while the timed region runs"""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.Q,
+                                       "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                                      stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.p:
+            self.p.terminate()
+            self.p.wait()
+
+    def summary(self):
+        self.f.flush()
+        rows = [r.split(",") for r in open(self.f.name).read().strip().splitlines() if r.count(",") >= 8]
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": float(rows[0][2]),
+                "reasons": reasons, "samples": len(rows)}
+
+
+def fp32_peak_tflops(dev):
+    """non-FMA FP32 issue rate (FADD + FMUL, one op a lane a clock) measured by trench-gguf_b200/peak.cu"""
+    lib = ctypes.CDLL(os.path.join(PKG, "libgpuq_peak.so"))
+    lib.peak_fp32_ops_per_s.restype = ctypes.c_double
+    lib.peak_fp32_ops_per_s.argtypes = [ctypes.c_int]
+    return lib.peak_fp32_ops_per_s(dev) / 1e12
+
+
+def cpu_baseline(types, sample_rows, seed=102):
+    """the reference's own block functions on this host's cores (oracle/_ref), else the C restatement; one expert's
+    first `sample_rows` rows of the config-2 shape, MXFP4 -> each type"""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+    import workloads
+    kind = "reference" if orc.available("reference") else "port"
+    chk = orc.Checker("reference" if kind == "reference" else "oracle", os.path.join(PKG, "gpuq_tables.bin"))
+    raw, im = workloads.config2(experts=1, rows=sample_rows, cols=COLS, seed=seed)
+    x = chk.decode(39, raw, sample_rows * COLS).reshape(1, sample_rows, COLS)
+    threads = os.cpu_count() or 1
+    t0 = time.perf_counter()
+    for name in types:
+        chk.quantize(TYPES[name], x, im, threads=threads)
+    dt = time.perf_counter() - t0
+    n = len(types) * sample_rows * COLS
+    return {"value": n / dt / 1e9, "unit": "Gweights/s", "cores": threads, "kind": kind,
+            "sample": "%d rows x %d of one expert (MXFP4 -> %s), %.1f s" % (sample_rows, COLS, "+".join(types), dt)}
+
+
+def run_reference(args, rank):
+    types = args.types.split(",")
+    if rank != 0:
+        return
+    for _ in range(args.warmup):
+        cpu_baseline(types, 64)
+    vals = []
+    for _ in range(args.steps):
+        vals.append(cpu_baseline(types, 256))
+    v = statistics.median([r["value"] for r in vals])
+    cb = dict(vals[-1])
+    cb["value"] = v
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "Gweights/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * 256 * COLS * len(types) / (v * 1e9),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (config 2 distributions, seeded)",
+            "config": {"workload": "config 2 sample: 256 rows of one 2048x7168 MXFP4 expert -> " + "+".join(types),
+                       "threads": cb["cores"]},
+            "cpu_baseline": cb, "e2e": {"value": v, "unit": "Gweights/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank)
+    import torch
+    import gpuq
+    import workloads
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    types = args.types.split(",")
+    g = gpuq.Gpuq(device=local)
+    L = g.lib
+    E = args.experts
+    raw_np, im_np = workloads.config2(experts=E, rows=ROWS, cols=COLS, seed=102 + rank)
+    nw = E * ROWS * COLS
+    raw = torch.from_numpy(raw_np.reshape(-1)).to(dev)
+    im = torch.from_numpy(im_np).to(dev)
+    outs = {t: torch.empty(nw // 256 * g.block_bytes(TYPES[t]), dtype=torch.uint8, device=dev) for t in types}
+    stream = torch.cuda.Stream(device=dev)
+    sh = stream.cuda_stream
+
+    def launch(t):
+        n = L.gpuq_requantize_dev(39, ctypes.c_void_p(raw.data_ptr()), TYPES[t], ctypes.c_void_p(outs[t].data_ptr()),
+                                  E, ROWS, COLS, ctypes.c_void_p(im.data_ptr()), sh)
+        if n != outs[t].numel():
+            raise RuntimeError("gpuq_requantize_dev %s: %s" % (t, g.error()))
+
+    def barrier():
+        if dist:
+            dist.barrier()
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            for t in types:
+                launch(t)
+    torch.cuda.synchronize()
+    ev = {t: [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+          for t in types}
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for k in range(args.steps):
+                for t in types:
+                    ev[t][k][0].record(stream)
+                    launch(t)
+                    ev[t][k][1].record(stream)
+            stop.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    clocks = clk.summary()
+    ms = start.elapsed_time(stop)
+    per_type_ms = {t: sum(a.elapsed_time(b) for a, b in ev[t]) / args.steps for t in types}
+    if L.gpuq_status(1) != 0:
+        raise RuntimeError("device status set during the bench")
+    # max over ranks
+    tmax = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+    ms = float(tmax.item())
+    total_w = world * E * ROWS * COLS * len(types) * args.steps
+    value = total_w / (ms / 1e3) / 1e9
+    # e2e through the host C ABI from pinned memory
+    e2e = None
+    if not args.no_e2e:
+        hraw = torch.from_numpy(raw_np.reshape(-1)).pin_memory()
+        hout = {t: torch.empty(outs[t].numel(), dtype=torch.uint8).pin_memory() for t in types}
+        him = np.ascontiguousarray(im_np)
+
+        def host_step():
+            for t in types:
+                n = L.gpuq_requantize_batch(39, ctypes.c_void_p(hraw.data_ptr()), TYPES[t],
+                                            ctypes.c_void_p(hout[t].data_ptr()), E, ROWS, COLS, him.ctypes.data)
+                if n != hout[t].numel():
+                    raise RuntimeError("gpuq_requantize_batch %s: %s" % (t, g.error()))
+        for _ in range(max(1, args.warmup - 1)):
+            host_step()
+        barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            host_step()
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        tm = torch.tensor([dt], dtype=torch.float64, device=dev)
+        if dist:
+            dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+        dt = float(tm.item())
+        for t in types:   # the host path wrote the same bytes as the device path
+            if not torch.equal(hout[t], outs[t].cpu()):
+                raise RuntimeError("host and device paths differ for %s" % t)
+        e2e = {"value": total_w / dt / 1e9, "unit": "Gweights/s", "timing": "host clock around the synchronous calls",
+               "h2d_bytes_per_step": len(types) * (raw_np.nbytes + im_np.nbytes),
+               "d2h_bytes_per_step": sum(int(o.numel()) for o in outs.values())}
+    if rank != 0:
+        if dist:
+            dist.destroy_process_group()
+        return
+    ops = load_ops()
+    top = max(types, key=lambda t: per_type_ms[t])
+    roof = None
+    try:
+        peak = fp32_peak_tflops(local)
+        peak_src = "measured in this run (trench-gguf_b200/peak.cu: FADD/FMUL issue rate)"
+    except OSError:
+        peak, peak_src = None, "unavailable"
+    opw = ops.get(top.upper(), {}).get("ops_per_weight")
+    if opw and peak:
+        ach = opw * E * ROWS * COLS / (per_type_ms[top] / 1e3) / 1e12
+        roof = {"bound": "fp32", "kernel": top, "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
+                "peak_source": peak_src, "ops_per_weight": opw, "traffic": None}
+    cb = None
+    if not args.no_cpu and world == 1:
+        cb = cpu_baseline(types, 512)
+    line = {"metric": METRIC, "value": value, "unit": "Gweights/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (config 2 distributions, seeded per rank)",
+            "config": {"workload": "config 2 shard: %d experts x %d x %d MXFP4 a GPU -> %s" % (E, ROWS, COLS, "+".join(types)),
+                       "experts_per_gpu": E, "parallelism": "expert-sharded x%d" % world,
+                       "l2": "inputs (%d MB a GPU) larger than L2" % (raw_np.nbytes // 2**20)},
+            "per_type": {t: {"ms": per_type_ms[t], "gweights_s": E * ROWS * COLS / (per_type_ms[t] / 1e3) / 1e9} for t in types},
+            "gpu_launches": len(types) * args.steps, "e2e": e2e, "roofline": roof, "cpu_baseline": cb, "clocks": clocks}
+    print(json.dumps(line), flush=True)
+    if dist:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,100 @@
+/* include/gpuq.h - C ABI of libgpuq_cuda.so, the B200 (sm_100a) quantizer library.
+ *
+ * A drop-in replacement for trench-gguf's gpuq library: the first twelve entry points have the signatures, argument
+ * meaning and return conventions of trench-gguf gpuq/gpuq.hip (cited per entry), so its ctypes callers
+ * (tools/requant_experts.py, tools/convert_hf.py, tools/requant_table.py, tools/ldlq.py, gpuq/test_gpuq.py) load it
+ * unchanged through GPUQ_LIB / GPUQ_DIR. Outputs are byte-identical to ggml_quantize_chunk / ggml's to_float.
+ *
+ * Types (ggml type ids): IQ2_XXS 16, IQ2_XS 17, IQ3_XXS 18, IQ1_S 19, IQ4_NL 20, IQ3_S 21, IQ2_S 22, IQ4_XS 23,
+ * IQ1_M 29, Q8_0 8, Q2_K 10, Q3_K 11, Q4_K 12, Q5_K 13, Q6_K 14. Sources: F32 0, F16 1, Q8_0 8, BF16 30, MXFP4 39.
+ *
+ * Errors: the init functions return a non-zero code, every other entry returns 0 bytes; gpuq_last_error() then
+ * says why (an extension). Nothing traps the GPU: impossible search states are reported through gpuq_status().
+ */
+#ifndef GPUQ_H
+#define GPUQ_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Reads the tables file (trench-gguf gpuq_tables.bin format) and prepares device `device`, which becomes the
+ * current device and the one the host API uses. 0 ok; 1 no such device, 2 cannot open, 3 short or corrupt file,
+ * 4 allocation failed, 5 no tables. Replaces gpuq_init, gpuq/gpuq.hip:2059-2080. */
+int gpuq_init(const char * tables, int device);
+
+/* Bytes of one block of `type`, 0 for a type this library does not produce. Replaces gpuq.hip:2082-2101. */
+size_t gpuq_block_bytes(int type);
+
+/* 1 when gpuq_quantize* takes `type` with (with_imatrix = 1) or without (0) an importance matrix.
+ * Replaces gpuq.hip:2213-2215. */
+int gpuq_can_quantize(int type, int with_imatrix);
+
+/* nrow x n_per_row float32 host weights -> host bytes; imatrix: n_per_row weights or NULL (k-quants, Q8_0, IQ4_*).
+ * Returns the bytes written, 0 on error. Replaces gpuq.hip:2228-2232. */
+size_t gpuq_quantize(int type, const float * src, void * dst, int64_t nrow, int64_t n_per_row, const float * imatrix);
+
+/* nmat matrices of nrow x n_per_row; matrix m weighted by imatrix row m (imatrix: nmat x n_per_row or NULL).
+ * Replaces gpuq.hip:2217-2226. */
+size_t gpuq_quantize_batch(int type, const float * src, void * dst, int64_t nmat, int64_t nrow, int64_t n_per_row,
+                           const float * imatrix);
+
+/* 1 when the source type can be decoded on the GPU (F32, F16, BF16, Q8_0, MXFP4). Replaces gpuq.hip:2235. */
+int gpuq_can_dequantize(int src);
+
+/* Source tensor bytes of ggml type `src` (host) -> quantized `type` (host), decoded on the GPU.
+ * Replaces gpuq.hip:2252-2255. */
+size_t gpuq_requantize(int src, const void * raw, int type, void * dst, int64_t nrow, int64_t n_per_row,
+                       const float * imatrix);
+
+/* The batched form: nmat matrices, matrix m weighted by imatrix row m; nmat*nrow*n_per_row % 32 == 0.
+ * Replaces gpuq.hip:2237-2250. */
+size_t gpuq_requantize_batch(int src, const void * raw, int type, void * dst, int64_t nmat, int64_t nrow,
+                             int64_t n_per_row, const float * imatrix);
+
+/* Device API: nblocks contiguous 256-weight super-blocks of d_x (float32, device) -> d_dst (device); block b takes
+ * the 256 importance weights d_qw + ((b % qw_mod) / qw_div) * 256. The 256-block i-quants only (not IQ4_NL, not the
+ * k-quants), as the reference. On `stream` (a cudaStream_t), no synchronisation. Returns nblocks * block bytes, 0
+ * on a bad argument or launch error. Replaces gpuq_quantize_dev, gpuq.hip:2279-2289. */
+size_t gpuq_quantize_dev(int type, const float * d_x, void * d_dst, int64_t nblocks, const float * d_qw,
+                         int64_t qw_mod, int64_t qw_div, void * stream);
+
+/* 1 when gpuq_dequantize_dev decodes `type` (the seven grid i-quants and IQ4_XS). Replaces gpuq.hip:2291-2299. */
+int gpuq_can_dequantize_type(int type);
+
+/* ggml's to_float on the device: nblocks super-blocks -> nblocks * 256 floats, bit for bit.
+ * Replaces gpuq.hip:2301-2320. */
+size_t gpuq_dequantize_dev(int type, const void * d_q, float * d_out, int64_t nblocks, void * stream);
+
+/* n values of source type `src` (device bytes) -> n floats (device); n % 32 == 0. Replaces gpuq.hip:2322-2328. */
+size_t gpuq_dequantize_src_dev(int src, const void * d_raw, float * d_out, int64_t n, void * stream);
+
+/* ---- extensions (no counterpart in the reference; callers find them with hasattr) ---- */
+
+/* Why the last call on this thread failed (empty if it did not). */
+const char * gpuq_last_error(void);
+
+/* The current device's status word: bit 0 a neighbour search found no finite candidate, bit 1 a final code fell
+ * off the grid (ggml would trap; both mean non-finite input). reset != 0 clears it. Synchronises the device. */
+unsigned gpuq_status(int reset);
+
+/* gpuq_init on several devices: the host API then shards every call over them (whole matrices - experts - or row
+ * ranges of one matrix, contiguous slices of the output, no collective), one host thread a device.
+ * Same return codes as gpuq_init; devices[0] becomes the current device. */
+int gpuq_init_devices(const char * tables, const int * devices, int ndev);
+
+/* How many devices the host API shards over (0 before gpuq_init). */
+int gpuq_device_count(void);
+
+/* The device-pointer form of gpuq_requantize_batch: source bytes of type `src` already on the current device ->
+ * d_dst, matrix m weighted by d_imatrix row m (nmat x n_per_row floats, device; NULL for the no-imatrix types).
+ * Decodes inside the quantize kernel; on `stream`, no synchronisation, no library scratch. */
+size_t gpuq_requantize_dev(int src, const void * d_raw, int type, void * d_dst, int64_t nmat, int64_t nrow,
+                           int64_t n_per_row, const float * d_imatrix, void * stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,198 @@
+"""GPU parity: the sm_100a library through its C ABI against the reference's golden vectors and the oracle.
+
+The bar is byte identity: every block the GPU writes equals the block ggml (here: the reference's code, and the C
+restatement pinned to it) writes for the same weights and importance matrix.
+"""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+
+import gpuq as G
+import oracle as orc
+import workloads
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "golden.npz")
+TYPES = orc.TYPES
+NOIM = {"Q8_0", "Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K", "IQ4_NL", "IQ4_XS"}
+MODES = [(n, m) for n in TYPES for m in ([] if n == "Q8_0" else [1]) + ([0] if n in NOIM else [])]
+
+
+@pytest.fixture(scope="module")
+def golden():
+    return dict(np.load(GOLDEN))
+
+
+def ndiff(a, b, bb):
+    assert a.size == b.size
+    return int((a.reshape(-1, bb) != b.reshape(-1, bb)).any(1).sum())
+
+
+@pytest.mark.parametrize("name,mode", MODES)
+def test_golden_selftest(gpuq, golden, name, mode):
+    t = TYPES[name]
+    got = gpuq.quantize(t, golden["selftest_x"], golden["selftest_im"] if mode else None)
+    assert ndiff(got, golden["selftest_%s_%d" % (name, mode)], gpuq.block_bytes(t)) == 0
+
+
+def test_golden_configs(gpuq, golden):
+    g = golden
+    assert np.array_equal(gpuq.quantize(16, g["config1_x"][None], g["config1_im"][None]), g["config1_IQ2_XXS"])
+    for name in ("IQ1_S", "IQ1_M"):
+        got = gpuq.requantize(39, g["config2_raw"], TYPES[name], (2, 2, 7168), g["config2_im"])
+        assert np.array_equal(got, g["config2_%s" % name]), name
+    for name in ("IQ2_XS", "IQ2_S"):
+        got = gpuq.requantize(30, g["config3_raw"], TYPES[name], (2, 2, 7168), g["config3_im"])
+        assert np.array_equal(got, g["config3_%s" % name]), name
+    for name in ("Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K", "Q8_0"):
+        for m in ([] if name == "Q8_0" else [1]) + [0]:
+            got = gpuq.requantize(30, g["config4_raw"], TYPES[name], (1, 2, 28672), g["config4_im"][None] if m else None)
+            assert np.array_equal(got, g["config4_%s_%d" % (name, m)]), (name, m)
+
+
+@pytest.mark.parametrize("name,mode", MODES)
+def test_selftest_vs_oracle(gpuq, oracle, selftest_inputs, name, mode):
+    """the reference self-test's four matrices (64 x 2304 each) in one batch call, each with its imatrix row"""
+    xs, ims = selftest_inputs
+    t = TYPES[name]
+    want = oracle.quantize(t, xs, ims if mode else None, threads=8)
+    got = gpuq.quantize(t, xs, ims if mode else None)
+    assert ndiff(got, want, gpuq.block_bytes(t)) == 0
+    # one matrix a call (gpuq_quantize) gives the same bytes as its slice of the batch
+    one = np.empty(want.size // 4, np.uint8)
+    n = gpuq.lib.gpuq_quantize(t, xs[2].ctypes.data, one.ctypes.data, xs.shape[1], xs.shape[2],
+                               ims[2].ctypes.data if mode else None)
+    assert n == one.size and np.array_equal(one, want[2 * one.size:3 * one.size])
+
+
+@pytest.mark.parametrize("src", ["F16", "BF16", "Q8_0", "MXFP4"])
+@pytest.mark.parametrize("name", ["IQ2_XXS", "IQ1_M", "IQ4_XS", "Q4_K", "Q8_0"])
+def test_requantize_sources(gpuq, oracle, golden, src, name):
+    """source bytes decoded inside the quantize kernel == ggml's to_float then ggml_quantize_chunk"""
+    raw = golden["decode_%s_raw" % src]
+    x = oracle.decode(orc.SOURCES[src], raw, 4 * 1024).reshape(1, 4, 1024)
+    t = TYPES[name]
+    im = golden["selftest_im"][:1]
+    want = oracle.quantize(t, x, None if name == "Q8_0" else im)
+    got = gpuq.requantize(orc.SOURCES[src], raw, t, (1, 4, 1024), None if name == "Q8_0" else im)
+    assert np.array_equal(got, want)
+
+
+def test_chunked_pipeline_matches_one_chunk(gpuq, oracle, monkeypatch):
+    """many pipeline chunks (whole matrices and row ranges of one matrix) == the oracle"""
+    raw, im = workloads.config3(experts=3, rows=16, cols=7168, seed=5)
+    x = oracle.decode(30, raw, raw.size).reshape(3, 16, 7168)
+    want = oracle.quantize(TYPES["IQ2_S"], x, im, threads=8)
+    monkeypatch.setenv("GPUQ_CHUNK_MW", "1")     # 1 M weights a chunk: 3 chunks of whole experts... and rows
+    got = gpuq.requantize(30, raw, TYPES["IQ2_S"], (3, 16, 7168), im)
+    assert np.array_equal(got, want)
+    x1 = np.ascontiguousarray(np.concatenate(list(x), 0)[None])          # one 48-row matrix: row-range chunks
+    want1 = oracle.quantize(TYPES["IQ2_S"], x1, im[:1], threads=8)
+    monkeypatch.setenv("GPUQ_CHUNK_MW", "1")
+    assert np.array_equal(gpuq.quantize(TYPES["IQ2_S"], x1, im[:1]), want1)
+
+
+def test_pinned_host_buffers(gpuq, oracle):
+    import torch
+    raw, im = workloads.config2(experts=2, rows=8, cols=7168, seed=6)
+    src = torch.from_numpy(raw.reshape(-1).copy()).pin_memory()
+    nb = 2 * 8 * 7168 // 256
+    dst = torch.empty(nb * 56, dtype=torch.uint8).pin_memory()
+    got = gpuq.lib.gpuq_requantize_batch(39, src.data_ptr(), 29, dst.data_ptr(), 2, 8, 7168, im.ctypes.data)
+    assert got == nb * 56, gpuq.error()
+    x = oracle.decode(39, raw, raw.size // 17 * 32).reshape(2, 8, 7168)
+    assert np.array_equal(dst.numpy(), oracle.quantize(29, x, im))
+
+
+def dev_ptr(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def test_device_api_quantize_dequantize(gpuq, oracle):
+    """gpuq_quantize_dev's block -> importance-row addressing (qw_mod, qw_div) and gpuq_dequantize_dev == to_float"""
+    import torch
+    rng = np.random.default_rng(11)
+    B, rows = 2, 6
+    x = (rng.standard_t(4, (B * rows, 256)) * 0.02).astype(np.float32)
+    qw = rng.gamma(1.0, 1.0, (B, 256)).astype(np.float32)
+    st = torch.cuda.current_stream().cuda_stream
+    for name in ("IQ2_XXS", "IQ2_XS", "IQ2_S", "IQ3_XXS", "IQ3_S", "IQ1_S", "IQ1_M", "IQ4_XS"):
+        t = TYPES[name]
+        bb = gpuq.block_bytes(t)
+        dx = torch.from_numpy(x).cuda()
+        dq = torch.from_numpy(qw).cuda()
+        out = torch.zeros(B * rows * bb, dtype=torch.uint8, device="cuda")
+        n = gpuq.lib.gpuq_quantize_dev(t, dev_ptr(dx), dev_ptr(out), B * rows, dev_ptr(dq), B * rows, rows, st)
+        assert n == B * rows * bb, gpuq.error()
+        want = oracle.quantize_blocks(t, x, qw, B * rows, rows)
+        torch.cuda.synchronize()
+        got = out.cpu().numpy()
+        assert np.array_equal(got, want), name
+        f = torch.empty(B * rows * 256, dtype=torch.float32, device="cuda")
+        assert gpuq.lib.gpuq_dequantize_dev(t, dev_ptr(out), dev_ptr(f), B * rows, st) == f.numel() * 4
+        torch.cuda.synchronize()
+        assert np.array_equal(f.cpu().numpy().view(np.uint32), oracle.dequantize(t, want).view(np.uint32)), name
+    assert gpuq.lib.gpuq_status(1) == 0
+
+
+@pytest.mark.parametrize("src", ["F16", "BF16", "Q8_0", "MXFP4"])
+def test_device_api_decode(gpuq, golden, src):
+    import torch
+    raw = torch.from_numpy(golden["decode_%s_raw" % src].copy()).cuda()
+    want = golden["decode_%s" % src]
+    f = torch.empty(want.size, dtype=torch.float32, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    assert gpuq.lib.gpuq_dequantize_src_dev(orc.SOURCES[src], dev_ptr(raw), dev_ptr(f), want.size, st) == want.size * 4
+    torch.cuda.synchronize()
+    assert np.array_equal(f.cpu().numpy().view(np.uint32), want.view(np.uint32))
+
+
+def test_config_distributions_vs_oracle(gpuq, oracle):
+    """a few hundred rows from each benchmark config's distribution, target types of that config"""
+    w1, im1 = workloads.config1(rows=64, cols=14336, seed=201)
+    assert np.array_equal(gpuq.quantize(16, w1, im1[None]), oracle.quantize(16, w1, im1[None], threads=8))
+    raw2, im2 = workloads.config2(experts=2, rows=32, cols=7168, seed=202)
+    x2 = oracle.decode(39, raw2, raw2.size // 17 * 32).reshape(2, 32, 7168)
+    for t in (19, 29):
+        assert np.array_equal(gpuq.requantize(39, raw2, t, (2, 32, 7168), im2), oracle.quantize(t, x2, im2, threads=8)), t
+    raw3, im3 = workloads.config3(experts=2, rows=32, cols=2048, seed=203)   # the down-projection row length
+    x3 = oracle.decode(30, raw3, raw3.size).reshape(2, 32, 2048)
+    for t in (17, 22):
+        assert np.array_equal(gpuq.requantize(30, raw3, t, (2, 32, 2048), im3), oracle.quantize(t, x3, im3, threads=8)), t
+
+
+def test_edge_inputs(gpuq, oracle):
+    """zero, constant, huge-dynamic-range, denormal and single-row inputs"""
+    rng = np.random.default_rng(12)
+    x = (rng.standard_normal((8, 512)) * 0.02).astype(np.float32)
+    x[0] = 0
+    x[1] = 0.5
+    x[2, ::7] = 1e-38
+    x[3] *= 1e6
+    x[4, :256] = -np.abs(x[4, :256])
+    x[5] = np.float32(1e-44)
+    im = rng.gamma(1.0, 1.0, 512).astype(np.float32)
+    im[::5] = 0                               # zero importance for some columns
+    for name, t in TYPES.items():
+        modes = ([] if name == "Q8_0" else [1]) + ([0] if name in NOIM else [])
+        for m in modes:
+            want = oracle.quantize(t, x, im[None] if m else None)
+            assert np.array_equal(gpuq.quantize(t, x, im[None] if m else None), want), (name, m)
+    one = x[6:7]
+    assert np.array_equal(gpuq.quantize(16, one, im[None]), oracle.quantize(16, one, im[None]))
+
+
+def test_argument_errors(gpuq):
+    x = np.zeros((2, 300), np.float32)
+    y = np.zeros(1024, np.uint8)
+    im = np.ones(300, np.float32)
+    L = gpuq.lib
+    assert L.gpuq_quantize(16, x.ctypes.data, y.ctypes.data, 2, 300, im.ctypes.data) == 0      # 300 % 256
+    assert b"multiple" in L.gpuq_last_error()
+    assert L.gpuq_quantize(16, x.ctypes.data, y.ctypes.data, 2, 256, None) == 0               # IQ needs imatrix
+    assert L.gpuq_quantize(99, x.ctypes.data, y.ctypes.data, 2, 256, None) == 0
+    assert L.gpuq_requantize(16, x.ctypes.data, 8, y.ctypes.data, 2, 256, None) == 0          # F16? no: src 16
+    assert L.gpuq_can_quantize(16, 0) == 0 and L.gpuq_can_quantize(16, 1) == 1 and L.gpuq_can_quantize(12, 0) == 1

@@ -1,0 +1,110 @@
+"""CPU: the oracle (C restatement, oracle/oracle.c) pinned against the reference's own outputs and gguf-py.
+
+* golden.npz holds outputs of the reference's block functions compiled on the host (tests/golden/make_golden.py);
+* where the reference host build is present (oracle/_ref), the oracle is also compared with it on fresh inputs;
+* gguf-py's Q8_0 quantizer (documented bit-exact with ggml) and its dequantizers of every type are independent pins.
+"""
+import os
+
+import numpy as np
+import pytest
+
+import oracle as orc
+import workloads
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "golden.npz")
+TYPES = orc.TYPES
+NOIM = {"Q8_0", "Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K", "IQ4_NL", "IQ4_XS"}
+MODES = [(n, m) for n in TYPES for m in ([] if n == "Q8_0" else [1]) + ([0] if n in NOIM else [])]
+
+
+@pytest.fixture(scope="module")
+def golden():
+    return dict(np.load(GOLDEN))
+
+
+def blocks_differ(a, b, bb):
+    return int((a.reshape(-1, bb) != b.reshape(-1, bb)).any(1).sum())
+
+
+@pytest.mark.parametrize("name,mode", MODES)
+def test_oracle_selftest_golden(oracle, golden, name, mode):
+    t = TYPES[name]
+    got = oracle.quantize(t, golden["selftest_x"], golden["selftest_im"] if mode else None)
+    assert blocks_differ(got, golden["selftest_%s_%d" % (name, mode)], oracle.block_bytes(t)) == 0
+
+
+def test_oracle_config_golden(oracle, golden):
+    g = golden
+    assert np.array_equal(oracle.quantize(16, g["config1_x"][None], g["config1_im"][None]), g["config1_IQ2_XXS"])
+    x2 = oracle.decode(39, g["config2_raw"], g["config2_raw"].size // 17 * 32).reshape(2, 2, 7168)
+    for name in ("IQ1_S", "IQ1_M"):
+        assert np.array_equal(oracle.quantize(TYPES[name], x2, g["config2_im"]), g["config2_%s" % name]), name
+    x3 = oracle.decode(30, g["config3_raw"], g["config3_raw"].size).reshape(2, 2, 7168)
+    for name in ("IQ2_XS", "IQ2_S"):
+        assert np.array_equal(oracle.quantize(TYPES[name], x3, g["config3_im"]), g["config3_%s" % name]), name
+    x4 = oracle.decode(30, g["config4_raw"], g["config4_raw"].size).reshape(1, 2, 28672)
+    for name in ("Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K", "Q8_0"):
+        for m in ([] if name == "Q8_0" else [1]) + [0]:
+            got = oracle.quantize(TYPES[name], x4, g["config4_im"][None] if m else None)
+            assert np.array_equal(got, g["config4_%s_%d" % (name, m)]), (name, m)
+
+
+@pytest.mark.parametrize("src", ["F16", "BF16", "Q8_0", "MXFP4"])
+def test_oracle_decode_golden(oracle, golden, src):
+    raw = golden["decode_%s_raw" % src]
+    want = golden["decode_%s" % src]
+    assert np.array_equal(oracle.decode(orc.SOURCES[src], raw, want.size).view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("name", ["IQ2_XXS", "IQ2_XS", "IQ2_S", "IQ3_XXS", "IQ3_S", "IQ1_S", "IQ1_M", "IQ4_XS"])
+def test_oracle_dequant_golden_and_gguf(oracle, golden, name):
+    from gguf import quants as gq, GGMLQuantizationType as G
+    q = golden["selftest_%s_1" % name]
+    got = oracle.dequantize(TYPES[name], q)
+    assert np.array_equal(got.view(np.uint32), golden["dequant_%s" % name].view(np.uint32))
+    ref = gq.dequantize(q.reshape(-1, 4 * 1024 // 256 * oracle.block_bytes(TYPES[name]) // 4), G[name])
+    assert np.array_equal(got, ref.reshape(-1).astype(np.float32))
+
+
+def test_oracle_q8_0_matches_gguf(oracle):
+    from gguf import quants as gq, GGMLQuantizationType as G
+    rng = np.random.default_rng(7)
+    x = (rng.standard_t(3, (64, 4096)) * 0.01).astype(np.float32)
+    x[3] = 0
+    x[5, :32] = 1e-30
+    assert np.array_equal(oracle.quantize(8, x), gq.quantize(x, G.Q8_0).reshape(-1))
+
+
+def test_oracle_decode_matches_gguf(oracle):
+    from gguf import quants as gq, GGMLQuantizationType as G
+    rng = np.random.default_rng(8)
+    x = (rng.standard_normal((16, 1024)) * 0.05).astype(np.float32)
+    for src, raw, ref in (
+            (39, gq.quantize(x, G.MXFP4), None), (8, gq.quantize(x, G.Q8_0), None),
+            (30, workloads.bf16_bytes(x), None), (1, x.astype(np.float16), x.astype(np.float16).astype(np.float32))):
+        got = oracle.decode(src, raw, x.size)
+        if ref is None:
+            t = {39: G.MXFP4, 8: G.Q8_0, 30: G.BF16}[src]
+            ref = gq.dequantize(np.ascontiguousarray(raw).view(np.uint8).reshape(16, -1) if src != 30 else raw.view(np.uint8).reshape(16, -1), t)
+        assert np.array_equal(got, np.asarray(ref, dtype=np.float32).reshape(-1)), src
+
+
+@pytest.mark.parametrize("name,mode", MODES)
+def test_oracle_matches_reference_build(oracle, reference, name, mode):
+    """fresh inputs (all four self-test matrices at 32 x 2304) against the reference's own code"""
+    xs, ims = workloads.selftest(rows=32, cols=2304, seed=99)
+    t = TYPES[name]
+    a = oracle.quantize(t, xs, ims if mode else None, threads=4)
+    b = reference.quantize(t, xs, ims if mode else None, threads=4)
+    assert blocks_differ(a, b, oracle.block_bytes(t)) == 0
+
+
+def test_oracle_device_addressing_matches_reference(oracle, reference):
+    """gpuq_quantize_dev's importance addressing: block b takes qw row (b % qw_mod) // qw_div"""
+    rng = np.random.default_rng(3)
+    x = (rng.standard_normal((12, 256)) * 0.03).astype(np.float32)
+    qw = rng.gamma(1.0, 1.0, (3, 256)).astype(np.float32)
+    for t in (16, 29, 23):
+        a = oracle.quantize_blocks(t, x, qw, 12, 4)
+        assert np.array_equal(a, reference.quantize_blocks(t, x, qw, 12, 4))

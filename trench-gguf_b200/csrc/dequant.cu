@@ -1,0 +1,190 @@
+// dequant.cu - ggml's to_float of the i-quant types (dequantize_row_iq*, trench-gguf gpuq.hip:1850-2028) and the
+// source decoder (kdq, gpuq.hip:2123-2141), HBM-bound.
+//
+// Layout: one warp a 256-weight super-block, lane l producing weights 8l..8l+7 (its 32-weight sub-block l/4 and
+// 8-weight group l%4), stored as two 16-byte writes: a warp writes its 1 KiB of floats fully coalesced. Every
+// value is computed with ggml's expression in ggml's operand order; all products are exact in float32, so the
+// result equals ggml's to_float bit for bit.
+#include "common.cuh"
+#include "source.cuh"
+#include "kernels.h"
+
+namespace gq {
+namespace {
+
+__device__ __forceinline__ uint8_t ksigns(uint32_t k) { return (uint8_t) (k | ((__popc(k) & 1) << 7)); }
+__device__ __forceinline__ float sgn(uint32_t s, int j) { return (s >> j) & 1 ? -1.f : 1.f; }
+__device__ __forceinline__ uint32_t ld_u16(const uint8_t * p) { return (uint32_t) p[0] | ((uint32_t) p[1] << 8); }
+__device__ __forceinline__ uint32_t ld_u32(const uint8_t * p) {
+    return (uint32_t) p[0] | ((uint32_t) p[1] << 8) | ((uint32_t) p[2] << 16) | ((uint32_t) p[3] << 24);
+}
+__device__ __forceinline__ uint8_t gbyte(const uint64_t * grid, int gi, int j) {
+    return (uint8_t) (__ldg(grid + gi) >> (8 * j));
+}
+
+__constant__ int8_t c_iq4nl[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+
+template <int T>
+__device__ __forceinline__ void dq8(const uint8_t * q, int lane, const uint64_t * G, float * y) {
+    const int ib = lane >> 2, l = lane & 3;
+    if constexpr (T == IQ4_XS) {
+        const float d = half_to_float((uint16_t) ld_u16(q));
+        const uint32_t sh = ld_u16(q + 2);
+        const int ls = ((q[4 + ib / 2] >> (4 * (ib % 2))) & 0xf) | (((sh >> (2 * ib)) & 3) << 4);
+        const float dl = d * (ls - 32);
+        const int j0 = 8 * (l & 1), hi = l >> 1;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint8_t v = q[8 + 16 * ib + j0 + j];
+            y[j] = dl * c_iq4nl[hi ? v >> 4 : v & 0xf];
+        }
+    } else if constexpr (T == IQ1_M) {
+        const uint32_t s0 = ld_u16(q + 48), s1 = ld_u16(q + 50), s2 = ld_u16(q + 52), s3 = ld_u16(q + 54);
+        const uint16_t s16 = (uint16_t) ((s0 >> 12) | ((s1 >> 8) & 0x00f0) | ((s2 >> 4) & 0x0f00) | (s3 & 0xf000));
+        const float dd = half_to_float(s16);
+        const uint32_t sc = ld_u16(q + 48 + 2 * (ib / 2));
+        const float dl = l < 2 ? dd * (2 * ((sc >> (6 * (ib % 2))) & 0x7) + 1) : dd * (2 * ((sc >> (6 * (ib % 2) + 3)) & 0x7) + 1);
+        const uint8_t * qs = q + 4 * ib, * qh = q + 32 + 2 * ib;
+        const uint8_t h = qh[l / 2];
+        const int gi = qs[l] | ((l % 2 ? (h << 4) : (h << 8)) & 0x700);
+        const float delta = (h & (l % 2 ? 0x80 : 0x08)) ? -0.125f : 0.125f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) y[j] = dl * ((float) (int8_t) gbyte(G, gi, j) + delta);
+    } else {
+        const float d = half_to_float((uint16_t) ld_u16(q));
+        if constexpr (T == IQ2_XXS) {
+            const uint32_t a0 = ld_u32(q + 2 + 8 * ib), a1 = ld_u32(q + 6 + 8 * ib);
+            const float db = d * (0.5f + (a1 >> 28)) * 0.25f;
+            const int gi = (a0 >> (8 * l)) & 255;
+            const uint8_t s = ksigns((a1 >> (7 * l)) & 127);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) y[j] = db * gbyte(G, gi, j) * sgn(s, j);
+        } else if constexpr (T == IQ2_XS) {
+            const uint8_t sc = q[66 + ib];
+            const float db = d * (0.5f + (l < 2 ? (sc & 0xf) : (sc >> 4))) * 0.25f;
+            const uint32_t v = ld_u16(q + 2 + 2 * (4 * ib + l));
+            const int gi = v & 511;
+            const uint8_t s = ksigns(v >> 9);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) y[j] = db * gbyte(G, gi, j) * sgn(s, j);
+        } else if constexpr (T == IQ2_S) {
+            const uint8_t sc = q[74 + ib];
+            const float db = d * (0.5f + (l < 2 ? (sc & 0xf) : (sc >> 4))) * 0.25f;
+            const int gi = q[2 + 4 * ib + l] | ((q[66 + ib] << (8 - 2 * l)) & 0x300);
+            const uint8_t s = q[34 + 4 * ib + l];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) y[j] = db * gbyte(G, gi, j) * sgn(s, j);
+        } else if constexpr (T == IQ3_XXS) {
+            const uint32_t a = ld_u32(q + 66 + 4 * ib);
+            const float db = d * (0.5f + (a >> 28)) * 0.5f;
+            const uint8_t s = ksigns((a >> (7 * l)) & 127);
+            const int g1 = q[2 + 8 * ib + 2 * l], g2 = q[2 + 8 * ib + 2 * l + 1];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                y[j] = db * gbyte(G, g1, j) * sgn(s, j);
+                y[j + 4] = db * gbyte(G, g2, j) * sgn(s, j + 4);
+            }
+        } else if constexpr (T == IQ3_S) {
+            const uint8_t sc = q[106 + ib / 2];
+            const float db = d * (1 + 2 * ((ib % 2) ? (sc >> 4) : (sc & 0xf)));
+            const uint8_t hb = q[66 + ib];
+            const int g1 = q[2 + 8 * ib + 2 * l] | ((hb << (8 - 2 * l)) & 256);
+            const int g2 = q[2 + 8 * ib + 2 * l + 1] | ((hb << (7 - 2 * l)) & 256);
+            const uint8_t s = q[74 + 4 * ib + l];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                y[j] = db * gbyte(G, g1, j) * sgn(s, j);
+                y[j + 4] = db * gbyte(G, g2, j) * sgn(s, j + 4);
+            }
+        } else {   // IQ1_S
+            const uint32_t qh = ld_u16(q + 34 + 2 * ib);
+            const float dl = d * (2 * ((qh >> 12) & 7) + 1);
+            const float delta = qh & 0x8000 ? -0.125f : 0.125f;
+            const int gi = q[2 + 4 * ib + l] | (((qh >> (3 * l)) & 7) << 8);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) y[j] = dl * ((float) (int8_t) gbyte(G, gi, j) + delta);
+        }
+    }
+}
+
+template <int T>
+__global__ void __launch_bounds__(256) k_dequant(const uint8_t * __restrict__ q, float * __restrict__ out,
+                                                 int64_t nblocks, const uint64_t * __restrict__ grid) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = (int64_t) gridDim.x * (blockDim.x >> 5);
+    for (int64_t b = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); b < nblocks; b += nw) {
+        float y[8];
+        dq8<T>(q + b * block_bytes(T), lane, grid, y);
+        float4 * o = reinterpret_cast<float4 *>(out + b * QK + lane * 8);
+        if ((reinterpret_cast<uintptr_t>(out) & 15) == 0) {
+            o[0] = make_float4(y[0], y[1], y[2], y[3]);
+            o[1] = make_float4(y[4], y[5], y[6], y[7]);
+        } else {
+            float * p = out + b * QK + lane * 8;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) p[j] = y[j];
+        }
+    }
+}
+
+template <int SRC>
+__global__ void __launch_bounds__(256) k_decode(const uint8_t * __restrict__ raw, float * __restrict__ out, int64_t n8) {
+    const int64_t stride = (int64_t) gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += stride) {
+        float y[8];
+        decode8<SRC>(raw, i * 8, y);
+        if ((reinterpret_cast<uintptr_t>(out) & 15) == 0) {
+            float4 * o = reinterpret_cast<float4 *>(out + i * 8);
+            o[0] = make_float4(y[0], y[1], y[2], y[3]);
+            o[1] = make_float4(y[4], y[5], y[6], y[7]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) out[i * 8 + j] = y[j];
+        }
+    }
+}
+
+int grid_for(int64_t units, int per_cta) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t need = (units + per_cta - 1) / per_cta;
+    const int64_t cap = (int64_t) sms * 16;   // enough resident CTAs to cover HBM latency; grid-stride beyond
+    return (int) (need < cap ? (need > 0 ? need : 1) : cap);
+}
+
+}  // namespace
+
+cudaError_t launch_dequant(int type, const void * q, float * out, int64_t nblocks, DequantTab tab, cudaStream_t st) {
+    const int g = grid_for(nblocks, 8);
+    const uint8_t * qb = (const uint8_t *) q;
+    switch (type) {
+        case IQ2_XXS: k_dequant<IQ2_XXS><<<g, 256, 0, st>>>(qb, out, nblocks, tab.grid); break;
+        case IQ2_XS:  k_dequant<IQ2_XS><<<g, 256, 0, st>>>(qb, out, nblocks, tab.grid); break;
+        case IQ2_S:   k_dequant<IQ2_S><<<g, 256, 0, st>>>(qb, out, nblocks, tab.grid); break;
+        case IQ3_XXS: k_dequant<IQ3_XXS><<<g, 256, 0, st>>>(qb, out, nblocks, tab.grid); break;
+        case IQ3_S:   k_dequant<IQ3_S><<<g, 256, 0, st>>>(qb, out, nblocks, tab.grid); break;
+        case IQ1_S:   k_dequant<IQ1_S><<<g, 256, 0, st>>>(qb, out, nblocks, tab.grid); break;
+        case IQ1_M:   k_dequant<IQ1_M><<<g, 256, 0, st>>>(qb, out, nblocks, tab.grid); break;
+        case IQ4_XS:  k_dequant<IQ4_XS><<<g, 256, 0, st>>>(qb, out, nblocks, tab.grid); break;
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_decode(int src, const void * raw, float * out, int64_t n, cudaStream_t st) {
+    const int64_t n8 = n / 8;
+    const int g = grid_for(n8, 256);
+    const uint8_t * r = (const uint8_t *) raw;
+    switch (src) {
+        case SRC_F32:   k_decode<SRC_F32><<<g, 256, 0, st>>>(r, out, n8); break;
+        case SRC_F16:   k_decode<SRC_F16><<<g, 256, 0, st>>>(r, out, n8); break;
+        case SRC_BF16:  k_decode<SRC_BF16><<<g, 256, 0, st>>>(r, out, n8); break;
+        case SRC_Q8_0:  k_decode<SRC_Q8_0><<<g, 256, 0, st>>>(r, out, n8); break;
+        case SRC_MXFP4: k_decode<SRC_MXFP4><<<g, 256, 0, st>>>(r, out, n8); break;
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace gq

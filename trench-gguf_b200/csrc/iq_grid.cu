@@ -1,0 +1,518 @@
+// iq_grid.cu - the grid-trial i-quants: IQ2_XXS, IQ2_XS, IQ2_S, IQ3_XXS, IQ3_S.
+//
+// What is computed: ggml's quantize_row_{iq2_xxs,iq2_xs,iq2_s,iq3_xxs,iq3_s}_impl on one 256-weight super-block
+// (trench-gguf gpuq.hip:246-387, :825-969, :691-822, :995-1143, :1146-1283): per sub-block, signs split off (with
+// the even-parity fix for the 7-bit sign fields), 13..31 trial inverse scales, each rounding the magnitudes to the
+// 2l+1 lattice, snapping every off-grid group to its nearest listed codebook neighbour, and scoring the trial by
+// its least-squares scale; the best trial is refined, the groups left off the grid are snapped again with the
+// final scale, and the sub-block scales are coded against the super-block scale.
+//
+// How it runs on sm_100a: one warp a super-block, FP32-ALU bound. Lanes own independent work only:
+//   * elementwise weights and sign groups (8 weights a lane),
+//   * the (sub-block, trial) pairs of the trial search (104..304 a super-block, 32 at a time), each lane running
+//     its trial's groups, neighbour searches and index-ordered sums exactly as ggml does,
+//   * the (sub-block, group) pairs of the re-gridding.
+// ggml's sequential decisions (which trial wins: a strict `>` scan in trial order) are replayed in trial order by
+// one lane per sub-block from the stored per-trial sums, so the choice is bit-identical. Sums that ggml runs in
+// index order (sumx2 over 256, the 16/32-weight sums) run in index order inside one lane.
+#include "common.cuh"
+#include "source.cuh"
+#include "kernels.h"
+
+namespace gq {
+namespace {
+
+template <int T> struct GT;
+template <> struct GT<IQ2_XXS> {   // gpuq.hip:246-387
+    static constexpr int SB = 32, GD = 8, KMAXQ = 3, NTR = 6, SIGMA_X2 = 0, PARITY = 1, QP_FIRST = 1, REGRID_ALL = 1,
+                         REGRID_ANY = 0, INIT_ON = 1, EPS_ZERO = 0;
+    static constexpr float STEP = 0.1f, EPS = 1e-15f;
+};
+template <> struct GT<IQ2_XS> {    // gpuq.hip:825-969
+    static constexpr int SB = 16, GD = 8, KMAXQ = 3, NTR = 9, SIGMA_X2 = 0, PARITY = 1, QP_FIRST = 0, REGRID_ALL = 0,
+                         REGRID_ANY = 1, INIT_ON = 1, EPS_ZERO = 0;
+    static constexpr float STEP = 0.1f, EPS = 1e-15f;
+};
+template <> struct GT<IQ2_S> {     // gpuq.hip:691-822
+    static constexpr int SB = 16, GD = 8, KMAXQ = 3, NTR = 9, SIGMA_X2 = 1, PARITY = 0, QP_FIRST = 0, REGRID_ALL = 0,
+                         REGRID_ANY = 1, INIT_ON = 1, EPS_ZERO = 0;
+    static constexpr float STEP = 0.1f, EPS = 1e-8f;
+};
+template <> struct GT<IQ3_XXS> {   // gpuq.hip:995-1143
+    static constexpr int SB = 32, GD = 4, KMAXQ = 8, NTR = 15, SIGMA_X2 = 1, PARITY = 1, QP_FIRST = 0, REGRID_ALL = 0,
+                         REGRID_ANY = 1, INIT_ON = 1, EPS_ZERO = 0;
+    static constexpr float STEP = 0.2f, EPS = 1e-8f;
+};
+template <> struct GT<IQ3_S> {     // gpuq.hip:1146-1283
+    static constexpr int SB = 32, GD = 4, KMAXQ = 8, NTR = 9, SIGMA_X2 = 1, PARITY = 0, QP_FIRST = 0, REGRID_ALL = 1,
+                         REGRID_ANY = 1, INIT_ON = 0, EPS_ZERO = 1;
+    static constexpr float STEP = 0.2f, EPS = 0.f;
+};
+
+template <int T> struct Shape {
+    using P = GT<T>;
+    static constexpr int NSUB = QK / P::SB;           // sub-blocks a super-block
+    static constexpr int NG = P::SB / P::GD;          // codebook groups a sub-block
+    static constexpr int NT = 2 * P::NTR + 1;         // trials a sub-block
+    static constexpr int NTASK = NSUB * NT;
+    static constexpr int PAD = P::SB + 1;             // padded sub-block stride (conflict-free across sub-blocks)
+    static constexpr int BITS = P::GD == 8 ? 2 : 3;   // packed level bits a dimension
+    static constexpr int NSG = P::SB / 8;             // 8-weight sign bytes a sub-block
+};
+
+// per-warp shared state of one super-block
+template <int T> struct alignas(16) WarpState {
+    using S = Shape<T>;
+    float x[S::NSUB * S::PAD], w[S::NSUB * S::PAD], wa[S::NSUB * S::PAD], xv[S::NSUB * S::PAD];
+    float t_sqx[S::NTASK], t_sq2[S::NTASK];
+    uint16_t t_lev[S::NTASK][S::NG];
+    uint8_t t_on[S::NTASK];
+    float denom[S::NSUB], scale[S::NSUB];
+    uint16_t lev[S::NSUB][S::NG];
+    int32_t gidx[S::NSUB][S::NG];
+    uint8_t signs[S::NSUB][S::NSG];
+    uint8_t skip[S::NSUB], regrid[S::NSUB];
+    uint8_t out[112];
+    float sigma2;
+};
+
+__device__ __forceinline__ int eidx(int sb, int pad, int e) { return (e / sb) * pad + (e % sb); }
+
+// make_qp_quants (gpuq.hip:114-176) on n weights of one sub-block, one lane; returns the scale
+template <int N>
+__device__ float qp_levels(int nmax, const float * x, const float * w) {
+    uint8_t L[N];
+    float mx = 0;
+#pragma unroll
+    for (int i = 0; i < N; ++i) mx = fmaxr(mx, x[i]);
+    if (mx < 1e-15f) return 0.f;
+    float iscale = nmax / mx;
+    const float scale0 = 1 / iscale;
+    float best_mse = 0;
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+        const int l = nearest_int(iscale * x[i]);
+        const float d = x[i] - scale0 * (float) (uint8_t) l;
+        best_mse += w[i] * d * d;
+    }
+    for (int is = -4; is <= 4; ++is) {
+        if (!is) continue;
+        const float iscale_is = (0.1f * is + nmax) / mx;
+        const float scale_is = 1 / iscale_is;
+        float mse = 0;
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            const int l = imin(nmax, nearest_int(iscale_is * x[i]));
+            const float d = x[i] - scale_is * l;
+            mse += w[i] * d * d;
+        }
+        if (mse < best_mse) { best_mse = mse; iscale = iscale_is; }
+    }
+    float sumlx = 0, suml2 = 0;
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+        const int l = imin(nmax, nearest_int(iscale * x[i]));
+        L[i] = (uint8_t) l;
+        sumlx += w[i] * x[i] * l;
+        suml2 += w[i] * l * l;
+    }
+    for (int pass = 0; pass < 5; ++pass) {
+        int changed = 0;
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            float slx = sumlx - w[i] * x[i] * L[i];
+            float sl2 = suml2 - w[i] * L[i] * L[i];
+            if (slx > 0 && sl2 > 0) {
+                const int nl = imin(nmax, nearest_int(x[i] * sl2 / slx));
+                if (nl != L[i]) {
+                    slx += w[i] * x[i] * nl;
+                    sl2 += w[i] * nl * nl;
+                    if (slx * slx * suml2 > sumlx * sumlx * sl2) { L[i] = (uint8_t) nl; sumlx = slx; suml2 = sl2; ++changed; }
+                }
+            }
+        }
+        if (!changed) break;
+    }
+    return suml2 > 0.0f ? sumlx / suml2 : 0.0f;
+}
+
+// the lattice value 2l+1 of a 3-bit level, as a float, by the 2^23 bias (exact, full-rate FADD)
+__device__ __forceinline__ float odd_level(uint32_t l) { return u2f(0x4B000000u + 2 * l + 1) - 8388608.f; }
+
+// Rounds one group to levels with inverse scale id; if the code is off the grid, searches its neighbour list with
+// scale s (iq2_find_best_neighbour gpuq.hip:178-197 / iq3_find_best_neighbour :972-992: weighted squared distance,
+// the first minimum in list order wins). Returns the packed levels, sets *on if the rounded code was on the grid;
+// returns 0xFFFFFFFF when no listed point has a finite distance.
+template <int GD, int KMAXQ>
+__device__ uint32_t group_to_grid(const float * xv, const float * wa, float id, float s, const SearchTab & tab, int * on) {
+    constexpr int BITS = GD == 8 ? 2 : 3;
+    uint32_t lev = 0;
+    int c3 = 0, p3 = 1;
+#pragma unroll
+    for (int i = 0; i < GD; ++i) {
+        const int l = imax(0, imin(KMAXQ - 1, nearest_int(0.5f * (id * xv[i] - 1))));
+        lev |= (uint32_t) l << (BITS * i);
+        c3 += l * p3;
+        p3 *= (GD == 8 ? 3 : 8);
+    }
+    const int m = __ldg(tab.code3 + c3);
+    *on = m >= 0;
+    if (m >= 0) return lev;
+    const uint32_t * lst = tab.neigh + (-m - 1);
+    const int n = (int) __ldg(lst);
+    float best = FLT_MAX;
+    uint32_t bl = 0xFFFFFFFFu;
+    if constexpr (GD == 8) {
+        // the 24 possible per-dimension terms w_i (s q - x_i)^2, q in {1, 3, 5}: each neighbour's distance is then
+        // 8 selects and the same 8 additions in the same order as ggml's loop
+        float t0[8], t1[8], t2[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float d0 = s * 1.f - xv[i], d1 = s * 3.f - xv[i], d2 = s * 5.f - xv[i];
+            t0[i] = wa[i] * d0 * d0; t1[i] = wa[i] * d1 * d1; t2[i] = wa[i] * d2 * d2;
+        }
+        for (int j = 1; j <= n; ++j) {
+            const uint32_t e = __ldg(lst + j);
+            float d2 = 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const uint32_t l = (e >> (2 * i)) & 3u;
+                d2 += l == 0 ? t0[i] : (l == 1 ? t1[i] : t2[i]);
+            }
+            if (d2 < best) { best = d2; bl = e; }
+        }
+    } else {
+        for (int j = 1; j <= n; ++j) {
+            const uint32_t e = __ldg(lst + j);
+            float d2 = 0.f;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float q = odd_level((e >> (3 * i)) & 7u);
+                const float d = s * q - xv[i];
+                d2 += wa[i] * d * d;
+            }
+            if (d2 < best) { best = d2; bl = e; }
+        }
+    }
+    return bl == 0xFFFFFFFFu ? bl : (bl & 0xFFFFu);
+}
+
+template <int GD>
+__device__ __forceinline__ int level_of(uint32_t lev, int i) { return GD == 8 ? (lev >> (2 * i)) & 3 : (lev >> (3 * i)) & 7; }
+
+template <int GD>
+__device__ __forceinline__ int code3_of(uint32_t lev) {
+    if constexpr (GD == 4) return (int) lev;   // base 8 = the packed 3-bit levels
+    int c = 0, p = 1;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) { c += (int) ((lev >> (2 * i)) & 3u) * p; p *= 3; }
+    return c;
+}
+
+// ------------------------------------------------------------------------------------------------ the kernel
+template <int T, int SRC>
+__global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ src, const float * __restrict__ qw,
+                                                 int64_t qw_mod, int64_t qw_div, int64_t qw_mat,
+                                                 uint8_t * __restrict__ out, int64_t nblocks, SearchTab tab,
+                                                 unsigned * status) {
+    using P = GT<T>;
+    using S = Shape<T>;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    WarpState<T> & st = reinterpret_cast<WarpState<T> *>(smem_raw)[wid];
+    const int64_t b = (int64_t) blockIdx.x * (blockDim.x >> 5) + wid;
+    if (b >= nblocks) return;
+
+    // ---- P0: this lane's 8 weights and importances (weights lane*8 .. lane*8+7)
+    float xr[8], qr[8];
+    decode8<SRC>(src, b * QK + lane * 8, xr);
+    load8_f32(qw + ((b / qw_mat) * qw_mod + (b % qw_mod) / qw_div) * QK + lane * 8, qr);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) st.x[eidx(P::SB, S::PAD, lane * 8 + j)] = xr[j];
+    __syncwarp();
+    // ---- P1: sumx2 in index order (one lane)
+    if (lane == 0) {
+        float s2 = 0;
+        for (int e = 0; e < QK; ++e) { const float v = st.x[eidx(P::SB, S::PAD, e)]; s2 += v * v; }
+        st.sigma2 = P::SIGMA_X2 ? 2 * s2 / QK : s2 / QK;
+    }
+    __syncwarp();
+    const float sigma2 = st.sigma2;
+    // ---- P2 + P3: weights, sqrt weights, signs of this lane's 8-weight group
+    {
+        float wr[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            wr[j] = qr[j] * sqrtf(sigma2 + xr[j] * xr[j]);
+            const int ei = eidx(P::SB, S::PAD, lane * 8 + j);
+            st.w[ei] = wr[j];
+            st.wa[ei] = sqrtf(wr[j]);
+        }
+        int nflip = 0;
+        unsigned sg = 0;
+        float xv[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (xr[j] >= 0) xv[j] = xr[j]; else { xv[j] = -xr[j]; ++nflip; sg |= 1u << j; }
+        }
+        if (P::PARITY && (nflip % 2)) {
+            int im = 0;
+            float mn = wr[0] * xr[0] * xr[0];
+#pragma unroll
+            for (int j = 1; j < 8; ++j) { const float a = wr[j] * xr[j] * xr[j]; if (a < mn) { mn = a; im = j; } }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) if (j == im) xv[j] = -xv[j];
+            sg ^= 1u << im;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) st.xv[eidx(P::SB, S::PAD, lane * 8 + j)] = xv[j];
+        const int e0 = lane * 8;
+        st.signs[e0 / P::SB][(e0 % P::SB) / 8] = (uint8_t) (P::PARITY ? (sg & 127u) : sg);
+    }
+    __syncwarp();
+    // ---- P4: sub-block guard and the trial range
+    if (lane < S::NSUB) {
+        const float * xv = st.xv + lane * S::PAD;
+        float mx = xv[0];
+        for (int i = 1; i < P::SB; ++i) mx = fmaxr(mx, xv[i]);
+        int skip = P::EPS_ZERO ? !mx : mx < P::EPS;
+        float scale = 0.f, denom = mx;
+        if (!skip) {
+            if (P::QP_FIRST) {
+                scale = qp_levels<P::SB>(P::KMAXQ + 1, xv, st.w + lane * S::PAD);
+                denom = scale * P::KMAXQ;
+                if (denom <= 0) skip = 1;
+            } else {
+                scale = mx / (2 * P::KMAXQ - 1);
+            }
+        }
+        st.skip[lane] = (uint8_t) skip;
+        st.scale[lane] = scale;
+        st.denom[lane] = denom;
+    }
+    __syncwarp();
+    // ---- P5: the trials, one (sub-block, trial) a lane
+    for (int task = lane; task < S::NTASK; task += 32) {
+        const int s = task / S::NT, t = task - s * S::NT;
+        float sqx = 0, sq2 = 0;
+        unsigned onb = 0;
+        if (!st.skip[s]) {
+            const float id = ((float) (2 * P::KMAXQ - 1) + (float) (t - P::NTR) * P::STEP) / st.denom[s];
+            const float ts = 1 / id;
+            const float * xv = st.xv + s * S::PAD;
+            const float * wa = st.wa + s * S::PAD;
+            const float * w = st.w + s * S::PAD;
+#pragma unroll 1
+            for (int g = 0; g < S::NG; ++g) {
+                int on;
+                uint32_t lev = group_to_grid<P::GD, P::KMAXQ>(xv + g * P::GD, wa + g * P::GD, id, ts, tab, &on);
+                if (lev == 0xFFFFFFFFu) { atomicOr(status, ST_NO_NEIGHBOUR); lev = 0; }
+                st.t_lev[task][g] = (uint16_t) lev;
+                onb |= (unsigned) on << g;
+#pragma unroll
+                for (int i = 0; i < P::GD; ++i) {
+                    const float q = (float) (2 * level_of<P::GD>(lev, i) + 1);
+                    const int e = g * P::GD + i;
+                    sqx += w[e] * xv[e] * q;
+                    sq2 += w[e] * q * q;
+                }
+            }
+        }
+        st.t_sqx[task] = sqx;
+        st.t_sq2[task] = sq2;
+        st.t_on[task] = (uint8_t) onb;
+    }
+    __syncwarp();
+    // ---- P6: ggml's trial choice replayed in trial order; which groups to snap again
+    constexpr unsigned ALL = (1u << S::NG) - 1;
+    if (lane < S::NSUB) {
+        const int s = lane;
+        uint8_t rg = 0;
+        if (!st.skip[s]) {
+            float scale = st.scale[s], best = 0;
+            int win = -1;
+            for (int t = 0; t < S::NT; ++t) {
+                const float sqx = st.t_sqx[s * S::NT + t], sq2 = st.t_sq2[s * S::NT + t];
+                if (sq2 > 0 && sqx * sqx > best * sq2) { scale = sqx / sq2; best = scale * sqx; win = t; }
+            }
+            unsigned on = P::INIT_ON ? ALL : 0u;
+            for (int g = 0; g < S::NG; ++g) st.lev[s][g] = win >= 0 ? st.t_lev[s * S::NT + win][g] : 0;
+            if (win >= 0) on = st.t_on[s * S::NT + win];
+            const int n_off = __popc(~on & ALL);
+            if ((P::REGRID_ANY ? n_off > 0 : true) && scale > 0) rg = (uint8_t) (P::REGRID_ALL ? ALL : (~on & ALL));
+            st.scale[s] = scale;
+        }
+        st.regrid[s] = rg;
+    }
+    __syncwarp();
+    // ---- P7: snap the chosen groups again with the final scale, one (sub-block, group) a lane
+    for (int task = lane; task < S::NSUB * S::NG; task += 32) {
+        const int s = task / S::NG, g = task - s * S::NG;
+        if (st.regrid[s] & (1u << g)) {
+            const float scale = st.scale[s];
+            const float id = 1 / scale;
+            int on;
+            uint32_t lev = group_to_grid<P::GD, P::KMAXQ>(st.xv + s * S::PAD + g * P::GD, st.wa + s * S::PAD + g * P::GD,
+                                                          id, scale, tab, &on);
+            if (lev == 0xFFFFFFFFu) { atomicOr(status, ST_NO_NEIGHBOUR); lev = 0; }
+            st.lev[s][g] = (uint16_t) lev;
+        }
+    }
+    __syncwarp();
+    // ---- P8: refit, signs, grid indices (one sub-block a lane)
+    if (lane < S::NSUB) {
+        const int s = lane;
+        if (!st.skip[s]) {
+            float scale = st.scale[s];
+            if (st.regrid[s]) {
+                const float * xv = st.xv + s * S::PAD;
+                const float * w = st.w + s * S::PAD;
+                float sqx = 0, sq2 = 0;
+                for (int e = 0; e < P::SB; ++e) {
+                    const float q = (float) (2 * level_of<P::GD>(st.lev[s][e / P::GD], e % P::GD) + 1);
+                    sqx += w[e] * xv[e] * q;
+                    sq2 += w[e] * q * q;
+                }
+                if (sq2 > 0) scale = sqx / sq2;
+            }
+            if (scale < 0) {
+                scale = -scale;
+                for (int k = 0; k < S::NSG; ++k)
+                    st.signs[s][k] = (uint8_t) (P::PARITY ? (~st.signs[s][k]) & 127 : (uint8_t) ~st.signs[s][k]);
+            }
+            for (int g = 0; g < S::NG; ++g) {
+                const int gi = __ldg(tab.code3 + code3_of<P::GD>(st.lev[s][g]));
+                if (gi < 0) atomicOr(status, ST_OFF_GRID);
+                st.gidx[s][g] = gi < 0 ? 0 : gi;
+            }
+            st.scale[s] = scale;
+        } else {
+            st.scale[s] = 0.f;
+        }
+    }
+    __syncwarp();
+    // ---- P9: super-block scale and the block bytes (lane 0), then a coalesced store
+    if (lane == 0) {
+        uint8_t * y = st.out;
+        for (int i = 0; i < block_bytes(T); ++i) y[i] = 0;
+        float max_scale = 0;
+        for (int s = 0; s < S::NSUB; ++s) if (!st.skip[s]) max_scale = fmaxr(max_scale, st.scale[s]);
+        const float d = max_scale / 31;
+        const float idd = 1 / d;
+        auto scale4 = [&](int s) { return imax(0, imin(15, nearest_int(0.5f * (idd * st.scale[s] - 1)))); };
+        if constexpr (T == IQ2_XXS) {
+            if (max_scale) {
+                const uint16_t h = half_bits(d);
+                y[0] = h & 255; y[1] = h >> 8;
+                for (int s = 0; s < 8; ++s) {
+                    uint32_t q0 = 0, q1 = 0;
+                    if (!st.skip[s]) {
+                        for (int k = 0; k < 4; ++k) { q0 |= (uint32_t) st.gidx[s][k] << (8 * k); q1 |= (uint32_t) st.signs[s][k] << (7 * k); }
+                    }
+                    q1 |= (uint32_t) scale4(s) << 28;
+                    for (int j = 0; j < 4; ++j) { y[2 + 8 * s + j] = (q0 >> (8 * j)) & 255; y[6 + 8 * s + j] = (q1 >> (8 * j)) & 255; }
+                }
+            }
+        } else if constexpr (T == IQ2_XS) {
+            if (max_scale) {
+                const uint16_t h = half_bits(d);
+                y[0] = h & 255; y[1] = h >> 8;
+                for (int s = 0; s < 16; ++s) {
+                    if (!st.skip[s])
+                        for (int k = 0; k < 2; ++k) {
+                            const uint16_t v = (uint16_t) (st.gidx[s][k] | (st.signs[s][k] << 9));
+                            y[2 + 2 * (2 * s + k)] = v & 255; y[3 + 2 * (2 * s + k)] = v >> 8;
+                        }
+                    y[66 + s / 2] |= (uint8_t) (scale4(s) << (4 * (s % 2)));
+                }
+            }
+        } else if constexpr (T == IQ2_S) {
+            for (int s = 0; s < 16; ++s) {
+                if (st.skip[s]) continue;
+                for (int k = 0; k < 2; ++k) {
+                    const int i8 = 2 * s + k;
+                    y[2 + i8] = (uint8_t) (st.gidx[s][k] & 255);
+                    y[66 + i8 / 4] |= (uint8_t) ((st.gidx[s][k] >> 8) << (2 * (i8 % 4)));
+                    y[34 + i8] = st.signs[s][k];
+                }
+            }
+            if (max_scale) {
+                const uint16_t h = half_bits(d * 0.9875f);
+                y[0] = h & 255; y[1] = h >> 8;
+                for (int s = 0; s < 16; ++s) y[74 + s / 2] |= (uint8_t) (scale4(s) << (4 * (s % 2)));
+            }
+        } else if constexpr (T == IQ3_XXS) {
+            if (max_scale) {
+                const uint16_t h = half_bits(d * 1.0125f);
+                y[0] = h & 255; y[1] = h >> 8;
+                for (int s = 0; s < 8; ++s) {
+                    uint32_t ss = 0;
+                    if (!st.skip[s]) {
+                        for (int k = 0; k < 8; ++k) y[2 + 8 * s + k] = (uint8_t) st.gidx[s][k];
+                        ss = st.signs[s][0] | (st.signs[s][1] << 7) | (st.signs[s][2] << 14) | ((uint32_t) st.signs[s][3] << 21);
+                    }
+                    ss |= (uint32_t) scale4(s) << 28;
+                    for (int j = 0; j < 4; ++j) y[66 + 4 * s + j] = (ss >> (8 * j)) & 255;
+                }
+            }
+        } else {   // IQ3_S: qs / signs advance only past sub-blocks that were not skipped (gpuq.hip:1188-1190, :1266-1268)
+            int qo = 0, so = 0;
+            for (int s = 0; s < 8; ++s) {
+                if (st.skip[s]) continue;
+                for (int k = 0; k < 8; ++k) {
+                    y[2 + qo + k] = (uint8_t) (st.gidx[s][k] & 255);
+                    y[66 + s] |= (uint8_t) ((st.gidx[s][k] >> 8) << k);
+                }
+                qo += 8;
+                for (int k = 0; k < 4; ++k) y[74 + so + k] = st.signs[s][k];
+                so += 4;
+            }
+            if (max_scale) {
+                const uint16_t h = half_bits(d * 1.033f);
+                y[0] = h & 255; y[1] = h >> 8;
+                for (int s = 0; s < 8; s += 2) y[106 + s / 2] = (uint8_t) (scale4(s) | (scale4(s + 1) << 4));
+            }
+        }
+    }
+    __syncwarp();
+    uint8_t * yo = out + b * block_bytes(T);
+    for (int i = lane; i < block_bytes(T); i += 32) yo[i] = st.out[i];
+}
+
+template <int T, int SRC>
+cudaError_t launch_t(const LaunchArgs & a) {
+    constexpr int WARPS = 4;
+    const size_t smem = sizeof(WarpState<T>) * WARPS;
+    static_assert(sizeof(WarpState<T>) * WARPS <= 48 * 1024, "static smem budget");
+    const int64_t grid = (a.nblocks + WARPS - 1) / WARPS;
+    k_iq_grid<T, SRC><<<(unsigned) grid, WARPS * 32, smem, a.stream>>>(
+        (const uint8_t *) a.src, a.qw, a.qw_mod, a.qw_div, a.qw_mat, (uint8_t *) a.out, a.nblocks, a.tab, a.status);
+    return cudaGetLastError();
+}
+
+template <int T>
+cudaError_t launch_src(const LaunchArgs & a) {
+    switch (a.src_type) {
+        case SRC_F32:   return launch_t<T, SRC_F32>(a);
+        case SRC_F16:   return launch_t<T, SRC_F16>(a);
+        case SRC_BF16:  return launch_t<T, SRC_BF16>(a);
+        case SRC_Q8_0:  return launch_t<T, SRC_Q8_0>(a);
+        case SRC_MXFP4: return launch_t<T, SRC_MXFP4>(a);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_iq_grid(int type, const LaunchArgs & a) {
+    switch (type) {
+        case IQ2_XXS: return launch_src<IQ2_XXS>(a);
+        case IQ2_XS:  return launch_src<IQ2_XS>(a);
+        case IQ2_S:   return launch_src<IQ2_S>(a);
+        case IQ3_XXS: return launch_src<IQ3_XXS>(a);
+        case IQ3_S:   return launch_src<IQ3_S>(a);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace gq

@@ -1,0 +1,51 @@
+// kernels.h - the library's internal launch interface (host side; no torch types anywhere).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+#include "common.cuh"
+
+namespace gq {
+
+// One quantize launch: nblocks blocks of the target type from the source bytes `src` (ggml source type
+// src_type: F32 / F16 / BF16 / Q8_0 / MXFP4, decoded in the kernel's loads). Block b takes the importance weights
+// qw + ((b / qw_mat) * qw_mod + (b % qw_mod) / qw_div) * block_len (trench-gguf's kq addressing, gpuq.hip:1841-1847),
+// or none when qw is null (k-quants, Q8_0 and IQ4_*: ggml's no-imatrix paths).
+struct LaunchArgs {
+    int src_type;
+    const void * src;
+    const float * qw;
+    int64_t qw_mod, qw_div, qw_mat;
+    void * out;
+    int64_t nblocks;
+    SearchTab tab;
+    unsigned * status;
+    cudaStream_t stream;
+};
+
+cudaError_t launch_iq_grid(int type, const LaunchArgs & a);   // IQ2_XXS IQ2_XS IQ2_S IQ3_XXS IQ3_S
+cudaError_t launch_iq1(int type, const LaunchArgs & a);       // IQ1_S IQ1_M
+cudaError_t launch_iq4(int type, const LaunchArgs & a);       // IQ4_NL IQ4_XS
+cudaError_t launch_kquant(int type, const LaunchArgs & a);    // Q2_K .. Q6_K, Q8_0
+
+// ggml's to_float of the i-quant types with grids and IQ4_XS: nblocks super-blocks -> nblocks*256 floats
+cudaError_t launch_dequant(int type, const void * q, float * out, int64_t nblocks, DequantTab tab, cudaStream_t st);
+// source bytes (F32 / F16 / BF16 / Q8_0 / MXFP4) -> n floats
+cudaError_t launch_decode(int src, const void * raw, float * out, int64_t n, cudaStream_t st);
+
+inline bool is_iq_grid(int t) { return t == IQ2_XXS || t == IQ2_XS || t == IQ2_S || t == IQ3_XXS || t == IQ3_S; }
+inline bool is_iq1(int t) { return t == IQ1_S || t == IQ1_M; }
+inline bool is_iq4(int t) { return t == IQ4_NL || t == IQ4_XS; }
+inline bool is_kquant(int t) { return t == Q2_K || t == Q3_K || t == Q4_K || t == Q5_K || t == Q6_K || t == Q8_0; }
+// the types ggml also quantizes without an imatrix (k-quants' *_ref path, IQ4 with x^2 weights)
+inline bool takes_no_imatrix(int t) { return is_kquant(t) || is_iq4(t); }
+inline bool needs_search_tab(int t) { return is_iq_grid(t) || is_iq1(t); }
+
+inline cudaError_t launch_quantize(int type, const LaunchArgs & a) {
+    if (is_iq_grid(type)) return launch_iq_grid(type, a);
+    if (is_iq1(type)) return launch_iq1(type, a);
+    if (is_iq4(type)) return launch_iq4(type, a);
+    if (is_kquant(type)) return launch_kquant(type, a);
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace gq
