@@ -9,9 +9,12 @@
 //
 // How it runs on sm_100a: one warp a super-block, FP32-ALU bound. Lanes own independent work only:
 //   * elementwise weights and sign groups (8 weights a lane),
-//   * the (sub-block, trial) pairs of the trial search (104..304 a super-block, 32 at a time), each lane running
-//     its trial's groups, neighbour searches and index-ordered sums exactly as ggml does,
+//   * the (sub-block, trial) pairs of make_qp_quants' trial scales (IQ2_XXS) and of the trial search (104..304 a
+//     super-block), each lane running its trial's groups and index-ordered sums exactly as ggml does,
 //   * the (sub-block, group) pairs of the re-gridding.
+// The neighbour searches dominate (8k..22k candidate points a super-block). Each lane searches its own group's
+// list: the 24 possible per-dimension terms w_i (s q - x_i)^2 (q in {1, 3, 5}) are formed once, so a candidate's
+// distance is 8 selects and ggml's 8 additions in ggml's order, with the next list entry loaded one step ahead.
 // ggml's sequential decisions (which trial wins: a strict `>` scan in trial order) are replayed in trial order by
 // one lane per sub-block from the stored per-trial sums, so the choice is bit-identical. Sums that ggml runs in
 // index order (sumx2 over 256, the 16/32-weight sums) run in index order inside one lane.
@@ -58,12 +61,17 @@ template <int T> struct Shape {
     static constexpr int PAD = P::SB + 1;             // padded sub-block stride (conflict-free across sub-blocks)
     static constexpr int BITS = P::GD == 8 ? 2 : 3;   // packed level bits a dimension
     static constexpr int NSG = P::SB / 8;             // 8-weight sign bytes a sub-block
+    static constexpr int NROUND = (NTASK + 31) / 32;  // rounds of 32 trials
+    static constexpr int NRG = NSUB * NG;             // re-grid searches a super-block
 };
 
 // per-warp shared state of one super-block
 template <int T> struct alignas(16) WarpState {
     using S = Shape<T>;
-    float x[S::NSUB * S::PAD], w[S::NSUB * S::PAD], wa[S::NSUB * S::PAD], xv[S::NSUB * S::PAD];
+    float x2[QK];                                     // x*x, for sumx2
+    float w[S::NSUB * S::PAD], wa[S::NSUB * S::PAD], xv[S::NSUB * S::PAD], wx[S::NSUB * S::PAD];
+    float qmse[S::NSUB][9];                           // make_qp_quants' trial errors (IQ2_XXS)
+    uint8_t qL[S::NSUB][32];                          // make_qp_quants' levels (IQ2_XXS)
     float t_sqx[S::NTASK], t_sq2[S::NTASK];
     uint16_t t_lev[S::NTASK][S::NG];
     uint8_t t_on[S::NTASK];
@@ -78,38 +86,42 @@ template <int T> struct alignas(16) WarpState {
 
 __device__ __forceinline__ int eidx(int sb, int pad, int e) { return (e / sb) * pad + (e % sb); }
 
-// make_qp_quants (gpuq.hip:114-176) on n weights of one sub-block, one lane; returns the scale
+// make_qp_quants (gpuq.hip:114-176), split in two. Trial k's weighted error over one sub-block: k = 0 the
+// initial inverse scale nmax/max (levels stored unclamped, as ggml), k = 1..8 the trial scales is = -4..-1, 1..4.
 template <int N>
-__device__ float qp_levels(int nmax, const float * x, const float * w) {
-    uint8_t L[N];
-    float mx = 0;
-#pragma unroll
-    for (int i = 0; i < N; ++i) mx = fmaxr(mx, x[i]);
-    if (mx < 1e-15f) return 0.f;
-    float iscale = nmax / mx;
-    const float scale0 = 1 / iscale;
-    float best_mse = 0;
-#pragma unroll
-    for (int i = 0; i < N; ++i) {
-        const int l = nearest_int(iscale * x[i]);
-        const float d = x[i] - scale0 * (float) (uint8_t) l;
-        best_mse += w[i] * d * d;
-    }
-    for (int is = -4; is <= 4; ++is) {
-        if (!is) continue;
-        const float iscale_is = (0.1f * is + nmax) / mx;
-        const float scale_is = 1 / iscale_is;
-        float mse = 0;
-#pragma unroll
+__device__ float qp_trial_mse(int k, int nmax, float mx, const float * x, const float * w) {
+    float mse = 0;
+    if (k == 0) {
+        const float iscale = nmax / mx;
+        const float scale = 1 / iscale;
         for (int i = 0; i < N; ++i) {
-            const int l = imin(nmax, nearest_int(iscale_is * x[i]));
-            const float d = x[i] - scale_is * l;
+            const uint8_t L = (uint8_t) nearest_int(iscale * x[i]);
+            const float d = x[i] - scale * L;
             mse += w[i] * d * d;
         }
-        if (mse < best_mse) { best_mse = mse; iscale = iscale_is; }
+        return mse;
+    }
+    const int is = k <= 4 ? k - 5 : k - 4;
+    const float iscale_is = (0.1f * is + nmax) / mx;
+    const float scale_is = 1 / iscale_is;
+    for (int i = 0; i < N; ++i) {
+        const int l = imin(nmax, nearest_int(iscale_is * x[i]));
+        const float d = x[i] - scale_is * l;
+        mse += w[i] * d * d;
+    }
+    return mse;
+}
+
+// ... then, one lane a sub-block: ggml's choice among the trials (first strict minimum in trial order), the levels,
+// and the coordinate descent; L in shared memory. Returns the scale.
+template <int N>
+__device__ float qp_finish(int nmax, float mx, const float * x, const float * w, const float * mse, uint8_t * L) {
+    float iscale = nmax / mx, best_mse = mse[0];
+    for (int k = 1; k <= 8; ++k) {
+        const int is = k <= 4 ? k - 5 : k - 4;
+        if (mse[k] < best_mse) { best_mse = mse[k]; iscale = (0.1f * is + nmax) / mx; }
     }
     float sumlx = 0, suml2 = 0;
-#pragma unroll
     for (int i = 0; i < N; ++i) {
         const int l = imin(nmax, nearest_int(iscale * x[i]));
         L[i] = (uint8_t) l;
@@ -118,13 +130,13 @@ __device__ float qp_levels(int nmax, const float * x, const float * w) {
     }
     for (int pass = 0; pass < 5; ++pass) {
         int changed = 0;
-#pragma unroll
         for (int i = 0; i < N; ++i) {
-            float slx = sumlx - w[i] * x[i] * L[i];
-            float sl2 = suml2 - w[i] * L[i] * L[i];
+            const int Li = L[i];
+            float slx = sumlx - w[i] * x[i] * Li;
+            float sl2 = suml2 - w[i] * Li * Li;
             if (slx > 0 && sl2 > 0) {
                 const int nl = imin(nmax, nearest_int(x[i] * sl2 / slx));
-                if (nl != L[i]) {
+                if (nl != Li) {
                     slx += w[i] * x[i] * nl;
                     sl2 += w[i] * nl * nl;
                     if (slx * slx * suml2 > sumlx * sumlx * sl2) { L[i] = (uint8_t) nl; sumlx = slx; suml2 = sl2; ++changed; }
@@ -139,64 +151,6 @@ __device__ float qp_levels(int nmax, const float * x, const float * w) {
 // the lattice value 2l+1 of a 3-bit level, as a float, by the 2^23 bias (exact, full-rate FADD)
 __device__ __forceinline__ float odd_level(uint32_t l) { return u2f(0x4B000000u + 2 * l + 1) - 8388608.f; }
 
-// Rounds one group to levels with inverse scale id; if the code is off the grid, searches its neighbour list with
-// scale s (iq2_find_best_neighbour gpuq.hip:178-197 / iq3_find_best_neighbour :972-992: weighted squared distance,
-// the first minimum in list order wins). Returns the packed levels, sets *on if the rounded code was on the grid;
-// returns 0xFFFFFFFF when no listed point has a finite distance.
-template <int GD, int KMAXQ>
-__device__ uint32_t group_to_grid(const float * xv, const float * wa, float id, float s, const SearchTab & tab, int * on) {
-    constexpr int BITS = GD == 8 ? 2 : 3;
-    uint32_t lev = 0;
-    int c3 = 0, p3 = 1;
-#pragma unroll
-    for (int i = 0; i < GD; ++i) {
-        const int l = imax(0, imin(KMAXQ - 1, nearest_int(0.5f * (id * xv[i] - 1))));
-        lev |= (uint32_t) l << (BITS * i);
-        c3 += l * p3;
-        p3 *= (GD == 8 ? 3 : 8);
-    }
-    const int m = __ldg(tab.code3 + c3);
-    *on = m >= 0;
-    if (m >= 0) return lev;
-    const uint32_t * lst = tab.neigh + (-m - 1);
-    const int n = (int) __ldg(lst);
-    float best = FLT_MAX;
-    uint32_t bl = 0xFFFFFFFFu;
-    if constexpr (GD == 8) {
-        // the 24 possible per-dimension terms w_i (s q - x_i)^2, q in {1, 3, 5}: each neighbour's distance is then
-        // 8 selects and the same 8 additions in the same order as ggml's loop
-        float t0[8], t1[8], t2[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float d0 = s * 1.f - xv[i], d1 = s * 3.f - xv[i], d2 = s * 5.f - xv[i];
-            t0[i] = wa[i] * d0 * d0; t1[i] = wa[i] * d1 * d1; t2[i] = wa[i] * d2 * d2;
-        }
-        for (int j = 1; j <= n; ++j) {
-            const uint32_t e = __ldg(lst + j);
-            float d2 = 0.f;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const uint32_t l = (e >> (2 * i)) & 3u;
-                d2 += l == 0 ? t0[i] : (l == 1 ? t1[i] : t2[i]);
-            }
-            if (d2 < best) { best = d2; bl = e; }
-        }
-    } else {
-        for (int j = 1; j <= n; ++j) {
-            const uint32_t e = __ldg(lst + j);
-            float d2 = 0.f;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float q = odd_level((e >> (3 * i)) & 7u);
-                const float d = s * q - xv[i];
-                d2 += wa[i] * d * d;
-            }
-            if (d2 < best) { best = d2; bl = e; }
-        }
-    }
-    return bl == 0xFFFFFFFFu ? bl : (bl & 0xFFFFu);
-}
-
 template <int GD>
 __device__ __forceinline__ int level_of(uint32_t lev, int i) { return GD == 8 ? (lev >> (2 * i)) & 3 : (lev >> (3 * i)) & 7; }
 
@@ -207,6 +161,87 @@ __device__ __forceinline__ int code3_of(uint32_t lev) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) { c += (int) ((lev >> (2 * i)) & 3u) * p; p *= 3; }
     return c;
+}
+
+constexpr uint32_t NONE = 0xFFFFFFFFu;
+
+// ggml's rounding of one group at inverse scale id: l = clamp(nearest_int(0.5*(id*x - 1)), 0, kmaxq-1); returns
+// the packed levels and the grid-table entry of the code (>= 0 grid index, < 0 the neighbour list)
+template <int GD, int KMAXQ>
+__device__ __forceinline__ uint32_t round_group(const float * xv, float id, const SearchTab & tab, int * m) {
+    constexpr int BITS = GD == 8 ? 2 : 3;
+    uint32_t lev = 0;
+    int c3 = 0, p3 = 1;
+#pragma unroll
+    for (int i = 0; i < GD; ++i) {
+        const int l = imax(0, imin(KMAXQ - 1, nearest_int(0.5f * (id * xv[i] - 1))));
+        lev |= (uint32_t) l << (BITS * i);
+        c3 += l * p3;
+        p3 *= (GD == 8 ? 3 : 8);
+    }
+    *m = __ldg(tab.code3 + c3);
+    return lev;
+}
+
+// the 8-d grids: one lane's own search (iq2_find_best_neighbour, gpuq.hip:178-197): d2 = 0; d2 += w_i (s q_i -
+// x_i)^2 for i in order, the first strict minimum in list order wins; NaN and values >= FLT_MAX never win
+__device__ uint32_t search_lane8(int m, const float * xv, const float * wa, float s, const SearchTab & tab) {
+    float t0[8], t1[8], t2[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float d0 = s * 1.f - xv[i], d1 = s * 3.f - xv[i], d2 = s * 5.f - xv[i];
+        t0[i] = wa[i] * d0 * d0; t1[i] = wa[i] * d1 * d1; t2[i] = wa[i] * d2 * d2;
+    }
+    const uint32_t * lst = tab.neigh + (-m - 1);
+    const int n = (int) __ldg(lst);
+    float best = FLT_MAX;
+    uint32_t bl = NONE;
+    uint32_t e = __ldg(lst + 1);
+    for (int j = 1; j <= n; ++j) {
+        const uint32_t en = j < n ? __ldg(lst + j + 1) : 0u;   // the next entry, one step ahead
+        float d2 = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t l = (e >> (2 * i)) & 3u;
+            d2 += l == 0 ? t0[i] : (l == 1 ? t1[i] : t2[i]);
+        }
+        if (d2 < best) { best = d2; bl = e; }
+        e = en;
+    }
+    return bl == NONE ? NONE : (bl & 0xFFFFu);
+}
+
+// the 4-d grids: one lane's own search (lists of 2..38 points), ggml's distance and first-minimum rule
+// (iq3_find_best_neighbour, gpuq.hip:972-992)
+__device__ uint32_t search_lane4(int m, const float * xv, const float * wa, float s, const SearchTab & tab) {
+    const uint32_t * lst = tab.neigh + (-m - 1);
+    const int n = (int) __ldg(lst);
+    float best = FLT_MAX;
+    uint32_t bl = NONE;
+    for (int j = 1; j <= n; ++j) {
+        const uint32_t e = __ldg(lst + j);
+        float d2 = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float d = s * odd_level((e >> (3 * i)) & 7u) - xv[i];
+            d2 += wa[i] * d * d;
+        }
+        if (d2 < best) { best = d2; bl = e; }
+    }
+    return bl == NONE ? NONE : (bl & 0xFFFFu);
+}
+
+// A group's levels at inverse scale id / scale s: the rounding when on the grid, else the neighbour search.
+template <int T>
+__device__ __forceinline__ uint32_t group_levels(WarpState<T> & st, int lane, bool active, const float * xv,
+                                                 const float * wa, float id, float s, const SearchTab & tab, unsigned * on) {
+    using P = GT<T>;
+    int m = 0;
+    uint32_t lev = 0;
+    if (active) lev = round_group<P::GD, P::KMAXQ>(xv, id, tab, &m);
+    *on = active && m >= 0;
+    if (active && m < 0) lev = P::GD == 8 ? search_lane8(m, xv, wa, s, tab) : search_lane4(m, xv, wa, s, tab);
+    return lev;
 }
 
 // ------------------------------------------------------------------------------------------------ the kernel
@@ -227,13 +262,17 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
     float xr[8], qr[8];
     decode8<SRC>(src, b * QK + lane * 8, xr);
     load8_f32(qw + ((b / qw_mat) * qw_mod + (b % qw_mod) / qw_div) * QK + lane * 8, qr);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) st.x[eidx(P::SB, S::PAD, lane * 8 + j)] = xr[j];
+    {
+        float4 * x2 = reinterpret_cast<float4 *>(st.x2 + lane * 8);
+        x2[0] = make_float4(xr[0] * xr[0], xr[1] * xr[1], xr[2] * xr[2], xr[3] * xr[3]);
+        x2[1] = make_float4(xr[4] * xr[4], xr[5] * xr[5], xr[6] * xr[6], xr[7] * xr[7]);
+    }
     __syncwarp();
-    // ---- P1: sumx2 in index order (one lane)
+    // ---- P1: sumx2 in index order (one lane; the products were formed by their lanes)
     if (lane == 0) {
         float s2 = 0;
-        for (int e = 0; e < QK; ++e) { const float v = st.x[eidx(P::SB, S::PAD, e)]; s2 += v * v; }
+        const float4 * x2 = reinterpret_cast<const float4 *>(st.x2);
+        for (int e = 0; e < QK / 4; ++e) { const float4 v = x2[e]; s2 += v.x; s2 += v.y; s2 += v.z; s2 += v.w; }
         st.sigma2 = P::SIGMA_X2 ? 2 * s2 / QK : s2 / QK;
     }
     __syncwarp();
@@ -265,62 +304,82 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
             sg ^= 1u << im;
         }
 #pragma unroll
-        for (int j = 0; j < 8; ++j) st.xv[eidx(P::SB, S::PAD, lane * 8 + j)] = xv[j];
+        for (int j = 0; j < 8; ++j) {
+            const int ei = eidx(P::SB, S::PAD, lane * 8 + j);
+            st.xv[ei] = xv[j];
+            st.wx[ei] = wr[j] * xv[j];   // (w*x, the first product of ggml's w*x*q)
+        }
         const int e0 = lane * 8;
         st.signs[e0 / P::SB][(e0 % P::SB) / 8] = (uint8_t) (P::PARITY ? (sg & 127u) : sg);
     }
     __syncwarp();
-    // ---- P4: sub-block guard and the trial range
+    // ---- P4: sub-block guard and the trial range (IQ2_XXS: make_qp_quants, its 9 trials one a lane)
     if (lane < S::NSUB) {
         const float * xv = st.xv + lane * S::PAD;
         float mx = xv[0];
         for (int i = 1; i < P::SB; ++i) mx = fmaxr(mx, xv[i]);
-        int skip = P::EPS_ZERO ? !mx : mx < P::EPS;
-        float scale = 0.f, denom = mx;
-        if (!skip) {
-            if (P::QP_FIRST) {
-                scale = qp_levels<P::SB>(P::KMAXQ + 1, xv, st.w + lane * S::PAD);
-                denom = scale * P::KMAXQ;
-                if (denom <= 0) skip = 1;
-            } else {
-                scale = mx / (2 * P::KMAXQ - 1);
-            }
-        }
+        const int skip = P::EPS_ZERO ? !mx : mx < P::EPS;
         st.skip[lane] = (uint8_t) skip;
-        st.scale[lane] = scale;
-        st.denom[lane] = denom;
+        st.denom[lane] = mx;
+        st.scale[lane] = skip ? 0.f : mx / (2 * P::KMAXQ - 1);
     }
     __syncwarp();
-    // ---- P5: the trials, one (sub-block, trial) a lane
-    for (int task = lane; task < S::NTASK; task += 32) {
-        const int s = task / S::NT, t = task - s * S::NT;
+    if constexpr (P::QP_FIRST) {
+        constexpr int NMAX = P::KMAXQ + 1;
+        for (int task = lane; task < S::NSUB * 9; task += 32) {
+            const int s = task / 9, k = task - s * 9;
+            if (st.skip[s]) continue;
+            const float * xv = st.xv + s * S::PAD;
+            float qm = 0;   // (make_qp_quants' own max starts at 0)
+            for (int i = 0; i < P::SB; ++i) qm = fmaxr(qm, xv[i]);
+            st.qmse[s][k] = qp_trial_mse<P::SB>(k, NMAX, qm, xv, st.w + s * S::PAD);
+        }
+        __syncwarp();
+        if (lane < S::NSUB && !st.skip[lane]) {
+            const float * xv = st.xv + lane * S::PAD;
+            float qm = 0;
+            for (int i = 0; i < P::SB; ++i) qm = fmaxr(qm, xv[i]);
+            const float scale = qm < 1e-15f ? 0.f : qp_finish<P::SB>(NMAX, qm, xv, st.w + lane * S::PAD, st.qmse[lane], st.qL[lane]);
+            st.scale[lane] = scale;
+            st.denom[lane] = scale * P::KMAXQ;
+            if (!(scale * P::KMAXQ > 0)) st.skip[lane] = 1;
+        }
+        __syncwarp();
+    }
+    // ---- P5: the trials, one (sub-block, trial) a lane, 32 at a time; groups in order (their sums in index order)
+    for (int r = 0; r < S::NROUND; ++r) {
+        const int task = r * 32 + lane;
+        const int s = task < S::NTASK ? task / S::NT : 0, t = task - s * S::NT;
+        const bool live = task < S::NTASK && !st.skip[s];
+        const float id = live ? ((float) (2 * P::KMAXQ - 1) + (float) (t - P::NTR) * P::STEP) / st.denom[s] : 1.f;
+        const float ts = 1 / id;
+        const float * xv = st.xv + s * S::PAD;
+        const float * wa = st.wa + s * S::PAD;
+        const float * wx = st.wx + s * S::PAD;
+        const float * w = st.w + s * S::PAD;
         float sqx = 0, sq2 = 0;
         unsigned onb = 0;
-        if (!st.skip[s]) {
-            const float id = ((float) (2 * P::KMAXQ - 1) + (float) (t - P::NTR) * P::STEP) / st.denom[s];
-            const float ts = 1 / id;
-            const float * xv = st.xv + s * S::PAD;
-            const float * wa = st.wa + s * S::PAD;
-            const float * w = st.w + s * S::PAD;
 #pragma unroll 1
-            for (int g = 0; g < S::NG; ++g) {
-                int on;
-                uint32_t lev = group_to_grid<P::GD, P::KMAXQ>(xv + g * P::GD, wa + g * P::GD, id, ts, tab, &on);
-                if (lev == 0xFFFFFFFFu) { atomicOr(status, ST_NO_NEIGHBOUR); lev = 0; }
-                st.t_lev[task][g] = (uint16_t) lev;
-                onb |= (unsigned) on << g;
+        for (int g = 0; g < S::NG; ++g) {
+            unsigned on;
+            uint32_t lev = group_levels<T>(st, lane, live, xv + g * P::GD, wa + g * P::GD, id, ts, tab, &on);
+            if (!live) continue;
+            if (lev == NONE) { atomicOr(status, ST_NO_NEIGHBOUR); lev = 0; }
+            st.t_lev[task][g] = (uint16_t) lev;
+            onb |= on << g;
 #pragma unroll
-                for (int i = 0; i < P::GD; ++i) {
-                    const float q = (float) (2 * level_of<P::GD>(lev, i) + 1);
-                    const int e = g * P::GD + i;
-                    sqx += w[e] * xv[e] * q;
-                    sq2 += w[e] * q * q;
-                }
+            for (int i = 0; i < P::GD; ++i) {
+                const float q = odd_level(level_of<P::GD>(lev, i));
+                const int e = g * P::GD + i;
+                sqx += wx[e] * q;
+                sq2 += w[e] * q * q;
             }
         }
-        st.t_sqx[task] = sqx;
-        st.t_sq2[task] = sq2;
-        st.t_on[task] = (uint8_t) onb;
+        if (task < S::NTASK) {
+            st.t_sqx[task] = live ? sqx : 0.f;
+            st.t_sq2[task] = live ? sq2 : 0.f;
+            st.t_on[task] = (uint8_t) onb;
+        }
     }
     __syncwarp();
     // ---- P6: ggml's trial choice replayed in trial order; which groups to snap again
@@ -346,15 +405,16 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
     }
     __syncwarp();
     // ---- P7: snap the chosen groups again with the final scale, one (sub-block, group) a lane
-    for (int task = lane; task < S::NSUB * S::NG; task += 32) {
-        const int s = task / S::NG, g = task - s * S::NG;
-        if (st.regrid[s] & (1u << g)) {
-            const float scale = st.scale[s];
-            const float id = 1 / scale;
-            int on;
-            uint32_t lev = group_to_grid<P::GD, P::KMAXQ>(st.xv + s * S::PAD + g * P::GD, st.wa + s * S::PAD + g * P::GD,
-                                                          id, scale, tab, &on);
-            if (lev == 0xFFFFFFFFu) { atomicOr(status, ST_NO_NEIGHBOUR); lev = 0; }
+    for (int r0 = 0; r0 < S::NRG; r0 += 32) {
+        const int r = r0 + lane;
+        const int s = r < S::NRG ? r / S::NG : 0, g = r - s * S::NG;
+        const bool act = r < S::NRG && (st.regrid[s] & (1u << g));
+        const float scale = act ? st.scale[s] : 1.f;
+        unsigned on;
+        uint32_t lev = group_levels<T>(st, lane, act, st.xv + s * S::PAD + g * P::GD, st.wa + s * S::PAD + g * P::GD,
+                                       1 / scale, scale, tab, &on);
+        if (act) {
+            if (lev == NONE) { atomicOr(status, ST_NO_NEIGHBOUR); lev = 0; }
             st.lev[s][g] = (uint16_t) lev;
         }
     }
@@ -365,12 +425,12 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
         if (!st.skip[s]) {
             float scale = st.scale[s];
             if (st.regrid[s]) {
-                const float * xv = st.xv + s * S::PAD;
+                const float * wx = st.wx + s * S::PAD;
                 const float * w = st.w + s * S::PAD;
                 float sqx = 0, sq2 = 0;
                 for (int e = 0; e < P::SB; ++e) {
-                    const float q = (float) (2 * level_of<P::GD>(st.lev[s][e / P::GD], e % P::GD) + 1);
-                    sqx += w[e] * xv[e] * q;
+                    const float q = odd_level(level_of<P::GD>(st.lev[s][e / P::GD], e % P::GD));
+                    sqx += wx[e] * q;
                     sq2 += w[e] * q * q;
                 }
                 if (sq2 > 0) scale = sqx / sq2;
@@ -483,7 +543,9 @@ template <int T, int SRC>
 cudaError_t launch_t(const LaunchArgs & a) {
     constexpr int WARPS = 4;
     const size_t smem = sizeof(WarpState<T>) * WARPS;
-    static_assert(sizeof(WarpState<T>) * WARPS <= 48 * 1024, "static smem budget");
+    const cudaError_t e = cudaFuncSetAttribute(k_iq_grid<T, SRC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    if (e != cudaSuccess) return e;
+
     const int64_t grid = (a.nblocks + WARPS - 1) / WARPS;
     k_iq_grid<T, SRC><<<(unsigned) grid, WARPS * 32, smem, a.stream>>>(
         (const uint8_t *) a.src, a.qw, a.qw_mod, a.qw_div, a.qw_mat, (uint8_t *) a.out, a.nblocks, a.tab, a.status);
