@@ -94,6 +94,20 @@ int gpuq_device_count(void);
 size_t gpuq_requantize_dev(int src, const void * d_raw, int type, void * d_dst, int64_t nmat, int64_t nrow,
                            int64_t n_per_row, const float * d_imatrix, void * stream);
 
+/* Scratch size of gpuq_requantize_noalloc, held on every GPU that loads the library, from load to exit. */
+#define GPUQ_NOALLOC_SCRATCH_BYTES ((size_t) 64 << 20)
+
+/* No counterpart in the reference: gpuq_requantize_batch for callers that must not allocate device memory while
+ * they run (a process sharing the GPU under a fixed memory budget, or whose allocator owns all device memory).
+ * Same arguments, same bytes out, but the imatrix, the source bytes and the output are staged in a static device
+ * array of GPUQ_NOALLOC_SCRATCH_BYTES instead of buffers grown with cudaMalloc; it calls no cudaMalloc/cudaFree.
+ * A call whose staged bytes exceed the array returns 0 and says how much it needed (gpuq_last_error).
+ * gpuq_init must have run for the current device; the first call on each device looks up the array's address
+ * (make it before any stream capture). All calls on a device share the array, so calls that overlap on one GPU
+ * race; each call clears the status word it uses. Synchronous, on the default stream. */
+size_t gpuq_requantize_noalloc(int src, const void * raw, int type, void * dst, int64_t nmat, int64_t nrow,
+                               int64_t n_per_row, const float * imatrix);
+
 #ifdef __cplusplus
 }
 #endif

@@ -394,6 +394,15 @@ size_t run_host_job(HostJob & j) {
 }
 
 }  // namespace
+
+const SearchTab * current_search_tab(int type, bool * device_ready) {
+    Device * d = current_device();
+    if (device_ready) *device_ready = d != nullptr;
+    return d ? d->tab(type) : nullptr;
+}
+
+void set_last_error(const char * msg) { t_err = msg; }
+
 }  // namespace gq
 
 using namespace gq;

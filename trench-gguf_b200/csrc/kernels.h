@@ -32,6 +32,12 @@ cudaError_t launch_dequant(int type, const void * q, float * out, int64_t nblock
 // source bytes (F32 / F16 / BF16 / Q8_0 / MXFP4) -> n floats
 cudaError_t launch_decode(int src, const void * raw, float * out, int64_t n, cudaStream_t st);
 
+// The current device's search table of `type` (from gpuq_init), or null when the device is not initialized or the
+// type has no table. Implemented in api.cu.
+const SearchTab * current_search_tab(int type, bool * device_ready);
+// Records the reason of a failed call for gpuq_last_error(). Implemented in api.cu.
+void set_last_error(const char * msg);
+
 inline bool is_iq_grid(int t) { return t == IQ2_XXS || t == IQ2_XS || t == IQ2_S || t == IQ3_XXS || t == IQ3_S; }
 inline bool is_iq1(int t) { return t == IQ1_S || t == IQ1_M; }
 inline bool is_iq4(int t) { return t == IQ4_NL || t == IQ4_XS; }

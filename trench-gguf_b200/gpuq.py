@@ -25,7 +25,8 @@ NO_IMATRIX_OK = {8, 10, 11, 12, 13, 14, 20, 23}
 SYMBOLS = ("gpuq_init", "gpuq_block_bytes", "gpuq_can_quantize", "gpuq_quantize", "gpuq_quantize_batch",
            "gpuq_can_dequantize", "gpuq_requantize", "gpuq_requantize_batch", "gpuq_quantize_dev",
            "gpuq_can_dequantize_type", "gpuq_dequantize_dev", "gpuq_dequantize_src_dev",
-           "gpuq_last_error", "gpuq_status", "gpuq_init_devices", "gpuq_device_count", "gpuq_requantize_dev")
+           "gpuq_last_error", "gpuq_status", "gpuq_init_devices", "gpuq_device_count", "gpuq_requantize_dev",
+           "gpuq_requantize_noalloc")
 
 
 class GpuqError(RuntimeError):
@@ -66,6 +67,7 @@ def declare(gq):
         "gpuq_init_devices": (c.c_int, [c.c_char_p, c.POINTER(c.c_int), c.c_int]),
         "gpuq_device_count": (c.c_int, []),
         "gpuq_requantize_dev": (sz, [c.c_int, vp, c.c_int, vp, i64, i64, i64, vp, vp]),
+        "gpuq_requantize_noalloc": (sz, [c.c_int, vp, c.c_int, vp, i64, i64, i64, vp]),
     }
     for name, (res, args) in sig.items():
         f = getattr(gq, name)
