@@ -1350,6 +1350,9 @@ static int o_dequant_block(int type, const uint8_t * q, float * y, const uint64_
 }
 
 /* ------------------------------------------------------------------------------------------------ C API */
+#ifdef __cplusplus
+extern "C" {
+#endif
 int orc_init(const char * path) {
     FILE * f = fopen(path, "rb");
     if (!f) return 2;
@@ -1357,8 +1360,8 @@ int orc_init(const char * path) {
     g_ntab = 0;
     int32_t hdr[4];
     while (g_ntab < 16 && fread(hdr, sizeof(hdr), 1, f) == 1) {
-        otab_t t = {hdr[0], hdr[1], hdr[2], hdr[3], malloc(8 * (size_t) hdr[1] + 8), malloc(4 * (size_t) hdr[2] + 4),
-                    malloc(2 * (size_t) hdr[3] + 2)};
+        otab_t t = {hdr[0], hdr[1], hdr[2], hdr[3], (uint64_t *) malloc(8 * (size_t) hdr[1] + 8),
+                    (int32_t *) malloc(4 * (size_t) hdr[2] + 4), (uint16_t *) malloc(2 * (size_t) hdr[3] + 2)};
         if (fread(t.grid, 8, hdr[1], f) != (size_t) hdr[1] || fread(t.map, 4, hdr[2], f) != (size_t) hdr[2] ||
             fread(t.neigh, 2, hdr[3], f) != (size_t) hdr[3]) { fclose(f); return 3; }
         g_tab[g_ntab++] = t;
@@ -1424,3 +1427,11 @@ size_t orc_decode(int src, const void * raw, float * out, int64_t n) {
     }
     return (size_t) n * 4;
 }
+#ifdef __cplusplus
+}
+#endif
+
+#ifdef ORACLE_COUNT_OPS
+thread_local unsigned long long g_fops = 0;
+extern "C" unsigned long long orc_fops(int reset) { const unsigned long long v = g_fops; if (reset) g_fops = 0; return v; }
+#endif
