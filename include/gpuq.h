@@ -94,6 +94,12 @@ int gpuq_device_count(void);
 size_t gpuq_requantize_dev(int src, const void * d_raw, int type, void * d_dst, int64_t nmat, int64_t nrow,
                            int64_t n_per_row, const float * d_imatrix, void * stream);
 
+/* LDLQ's block error on the device: E = blk - to_float(d_q) for nblocks super-blocks of `type`, computed in float32
+ * (ggml's to_float, bit for bit) and stored as float64 (f64 != 0) or float32, as tools/ldlq.py:427 forms it from
+ * gpuq_dequantize_dev. d_blk: nblocks x 256 floats. Returns the bytes written to d_err, 0 on error. */
+size_t gpuq_dequantize_error_dev(int type, const void * d_q, const float * d_blk, void * d_err, int f64, int64_t nblocks,
+                                 void * stream);
+
 /* Scratch size of gpuq_requantize_noalloc, held on every GPU that loads the library, from load to exit. */
 #define GPUQ_NOALLOC_SCRATCH_BYTES ((size_t) 64 << 20)
 

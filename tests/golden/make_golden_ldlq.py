@@ -1,0 +1,50 @@
+"""Writes tests/golden/ldlq_golden.npz: the reference's own LDLQ loop on a small case.
+
+Imports trench-gguf's tools/ldlq.py (REF=<checkout>, default /root/reference) and runs its prepare_hessian and
+quantize_matrix with the block quantizer / dequantizer bound to the reference's own block functions compiled for
+the host (oracle/_ref). Stores the inputs (W, H, n, imatrix) and the outputs (bytes and proxy losses of plain
+rounding and of feedback) for IQ2_XXS and IQ1_M. The fixture pins oracle/ldlq_oracle.py (CPU tests) and the GPU
+loop (GPU tests) without the reference present.
+usage: python tests/golden/make_golden_ldlq.py
+"""
+import importlib.util
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+import oracle as orc  # noqa: E402
+import ldlq_oracle  # noqa: E402
+
+
+def main():
+    ref_dir = os.environ.get("REF", "/root/reference")
+    spec = importlib.util.spec_from_file_location("ref_ldlq", os.path.join(ref_dir, "tools", "ldlq.py"))
+    ref = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ref)
+    chk = orc.Checker("reference", os.path.join(ROOT, "trench-gguf_b200", "gpuq_tables.bin"))
+    ne1, ne0, n = 32, 512, 2048
+    H, imatrix = ldlq_oracle.synthetic_hessian(ne0, n, seed=105)
+    rng = np.random.default_rng(205)
+    W = (rng.standard_t(5, (ne1, ne0)) * 0.02).astype(np.float32)
+    out = {"W": W, "H": H, "n": np.array(n), "imatrix": imatrix}
+    U, perm, diag_n, dead = ref.prepare_hessian(H, n, damp=0.01)
+    for name in ("IQ2_XXS", "IQ1_M"):
+        quant, dequant, tsize = ldlq_oracle.checker_quant(chk, orc.TYPES[name])
+        plain, deq_p, _ = ref.quantize_matrix(W, quant, dequant, tsize, imatrix=imatrix, feedback=False)
+        fb, deq_f, _ = ref.quantize_matrix(W, quant, dequant, tsize, U=U, perm=perm, diag_n=diag_n, imatrix=imatrix,
+                                          weights="imatrix", feedback=True)
+        out["%s_plain" % name] = plain
+        out["%s_fb" % name] = fb
+        out["%s_loss_plain" % name] = np.array(ref.proxy_loss(W, deq_p, H, n))
+        out["%s_loss_fb" % name] = np.array(ref.proxy_loss(W, deq_f, H, n))
+        print(name, "proxy loss plain %.6g feedback %.6g" % (out["%s_loss_plain" % name], out["%s_loss_fb" % name]))
+    np.savez_compressed(os.path.join(HERE, "ldlq_golden.npz"), **out)
+    print("wrote", os.path.getsize(os.path.join(HERE, "ldlq_golden.npz")), "bytes")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,125 @@
+"""LDLQ / GPTQ error feedback (config 5).
+
+CPU: oracle/ldlq_oracle.py (the numpy restatement of tools/ldlq.py) reproduces the reference loop's bytes and proxy
+losses (tests/golden/ldlq_golden.npz, made by the reference's own ldlq.py with its host-built quantizer).
+GPU: trench-gguf_b200/ldlq_gpu.py against that restatement with the bar the reference sets for its own GPU loop
+(tools/test_ldlq.py:99-128): the fused error kernel and the plain (no feedback) batch are bit-exact; with feedback
+at least 99.9 % of the super-blocks are identical and the proxy losses agree to 1e-5 relative (float64 solve and
+GEMM summation orders differ between cuBLAS and the CPU BLAS, so an occasional weight can round differently).
+"""
+import os
+
+import numpy as np
+import pytest
+
+import ldlq_oracle as LO
+import oracle as orc
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "ldlq_golden.npz")
+IDENTICAL_MIN = 0.999      # share of identical super-blocks with feedback
+LOSS_RTOL = 1e-5           # relative proxy-loss difference with feedback
+
+
+@pytest.fixture(scope="module")
+def golden():
+    return dict(np.load(GOLDEN))
+
+
+@pytest.mark.parametrize("name", ["IQ2_XXS", "IQ1_M"])
+def test_oracle_ldlq_matches_reference_loop(oracle, golden, name):
+    g = golden
+    W, H, n, im = g["W"], g["H"], int(g["n"]), g["imatrix"]
+    quant, dequant, tsize = LO.checker_quant(oracle, orc.TYPES[name])
+    plain, deq_p = LO.quantize_matrix(W, quant, dequant, tsize, imatrix=im, feedback=False)
+    assert np.array_equal(plain, g["%s_plain" % name])
+    U, perm, diag_n, dead = LO.prepare_hessian(H, n, damp=0.01)
+    fb, deq_f = LO.quantize_matrix(W, quant, dequant, tsize, U=U, perm=perm, imatrix=im, feedback=True)
+    assert np.array_equal(fb, g["%s_fb" % name])
+    assert LO.proxy_loss(W, deq_f, H, n) == float(g["%s_loss_fb" % name])
+    assert LO.proxy_loss(W, deq_f, H, n) < LO.proxy_loss(W, deq_p, H, n)   # feedback helps
+
+
+def test_prepare_hessian_dead_columns_and_act_order():
+    H, _ = LO.synthetic_hessian(512, 1024, seed=3)
+    H[7, :] = 0
+    H[:, 7] = 0
+    U, perm, d, dead = LO.prepare_hessian(H, 1024, order="act")
+    assert dead[7] and not dead[8]
+    assert sorted(perm.tolist()) == list(range(512))
+    assert np.allclose(U, np.triu(U))
+
+
+# ------------------------------------------------------------------------------------------------ GPU
+def _gpu_setup(tables):
+    import torch
+    import gpuq as G
+    import ldlq_gpu
+    g = G.Gpuq(device=0, tables=tables)
+    return torch, G, ldlq_gpu, g
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", ["IQ2_XXS", "IQ1_M", "IQ2_S", "IQ3_XXS", "IQ4_XS"])
+def test_gpu_error_kernel_is_blk_minus_to_float(tables, name):
+    torch, G, ldlq_gpu, g = _gpu_setup(tables)
+    gqt = ldlq_gpu.GpuQuant(g, G.TYPES[name])
+    rng = np.random.default_rng(9)
+    blk = torch.from_numpy((rng.standard_normal((2, 5, 256)) * 0.03).astype(np.float32)).cuda()
+    qw = torch.from_numpy(rng.gamma(1.0, 1.0, (2, 256)).astype(np.float32)).cuda()
+    raw = torch.empty((2, 5, gqt.tsize), dtype=torch.uint8, device="cuda")
+    gqt.quant(blk, qw, raw)
+    q = gqt.dequant(raw)
+    for dt in (torch.float64, torch.float32):
+        E = gqt.error(raw, blk, dt)
+        assert torch.equal(E, (blk - q).to(dt))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", ["IQ2_XXS", "IQ1_M"])
+def test_gpu_ldlq_against_reference_loop(tables, oracle, golden, name):
+    torch, G, ldlq_gpu, g = _gpu_setup(tables)
+    gd = golden
+    W, H, n, im = gd["W"], gd["H"], int(gd["n"]), gd["imatrix"]
+    gqt = ldlq_gpu.GpuQuant(g, G.TYPES[name])
+    dev = torch.device("cuda")
+    Wd = torch.from_numpy(W[None].copy()).to(dev)
+    imd = torch.from_numpy(im[None].copy()).to(dev)
+    plain = ldlq_gpu.quantize_matrix_torch(Wd, gqt, imatrix=imd, feedback=False).cpu().numpy()[0]
+    assert np.array_equal(plain, gd["%s_plain" % name])
+    U, perm, diag_n, _ = LO.prepare_hessian(H, n, damp=0.01)
+    fb = ldlq_gpu.quantize_matrix_torch(Wd, gqt, U=torch.from_numpy(U).to(dev), perm=torch.from_numpy(perm).to(dev),
+                                        diag_n=torch.from_numpy(diag_n).to(dev), imatrix=imd, weights="imatrix",
+                                        feedback=True, f64=True).cpu().numpy()[0]
+    tsize = gqt.tsize
+    same = (fb.reshape(W.shape[0], -1, tsize) == gd["%s_fb" % name].reshape(W.shape[0], -1, tsize)).all(-1).mean()
+    assert same >= IDENTICAL_MIN
+    deq = oracle.dequantize(G.TYPES[name], fb).reshape(W.shape)
+    loss, want = ldlq_gpu.proxy_loss(W, deq, H, n), float(gd["%s_loss_fb" % name])
+    assert abs(loss - want) <= LOSS_RTOL * want
+
+
+@pytest.mark.gpu
+def test_gpu_ldlq_batch_and_larger_case(tables, oracle):
+    """gate + up as one batch sharing U (B = 2), 64 rows x 1024 columns (4 blocks): each matrix against the
+    restatement's loop on the same U"""
+    torch, G, ldlq_gpu, g = _gpu_setup(tables)
+    ne1, ne0, n = 64, 1024, 4096
+    H, im = LO.synthetic_hessian(ne0, n, seed=55)
+    rng = np.random.default_rng(56)
+    Ws = [(rng.standard_t(5, (ne1, ne0)) * 0.02).astype(np.float32) for _ in range(2)]
+    ims = [im, (im * (0.5 + rng.random(ne0))).astype(np.float32)]
+    U, perm, diag_n, _ = LO.prepare_hessian(H, n, damp=0.01)
+    typ = G.TYPES["IQ2_XXS"]
+    gqt = ldlq_gpu.GpuQuant(g, typ)
+    dev = torch.device("cuda")
+    out = ldlq_gpu.quantize_matrix_torch(torch.from_numpy(np.stack(Ws)).to(dev), gqt, U=torch.from_numpy(U).to(dev),
+                                         perm=torch.from_numpy(perm).to(dev), diag_n=torch.from_numpy(diag_n).to(dev),
+                                         imatrix=torch.from_numpy(np.stack(ims)).to(dev), feedback=True).cpu().numpy()
+    quant, dequant, tsize = LO.checker_quant(oracle, typ)
+    for b in range(2):
+        want, deq_w = LO.quantize_matrix(Ws[b], quant, dequant, tsize, U=U, perm=perm, imatrix=ims[b], feedback=True)
+        same = (out[b].reshape(ne1, -1, tsize) == want.reshape(ne1, -1, tsize)).all(-1).mean()
+        assert same >= IDENTICAL_MIN, (b, same)
+        deq = oracle.dequantize(typ, out[b]).reshape(ne1, ne0)
+        lw = LO.proxy_loss(Ws[b], deq_w, H, n)
+        assert abs(LO.proxy_loss(Ws[b], deq, H, n) - lw) <= LOSS_RTOL * lw

@@ -589,6 +589,21 @@ size_t gpuq_dequantize_dev(int type, const void * d_q, float * d_out, int64_t nb
     return (size_t) nblocks * QK * 4;
 }
 
+size_t gpuq_dequantize_error_dev(int type, const void * d_q, const float * d_blk, void * d_err, int f64, int64_t nblocks,
+                                 void * stream) {
+    if (!gpuq_can_dequantize_type(type) || nblocks <= 0 || !d_q || !d_blk || !d_err) {
+        set_err("gpuq_dequantize_error_dev: bad arguments");
+        return 0;
+    }
+    Device * d = current_device();
+    if (!d) { set_err("gpuq_dequantize_error_dev: current device not initialized"); return 0; }
+    if (launch_dequant_error(type, d_q, d_blk, d_err, f64 != 0, nblocks, DequantTab{d->dq_grid(type)}, (cudaStream_t) stream) != cudaSuccess) {
+        set_err("gpuq_dequantize_error_dev: launch failed");
+        return 0;
+    }
+    return (size_t) nblocks * QK * (f64 ? 8 : 4);
+}
+
 size_t gpuq_dequantize_src_dev(int src, const void * d_raw, float * d_out, int64_t n, void * stream) {
     if (!raw_bytes(src, 32) || n <= 0 || n % 32 || !d_raw || !d_out) { set_err("gpuq_dequantize_src_dev: bad arguments"); return 0; }
     if (launch_decode(src, d_raw, d_out, n, (cudaStream_t) stream) != cudaSuccess) { set_err("gpuq_dequantize_src_dev: launch failed"); return 0; }

@@ -127,6 +127,30 @@ __global__ void __launch_bounds__(256) k_dequant(const uint8_t * __restrict__ q,
     }
 }
 
+// LDLQ's block error: E = blk - to_float(q) in float32 (ggml's to_float), stored as float64 or float32
+// (tools/ldlq.py:427 `E = (blk - q).to(Ud.dtype)`), one pass over the bytes and the block
+template <int T, bool F64>
+__global__ void __launch_bounds__(256) k_dequant_error(const uint8_t * __restrict__ q, const float * __restrict__ blk,
+                                                       void * __restrict__ err, int64_t nblocks,
+                                                       const uint64_t * __restrict__ grid) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = (int64_t) gridDim.x * (blockDim.x >> 5);
+    for (int64_t b = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); b < nblocks; b += nw) {
+        float y[8], x[8];
+        dq8<T>(q + b * block_bytes(T), lane, grid, y);
+        load8_f32(blk + b * QK + lane * 8, x);
+        if constexpr (F64) {
+            double * e = reinterpret_cast<double *>(err) + b * QK + lane * 8;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) e[j] = (double) (x[j] - y[j]);
+        } else {
+            float * e = reinterpret_cast<float *>(err) + b * QK + lane * 8;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) e[j] = x[j] - y[j];
+        }
+    }
+}
+
 template <int SRC>
 __global__ void __launch_bounds__(256) k_decode(const uint8_t * __restrict__ raw, float * __restrict__ out, int64_t n8) {
     const int64_t stride = (int64_t) gridDim.x * blockDim.x;
@@ -169,6 +193,27 @@ cudaError_t launch_dequant(int type, const void * q, float * out, int64_t nblock
         case IQ4_XS:  k_dequant<IQ4_XS><<<g, 256, 0, st>>>(qb, out, nblocks, tab.grid); break;
         default: return cudaErrorInvalidValue;
     }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_dequant_error(int type, const void * q, const float * blk, void * err, bool f64, int64_t nblocks,
+                                 DequantTab tab, cudaStream_t st) {
+    const int g = grid_for(nblocks, 8);
+    const uint8_t * qb = (const uint8_t *) q;
+#define DE(T) (f64 ? (k_dequant_error<T, true><<<g, 256, 0, st>>>(qb, blk, err, nblocks, tab.grid), 0) \
+                   : (k_dequant_error<T, false><<<g, 256, 0, st>>>(qb, blk, err, nblocks, tab.grid), 0))
+    switch (type) {
+        case IQ2_XXS: DE(IQ2_XXS); break;
+        case IQ2_XS:  DE(IQ2_XS); break;
+        case IQ2_S:   DE(IQ2_S); break;
+        case IQ3_XXS: DE(IQ3_XXS); break;
+        case IQ3_S:   DE(IQ3_S); break;
+        case IQ1_S:   DE(IQ1_S); break;
+        case IQ1_M:   DE(IQ1_M); break;
+        case IQ4_XS:  DE(IQ4_XS); break;
+        default: return cudaErrorInvalidValue;
+    }
+#undef DE
     return cudaGetLastError();
 }
 

@@ -29,6 +29,9 @@ cudaError_t launch_kquant(int type, const LaunchArgs & a);    // Q2_K .. Q6_K, Q
 
 // ggml's to_float of the i-quant types with grids and IQ4_XS: nblocks super-blocks -> nblocks*256 floats
 cudaError_t launch_dequant(int type, const void * q, float * out, int64_t nblocks, DequantTab tab, cudaStream_t st);
+// LDLQ block error E = blk - to_float(q), float32 maths, stored as float64 (f64) or float32
+cudaError_t launch_dequant_error(int type, const void * q, const float * blk, void * err, bool f64, int64_t nblocks,
+                                 DequantTab tab, cudaStream_t st);
 // source bytes (F32 / F16 / BF16 / Q8_0 / MXFP4) -> n floats
 cudaError_t launch_decode(int src, const void * raw, float * out, int64_t n, cudaStream_t st);
 

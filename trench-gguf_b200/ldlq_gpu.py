@@ -1,0 +1,181 @@
+"""LDLQ / GPTQ error-feedback re-quantization on the B200 (config 5), over this library's device API.
+
+Mirrors trench-gguf's GPU loop in tools/ldlq.py - `GpuQuant` (ldlq.py:334-388), `prepare_hessian_torch`
+(ldlq.py:275-323), `quantize_matrix_torch` (ldlq.py:391-431), `proxy_loss` (ldlq.py:110-113) - with the same
+names, arguments and results, so ldlq.py's callers can switch modules. The maths is the reference's: for each
+256-column block (a super-block of the type) in order, quantize the block (this library's byte-identical
+kernels, gpuq_quantize_dev), dequantize it (gpuq_dequantize_dev, ggml's to_float bit for bit), form E = W_B - Q_B
+in float32 cast to float64, solve E U_BB^-1 (float64 triangular solve) and subtract (E U_BB^-1) U_B,rest cast to
+float32 from the remaining columns. The triangular solve and the float64 update are plain library calls (cuBLAS
+through torch); the quantizer, the dequantizer and the error are this library's kernels, fused where ggml's order
+allows (gpuq_dequantize_error_dev forms E from the bytes in one pass).
+
+Several matrices that share U (gate and up of one expert) run as one batch: one quantize launch a block for all
+their rows (block b of the batch takes imatrix row b // rows).
+"""
+import ctypes
+
+import numpy as np
+
+import gpuq as G
+
+QK = 256
+
+
+class GpuQuant:
+    """device-pointer quantizer / dequantizer of one type for torch tensors (the reference's GpuQuant contract)"""
+
+    def __init__(self, gq, typ, tsize=None, bs=QK):
+        self.gq = gq if hasattr(gq, "gpuq_quantize_dev") else gq.lib
+        G.declare(self.gq)
+        self.typ, self.bs = int(typ), bs
+        self.tsize = int(tsize or self.gq.gpuq_block_bytes(self.typ))
+
+    @staticmethod
+    def supported(gq, typ):
+        lib = gq if hasattr(gq, "gpuq_quantize_dev") else gq.lib
+        G.declare(lib)
+        return lib.gpuq_block_bytes(int(typ)) > 0 and int(typ) != 20 and lib.gpuq_can_dequantize_type(int(typ)) == 1
+
+    @staticmethod
+    def _stream():
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+
+    def _err(self, what):
+        return RuntimeError("%s failed (type %d): %s" % (what, self.typ, self.gq.gpuq_last_error().decode()))
+
+    def quant(self, blk, qw, raw):
+        """blk [B, rows, bs] f32 contiguous (device), qw [B, bs] f32 contiguous -> raw [B, rows, tsize] uint8"""
+        B, rows = blk.shape[0], blk.shape[1]
+        got = self.gq.gpuq_quantize_dev(self.typ, blk.data_ptr(), raw.data_ptr(), B * rows, qw.data_ptr(), B * rows,
+                                        rows, self._stream())
+        if got != B * rows * self.tsize:
+            raise self._err("gpuq_quantize_dev")
+
+    def dequant(self, raw):
+        """raw [B, rows, tsize] uint8 contiguous -> f32 [B, rows, bs]"""
+        import torch
+        B, rows = raw.shape[0], raw.shape[1]
+        f = torch.empty((B, rows, self.bs), dtype=torch.float32, device=raw.device)
+        if self.gq.gpuq_dequantize_dev(self.typ, raw.data_ptr(), f.data_ptr(), B * rows, self._stream()) == 0:
+            raise self._err("gpuq_dequantize_dev")
+        return f
+
+    def error(self, raw, blk, out_dtype):
+        """E = (blk - to_float(raw)) in float32, cast to out_dtype (float64 or float32): one kernel"""
+        import torch
+        B, rows = raw.shape[0], raw.shape[1]
+        E = torch.empty((B, rows, self.bs), dtype=out_dtype, device=raw.device)
+        f64 = 1 if out_dtype == torch.float64 else 0
+        if self.gq.gpuq_dequantize_error_dev(self.typ, raw.data_ptr(), blk.data_ptr(), E.data_ptr(), f64, B * rows,
+                                             self._stream()) == 0:
+            raise self._err("gpuq_dequantize_error_dev")
+        return E
+
+    def dequant_src(self, src, raw_host, n, device):
+        """source tensor bytes (ggml type src, numpy uint8) -> f32 [n] on the device, None if not decodable here"""
+        import torch
+        if self.gq.gpuq_can_dequantize(int(src)) != 1:
+            return None
+        rb = torch.from_numpy(np.ascontiguousarray(raw_host).reshape(-1)).to(device)
+        f = torch.empty(n, dtype=torch.float32, device=device)
+        if self.gq.gpuq_dequantize_src_dev(int(src), rb.data_ptr(), f.data_ptr(), n, self._stream()) == 0:
+            raise self._err("gpuq_dequantize_src_dev")
+        return f
+
+
+def prepare_hessian_torch(H, n, damp=0.01, order="seq", bs=QK, device="cuda", out="numpy"):
+    """ldlq.py:275-323: normalised, dead columns zeroed, optional act-order block permutation, damped; U the upper
+    Cholesky factor of the inverse (float32 on the GPU first; float64 and more ridge when it does not factor).
+    Returns (U float64, perm, diag_n, dead) as numpy arrays, or with out="torch" as tensors on `device`."""
+    import torch
+    dt = torch.float64 if device == "cpu" else torch.float32
+    ne0 = H.shape[0]
+    if isinstance(H, torch.Tensor):
+        Hn = H.to(device=device, dtype=torch.float64) / max(float(n), 1.0)
+    else:
+        Hn = torch.as_tensor(np.asarray(H), dtype=torch.float64).to(device) / max(float(n), 1.0)
+    d = torch.diagonal(Hn).clone()
+    dead = d <= 0
+    if bool(dead.any()):
+        Hn[dead, :] = 0
+        Hn[:, dead] = 0
+        Hn[dead, dead] = 1.0
+        d = torch.diagonal(Hn).clone()
+    nblk = ne0 // bs
+    if order == "act":
+        blk_order = torch.argsort(-d.reshape(nblk, bs).sum(1), stable=True)
+    else:
+        blk_order = torch.arange(nblk, device=device)
+    perm = (blk_order[:, None] * bs + torch.arange(bs, device=device)[None]).reshape(-1)
+    Hp64 = Hn[perm][:, perm]
+    mean_d = float(torch.diagonal(Hp64).mean())
+
+    def factor(dtype, extra):
+        Hp = Hp64.to(dtype).clone()
+        Hp.diagonal().add_((damp + extra) * mean_d)
+        Lc = torch.linalg.cholesky(Hp)
+        Hinv = torch.cholesky_inverse(Lc)
+        Hinv = 0.5 * (Hinv + Hinv.T)
+        return torch.linalg.cholesky(Hinv, upper=True)
+
+    U = None
+    for dtype, extra in ((dt, 0.0), (torch.float64, 0.0), (torch.float64, 10 * damp), (torch.float64, 100 * damp)):
+        try:
+            U = factor(dtype, extra)
+            break
+        except Exception:
+            continue
+    if U is None:
+        raise RuntimeError("Hessian could not be factored even with %.0f%% ridge" % (100 * (damp + 100 * damp)))
+    if out == "torch":
+        return U.double(), perm, d[perm], dead
+    return U.double().cpu().numpy(), perm.cpu().numpy(), d[perm].cpu().numpy(), dead.cpu().numpy()
+
+
+def quantize_matrix_torch(W, gqt, U=None, perm=None, diag_n=None, imatrix=None, weights="imatrix", feedback=True,
+                          bs=QK, f64=True):
+    """ldlq.py:391-431. W: f32 [B, ne1, ne0] on the device (B matrices sharing U and perm); gqt: GpuQuant; U:
+    [ne0, ne0] on the device; perm: [ne0] long; diag_n: [ne0] (permuted order); imatrix: [B, ne0] f32.
+    Returns uint8 [B, ne1, nblk*tsize] on the device in GGUF row layout."""
+    import torch
+    B, ne1, ne0 = W.shape
+    nblk = ne0 // bs
+    tsize = gqt.tsize
+    dev = W.device
+    if perm is None:
+        perm = torch.arange(ne0, device=dev)
+    Wp = W.index_select(2, perm).contiguous()
+    Ud = None
+    if feedback:
+        Ud = U.to(torch.float64 if f64 else torch.float32)
+    if weights == "imatrix":
+        imp = imatrix.index_select(1, perm).contiguous()
+    elif weights == "diag":
+        imp = diag_n.to(torch.float32)[None].expand(B, ne0).contiguous()
+    elif weights != "schur":
+        raise ValueError(weights)
+    blk_order = (perm.view(nblk, bs)[:, 0] // bs).tolist()
+    out = torch.empty((nblk, B, ne1, tsize), dtype=torch.uint8, device=dev)
+    for k in range(nblk):
+        c0, c1 = k * bs, (k + 1) * bs
+        blk = Wp[:, :, c0:c1].contiguous()
+        if weights == "schur":
+            Ubb = U[c0:c1, c0:c1].double()
+            qw = torch.diagonal(torch.linalg.inv(Ubb.T @ Ubb)).to(torch.float32)[None].expand(B, bs).contiguous()
+        else:
+            qw = imp[:, c0:c1].contiguous()
+        raw = out[blk_order[k]]
+        gqt.quant(blk, qw, raw)
+        if feedback and k + 1 < nblk:
+            E = gqt.error(raw, blk, Ud.dtype)
+            Es = torch.linalg.solve_triangular(Ud[c0:c1, c0:c1], E, upper=True, left=False)   # E U_BB^-1
+            Wp[:, :, c1:] -= (Es @ Ud[c0:c1, c1:]).to(torch.float32)
+    return out.permute(1, 2, 0, 3).reshape(B, ne1, nblk * tsize)
+
+
+def proxy_loss(W, deq, H, n):
+    """tr((W - Q) H (W - Q)^T) / n (ldlq.py:110-113), numpy inputs"""
+    D = (np.asarray(W) - np.asarray(deq)).astype(np.float64)
+    return float(np.einsum("ij,jk,ik->", D, np.asarray(H, dtype=np.float64), D) / max(float(n), 1.0))
