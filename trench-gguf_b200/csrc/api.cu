@@ -281,6 +281,9 @@ int64_t chunk_values() {
 // runs the chunks [c0, c1) of a job on one device through the 3-stream pipeline; false on error
 bool run_chunks(Device & d, const HostJob & j, size_t c0, size_t c1) {
     std::lock_guard<std::mutex> lk(d.mu);
+    if (const char * f = std::getenv("GPUQ_FAIL_DEVICE")) {   // host-side fault injection: this device's worker fails
+        if (std::atoi(f) == d.id) { set_err("device worker failure injected by GPUQ_FAIL_DEVICE"); return false; }
+    }
     if (cudaSetDevice(d.id) != cudaSuccess) { set_err("cudaSetDevice(%d) failed", d.id); return false; }
     const int bs = block_len(j.type), bb = block_bytes(j.type);
     const int64_t nb_row = j.n_per_row / bs;
