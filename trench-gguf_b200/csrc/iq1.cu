@@ -2,24 +2,18 @@
 // (trench-gguf gpuq.hip:390-514, :517-688).
 //
 // Per sub-block (32 weights for IQ1_S, 16 for IQ1_M): the weights sorted (stable), weighted prefix sums, then an
-// exhaustive search over every split (i1 <= i2) of the sorted weights into the three levels {-1, 0, +1} + shift,
-// keeping the split with the best least-squares score; the levels are then snapped to the 2048-point codebook
-// (neighbour search with the shifted level values), the scale refit, and the scales coded (IQ1_M also refits the
-// super-block scale over all 256 weights).
+// exhaustive scan over every split (i1 <= i2) of the sorted weights into the three levels {-1, 0, +1} + shift,
+// keeping the split with the best least-squares score (a strictly sequential rule: ggml accepts when
+// sumqx^2 > best*sumq2, re-rounding best at each acceptance); the levels are then snapped to the 2048-point
+// codebook (nearest listed neighbour with the shifted level values), the scale refit, and the scales coded
+// (IQ1_M also refits the super-block scale over all 256 weights, skipped sub-blocks included).
 //
-// sm_100a mapping: one warp a super-block, sub-blocks in turn. Lanes own independent work:
-//   * weights and the stable-sort rank of one weight a lane (rank = #smaller + #equal before it: ggml's stable
-//     order, -0 == +0);
-//   * 32 splits a round in the split search (561 splits x 2 shifts for IQ1_S, 153 x 4 for IQ1_M);
-//   * 32 codebook candidates at a time in the neighbour searches (the first minimum in list order wins: an exact
-//     (distance, position) argmin).
-// ggml accepts a candidate when sumqx^2 > best*sumq2 with best re-rounded at each acceptance, a strictly
-// sequential rule. It is reproduced exactly: a candidate whose score is below (1 - 2^-11) of the best score seen
-// before it cannot be accepted (the running best can only drift by a few ulps an acceptance), so only the
-// candidates at or near a running maximum are replayed, in candidate order, by the whole warp in lockstep with
-// ggml's own comparison. If more than 256 candidates of one sub-block ever qualify (where the drift bound would
-// need checking), that sub-block's search is replayed over every candidate instead.
-// Sums that ggml runs in index order (sumx2, the prefix sums, the refits) run in index order inside one lane.
+// sm_100a mapping: one warp a tile of 32 sub-blocks (4 IQ1_S or 2 IQ1_M super-blocks), ONE LANE A SUB-BLOCK.
+// Every lane runs its sub-block's sort, prefix sums, split scan, codebook snap and refit exactly as ggml does -
+// sequential order inside the lane, so the decisions are ggml's by construction - and the 32 lanes run 32
+// sub-blocks side by side (the reference runs one super-block a thread). Per-lane arrays live in shared memory
+// lane-minor ([element][lane]): every access of the warp hits 32 different banks. One lane a super-block computes
+// sumx2 and the super-block scale in index order; the bytes leave through coalesced stores.
 #include "common.cuh"
 #include "source.cuh"
 #include "kernels.h"
@@ -28,35 +22,23 @@ namespace gq {
 namespace {
 
 constexpr float DELTA = 0.125f;
-// the splits (i1, i2), 0 <= i1 <= i2 <= n, in ggml's loop order (i1 outer, i2 inner)
-template <int N, int NP> struct Splits { uint8_t v[NP][2]; };
-template <int N, int NP> constexpr Splits<N, NP> make_splits() {
-    Splits<N, NP> p{};
-    int k = 0;
-    for (int i1 = 0; i1 <= N; ++i1)
-        for (int i2 = i1; i2 <= N; ++i2) { p.v[k][0] = (uint8_t) i1; p.v[k][1] = (uint8_t) i2; ++k; }
-    return p;
-}
-__constant__ Splits<32, 561> c_split32 = make_splits<32, 561>();
-__constant__ Splits<16, 153> c_split16 = make_splits<16, 153>();
-constexpr float FILTER = 1.0f - 0x1.0p-11f;
-constexpr int MAX_REPLAY = 256;
 
 template <int T> struct IQ1;
-template <> struct IQ1<IQ1_S> { static constexpr int SB = 32, NPAIR = 561, NC = 2; static constexpr float EPS = 1e-12f; };
-template <> struct IQ1<IQ1_M> { static constexpr int SB = 16, NPAIR = 153, NC = 4; static constexpr float EPS = 1e-7f; };
+template <> struct IQ1<IQ1_S> { static constexpr int SB = 32, WARPS = 2; static constexpr float EPS = 1e-12f; };
+template <> struct IQ1<IQ1_M> { static constexpr int SB = 16, WARPS = 4; static constexpr float EPS = 1e-7f; };
 
-template <int T> struct alignas(16) IQ1State {
-    static constexpr int SB = IQ1<T>::SB, NSUB = QK / SB;
-    float x[QK], w[QK];
-    float px[2][SB + 1], pw[2][SB + 1];     // IQ1_S uses px[0] / pw[0] only
-    int idx[SB];
-    int8_t L[SB];
-    float scales[NSUB];
-    int8_t shifts[NSUB];
-    uint16_t gidx[NSUB][SB / 8];
-    float sigma2;
-    uint8_t out[56];
+template <int T> struct alignas(16) IQ1Warp {
+    static constexpr int SB = IQ1<T>::SB, NSUB = QK / SB, NSB = 32 / NSUB, NH = T == IQ1_M ? 2 : 1;
+    float x[SB][32], w[SB][32];              // the lane's sub-block, element-major / lane-minor
+    float px[NH][SB + 1][32], pw[NH][SB + 1][32];   // prefix sums (IQ1_M: one pair a half of the sub-block)
+    uint8_t idx[SB][32];                     // stable ascending order of the sub-block's weights
+    int8_t L[SB][32];
+    float scales[32];
+    int8_t shifts[32];
+    uint8_t dropped[32];                     // sub-block skipped by ggml: nothing written for it
+    uint16_t gidx[SB / 8][32];
+    float sigma2[NSB];
+    uint8_t out[NSB][56];
 };
 
 // the shifted level values of level l: x_p = {-1+d, d, 1+d}, x_m = {-1-d, -d, 1-d} (gpuq.hip:404-405)
@@ -64,310 +46,265 @@ __device__ __forceinline__ float lvl(int l, bool minus) {
     return minus ? (l == 0 ? -1 - DELTA : (l == 1 ? -DELTA : 1 - DELTA)) : (l == 0 ? -1 + DELTA : (l == 1 ? DELTA : 1 + DELTA));
 }
 
-// one candidate's (sumqx, sumq2) -> IQ1_S split score terms, ggml's expressions (gpuq.hip:441-448)
-__device__ __forceinline__ void iq1s_cand(const float * sx, const float * sw, int i1, int i2, bool minus, float & qx, float & q2) {
-    const float a = lvl(0, minus), b = lvl(1, minus), c = lvl(2, minus);
-    qx = (sx[i1] - sx[0]) * a + (sx[i2] - sx[i1]) * b + (sx[32] - sx[i2]) * c;
-    q2 = (sw[i1] - sw[0]) * a * a + (sw[i2] - sw[i1]) * b * b + (sw[32] - sw[i2]) * c * c;
-}
-
-// IQ1_M: the four shift combinations of one split (gpuq.hip:579-603)
-__device__ __forceinline__ void iq1m_cands(const IQ1State<IQ1_M> & st, int i1, int i2, float * qx, float * q2) {
-    const float p2 = 1 + DELTA, m2 = 1 - DELTA;
-    const float cp1 = (-1 + DELTA) * (-1 + DELTA) - DELTA * DELTA, cp2 = DELTA * DELTA - (1 + DELTA) * (1 + DELTA);
-    const float cm1 = (-1 - DELTA) * (-1 - DELTA) - (-DELTA) * (-DELTA), cm2 = (-DELTA) * (-DELTA) - (1 - DELTA) * (1 - DELTA);
-    float qxp[2], qxm[2], q2p[2], q2m[2];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        const float tx = st.px[h][16], tw = st.pw[h][16];
-        const float sx = st.px[h][i1] + st.px[h][i2];
-        qxp[h] = tx * p2 - sx;
-        qxm[h] = tx * m2 - sx;
-        q2p[h] = tw * p2 * p2 + st.pw[h][i1] * cp1 + st.pw[h][i2] * cp2;
-        q2m[h] = tw * m2 * m2 + st.pw[h][i1] * cm1 + st.pw[h][i2] * cm2;
-    }
-    qx[0] = qxp[0] + qxp[1]; qx[1] = qxp[0] + qxm[1]; qx[2] = qxm[0] + qxp[1]; qx[3] = qxm[0] + qxm[1];
-    q2[0] = q2p[0] + q2p[1]; q2[1] = q2p[0] + q2m[1]; q2[2] = q2m[0] + q2p[1]; q2[3] = q2m[0] + q2m[1];
-}
-
-__device__ __forceinline__ float approx_score(float qx, float q2) { return q2 > 0 ? qx * qx / q2 : -FLT_MAX; }
-
-// The split search of one sub-block, warp-wide. Returns (b1, b2, bk) and the accepted scale (ggml's last
-// accepted candidate), all warp-uniform; b1 < 0 when nothing was accepted.
+// nearest listed codebook point to the 8 weights of group g of this lane's sub-block, shifted levels (minus: x_m),
+// scale s (iq1_find_best_neighbour2, gpuq.hip:199-232): ggml's distance d2 = 0; d2 += w_i (s q_i - x_i)^2 in order,
+// the first strict minimum in list order. Returns the grid index, -1 if no listed candidate is finite (ggml would
+// then scan the whole grid reading past the group - reported as a device-status error instead).
 template <int T>
-__device__ void split_search(const IQ1State<T> & st, int lane, int & b1, int & b2, int & bk, float & scale, float mx) {
-    constexpr int NP = IQ1<T>::NPAIR, NC = IQ1<T>::NC;
-    float best = -FLT_MAX;
-    scale = mx;
-    b1 = b2 = bk = -1;
-    float carry = -FLT_MAX;    // max score of the candidates of earlier rounds
-    int replayed = 0;
-    bool overflow = false;
-    for (int r0 = 0; r0 < NP && !overflow; r0 += 32) {
-        const int k = r0 + lane;
-        const bool live = k < NP;
-        int i1 = 0, i2 = 0;
-        float qx[NC], q2[NC];
-        if (live) {
-            if (T == IQ1_S) { i1 = c_split32.v[k][0]; i2 = c_split32.v[k][1]; }
-            else { i1 = c_split16.v[k][0]; i2 = c_split16.v[k][1]; }
-            if constexpr (T == IQ1_S) {
-                iq1s_cand(st.px[0], st.pw[0], i1, i2, false, qx[0], q2[0]);
-                iq1s_cand(st.px[0], st.pw[0], i1, i2, true, qx[1], q2[1]);
-            } else {
-                iq1m_cands(st, i1, i2, qx, q2);
-            }
-        } else {
+__device__ int snap_group(const IQ1Warp<T> & st, int lane, int g, int m, float s, bool minus, const SearchTab & tab) {
+    float t0[8], t1[8], t2[8];
+    const float q0 = lvl(0, minus), q1 = lvl(1, minus), q2 = lvl(2, minus);
 #pragma unroll
-            for (int c = 0; c < NC; ++c) { qx[c] = 0; q2[c] = 0; }
-        }
-        // exclusive prefix max of the scores over the lanes before this one (candidate order), plus the carry
-        float sc[NC], lmax = -FLT_MAX;
-#pragma unroll
-        for (int c = 0; c < NC; ++c) { sc[c] = approx_score(qx[c], q2[c]); lmax = fmaxf(lmax, sc[c]); }
-        float incl = lmax;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const float v = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl = fmaxf(incl, v);
-        }
-        float run = fmaxf(carry, __shfl_up_sync(0xffffffffu, incl, 1));
-        if (lane == 0) run = carry;
-        unsigned flags = 0;
-#pragma unroll
-        for (int c = 0; c < NC; ++c) {
-            if (q2[c] > 0 && !(sc[c] < run * FILTER)) flags |= 1u << c;
-            run = fmaxf(run, sc[c]);
-        }
-        carry = fmaxf(carry, __shfl_sync(0xffffffffu, incl, 31));
-        unsigned m = __ballot_sync(0xffffffffu, flags != 0);
-        while (m) {
-            const int src = __ffs(m) - 1;
-            m &= m - 1;
-            const unsigned f = __shfl_sync(0xffffffffu, flags, src);
-            const int ci1 = __shfl_sync(0xffffffffu, i1, src), ci2 = __shfl_sync(0xffffffffu, i2, src);
-#pragma unroll
-            for (int c = 0; c < NC; ++c) {
-                const float cqx = __shfl_sync(0xffffffffu, qx[c], src), cq2 = __shfl_sync(0xffffffffu, q2[c], src);
-                if (!(f & (1u << c))) continue;
-                ++replayed;
-                if (cq2 > 0 && cqx * cqx > best * cq2) {
-                    scale = cqx / cq2;
-                    best = scale * cqx;
-                    b1 = ci1; b2 = ci2; bk = c;
-                }
-            }
-        }
-        if (replayed > MAX_REPLAY) overflow = true;
+    for (int i = 0; i < 8; ++i) {
+        const float xi = st.x[8 * g + i][lane], wi = st.w[8 * g + i][lane];
+        const float d0 = s * q0 - xi, d1 = s * q1 - xi, d2 = s * q2 - xi;
+        t0[i] = wi * d0 * d0; t1[i] = wi * d1 * d1; t2[i] = wi * d2 * d2;
     }
-    if (!overflow) return;
-    // pathological score landscape: the whole sequence in order, every candidate (exact by construction)
-    best = -FLT_MAX; scale = mx; b1 = b2 = bk = -1;
-    for (int k = 0; k < NP; ++k) {
-        int i1, i2;
-        float qx[NC], q2[NC];
-        if (T == IQ1_S) { i1 = c_split32.v[k][0]; i2 = c_split32.v[k][1]; }
-        else { i1 = c_split16.v[k][0]; i2 = c_split16.v[k][1]; }
-        if constexpr (T == IQ1_S) {
-            iq1s_cand(st.px[0], st.pw[0], i1, i2, false, qx[0], q2[0]);
-            iq1s_cand(st.px[0], st.pw[0], i1, i2, true, qx[1], q2[1]);
-        } else {
-            iq1m_cands(st, i1, i2, qx, q2);
-        }
-#pragma unroll
-        for (int c = 0; c < NC; ++c)
-            if (q2[c] > 0 && qx[c] * qx[c] > best * q2[c]) { scale = qx[c] / q2[c]; best = scale * qx[c]; b1 = i1; b2 = i2; bk = c; }
-    }
-}
-
-// nearest listed codebook point to the 8 weights x (weights w) with shifted levels (minus: x_m) and scale s
-// (iq1_find_best_neighbour2, gpuq.hip:199-232): warp-wide over the list, the first minimum wins. Returns the
-// grid index, -1 if no candidate has a finite distance.
-__device__ int iq1_nearest(const SearchTab & tab, int c3, const float * x, const float * w, float s, bool minus, int lane) {
-    const uint32_t * lst = tab.neigh + (-__ldg(tab.code3 + c3) - 1);
+    const uint32_t * lst = tab.neigh + (-m - 1);
     const int n = (int) __ldg(lst);
     float best = FLT_MAX;
-    int bj = 0x7fffffff;
-    uint32_t be = 0;
-    for (int j = 1 + lane; j <= n; j += 32) {
-        const uint32_t e = __ldg(lst + j);
+    uint32_t bl = 0xFFFFFFFFu;
+    uint32_t e = __ldg(lst + 1);
+    for (int j = 1; j <= n; ++j) {
+        const uint32_t en = j < n ? __ldg(lst + j + 1) : 0u;
         float d2 = 0.f;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            const float q = lvl((e >> (2 * i)) & 3u, minus);
-            const float d = s * q - x[i];
-            d2 += w[i] * d * d;
+            const uint32_t l = (e >> (2 * i)) & 3u;
+            d2 += l == 0 ? t0[i] : (l == 1 ? t1[i] : t2[i]);
         }
-        if (d2 < best) { best = d2; bj = j; be = e; }
+        if (d2 < best) { best = d2; bl = e; }
+        e = en;
     }
-    // (distance, list position) argmin across the warp
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oj = __shfl_xor_sync(0xffffffffu, bj, o);
-        const uint32_t oe = __shfl_xor_sync(0xffffffffu, be, o);
-        if (ob < best || (ob == best && oj < bj)) { best = ob; bj = oj; be = oe; }
-    }
-    return bj == 0x7fffffff ? -1 : (int) (be >> 16);
+    return bl == 0xFFFFFFFFu ? -1 : (int) (bl >> 16);
 }
 
 template <int T, int SRC>
-__global__ void __launch_bounds__(128) k_iq1(const uint8_t * __restrict__ src, const float * __restrict__ qw,
-                                            int64_t qw_mod, int64_t qw_div, int64_t qw_mat, uint8_t * __restrict__ out,
-                                            int64_t nblocks, SearchTab tab, unsigned * status) {
-    constexpr int SB = IQ1<T>::SB, NSUB = QK / SB;
+__global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __restrict__ src, const float * __restrict__ qw,
+                                                            int64_t qw_mod, int64_t qw_div, int64_t qw_mat,
+                                                            uint8_t * __restrict__ out, int64_t nblocks, SearchTab tab,
+                                                            unsigned * status) {
+    using W = IQ1Warp<T>;
+    constexpr int SB = W::SB, NSUB = W::NSUB, NSB = W::NSB;
+    constexpr int BB = block_bytes(T);
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    IQ1State<T> & st = reinterpret_cast<IQ1State<T> *>(smem_raw)[wid];
-    const int64_t b = (int64_t) blockIdx.x * (blockDim.x >> 5) + wid;
-    if (b >= nblocks) return;
-    float xr[8], qr[8];
-    decode8<SRC>(src, b * QK + lane * 8, xr);
-    load8_f32(qw + ((b / qw_mat) * qw_mod + (b % qw_mod) / qw_div) * QK + lane * 8, qr);
+    W & st = reinterpret_cast<W *>(smem_raw)[wid];
+    const int64_t b0 = ((int64_t) blockIdx.x * (blockDim.x >> 5) + wid) * NSB;
+    if (b0 >= nblocks) return;
+    const int nb = (int) (nblocks - b0 < NSB ? nblocks - b0 : NSB);
+    // ---- loads: 8 consecutive weights a lane a pass, scattered into the lane-minor layout
+    float qr[NSB][8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) st.x[lane * 8 + j] = xr[j];
-    __syncwarp();
-    if (lane == 0) {
-        float s2 = 0;
-        for (int i = 0; i < QK; ++i) s2 += st.x[i] * st.x[i];
-        st.sigma2 = 2 * s2 / QK;
+    for (int k = 0; k < NSB; ++k) {
+        const int e = lane * 8;                        // element of super-block k
+        float v[8];
+        if (k < nb) {
+            const int64_t b = b0 + k;
+            decode8<SRC>(src, b * QK + e, v);
+            load8_f32(qw + ((b / qw_mat) * qw_mod + (b % qw_mod) / qw_div) * QK + e, qr[k]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) { v[j] = 0.f; qr[k][j] = 0.f; }
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) st.x[(e + j) % SB][k * NSUB + (e + j) / SB] = v[j];
     }
     __syncwarp();
-    const float sigma2 = st.sigma2;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) st.w[lane * 8 + j] = qr[j] * sqrtf(sigma2 + xr[j] * xr[j]);
+    // ---- sumx2 in index order, one lane a super-block
+    if (lane < NSB) {
+        float s2 = 0;
+        for (int e = 0; e < QK; ++e) { const float v = st.x[e % SB][lane * NSUB + e / SB]; s2 += v * v; }
+        st.sigma2[lane] = 2 * s2 / QK;
+    }
     __syncwarp();
-    float max_scale = 0;   // (lane 0's copy is the one used)
-    for (int ib = 0; ib < NSUB; ++ib) {
-        const float * xb = st.x + SB * ib;
-        const float * wb = st.w + SB * ib;
-        float mx = 0;
-        if (lane == 0) {
-            mx = fabsf(xb[0]);
-            for (int i = 1; i < SB; ++i) mx = fmaxr(mx, fabsf(xb[i]));
+#pragma unroll
+    for (int k = 0; k < NSB; ++k) {
+        const int e = lane * 8;
+        const float sg = st.sigma2[k];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float xv = st.x[(e + j) % SB][k * NSUB + (e + j) / SB];
+            st.w[(e + j) % SB][k * NSUB + (e + j) / SB] = qr[k][j] * sqrtf(sg + xv * xv);
         }
-        mx = __shfl_sync(0xffffffffu, mx, 0);
-        const int8_t skip_shift = T == IQ1_S ? 1 : 0;
-        if (mx < IQ1<T>::EPS) {
-            if (lane == 0) { st.scales[ib] = 0; st.shifts[ib] = skip_shift; st.gidx[ib][0] = 0xFFFF; }
-            __syncwarp();
-            continue;
-        }
-        // stable ascending order: lane i's weight goes to position rank_i
-        if (lane < SB) {
-            const float k = xb[lane];
-            int r = 0;
-            for (int j = 0; j < SB; ++j) { const float v = xb[j]; r += (v < k) || (v == k && j < lane); }
-            st.idx[r] = lane;
-        }
-        __syncwarp();
-        if (lane == 0) {
-            if constexpr (T == IQ1_S) {
-                st.px[0][0] = st.pw[0][0] = 0;
-                for (int j = 0; j < SB; ++j) {
-                    const int i = st.idx[j];
-                    st.px[0][j + 1] = st.px[0][j] + wb[i] * xb[i];
-                    st.pw[0][j + 1] = st.pw[0][j] + wb[i];
-                }
-            } else {
-                st.px[0][0] = st.px[1][0] = st.pw[0][0] = st.pw[1][0] = 0;
-                for (int j = 0; j < SB; ++j) {
-                    const int i = st.idx[j], h = i < SB / 2 ? 0 : 1;
-                    st.px[h][j + 1] = st.px[h][j] + wb[i] * xb[i];
-                    st.px[1 - h][j + 1] = st.px[1 - h][j];
-                    st.pw[h][j + 1] = st.pw[h][j] + wb[i];
-                    st.pw[1 - h][j + 1] = st.pw[1 - h][j];
-                }
+    }
+    __syncwarp();
+    // ---- one lane a sub-block: guard, stable sort, prefix sums, the split scan, the codebook snap, the refit
+    const int kb = lane / NSUB;                        // super-block of this lane's sub-block
+    const bool live = kb < nb;
+    float scale = 0.f;
+    int shift = T == IQ1_S ? 1 : 0;
+    bool dropped = true;
+    if (live) {
+        float mx = fabsf(st.x[0][lane]);
+        for (int i = 1; i < SB; ++i) mx = fmaxr(mx, fabsf(st.x[i][lane]));
+        if (!(mx < IQ1<T>::EPS)) {
+            // insertion sort of the indices by weight (glibc's stable qsort order: ties keep index order)
+            st.idx[0][lane] = 0;
+            for (int i = 1; i < SB; ++i) {
+                const float k = st.x[i][lane];
+                int j = i - 1;
+                while (j >= 0 && st.x[st.idx[j][lane]][lane] > k) { st.idx[j + 1][lane] = st.idx[j][lane]; --j; }
+                st.idx[j + 1][lane] = (uint8_t) i;
             }
-        }
-        __syncwarp();
-        int b1, b2, bk;
-        float scale;
-        split_search<T>(st, lane, b1, b2, bk, scale, mx);
-        if (b1 < 0) {   // (nothing accepted: the sub-block is dropped, as ggml does)
-            if (lane == 0) { st.scales[ib] = 0; st.shifts[ib] = skip_shift; st.gidx[ib][0] = 0xFFFF; }
-            __syncwarp();
-            continue;
-        }
-        if (lane < SB) st.L[st.idx[lane]] = (int8_t) (lane < b1 ? 0 : lane < b2 ? 1 : 2);
-        __syncwarp();
-        if (scale < 0) {
-            if (lane < SB) st.L[lane] = (int8_t) (2 - st.L[lane]);
-            scale = -scale;
-            bk = T == IQ1_S ? 1 - bk : 3 - bk;   // IQ1_S: 0 = +shift, 1 = -shift
-        }
-        __syncwarp();
-        // codebook snap, one group of 8 at a time, warp-wide neighbour search when off the grid
-        bool all_on = true;
-        int gi_g[SB / 8];
-#pragma unroll
-        for (int g = 0; g < SB / 8; ++g) {
-            int c3 = 0, p3 = 1;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) { c3 += st.L[8 * g + i] * p3; p3 *= 3; }
-            const int m = __ldg(tab.code3 + c3);
-            const bool minus = T == IQ1_S ? bk == 1 : (g == 0 ? bk >= 2 : (bk % 2) != 0);
-            if (m >= 0) { gi_g[g] = m; continue; }
-            all_on = false;
-            const int gi = iq1_nearest(tab, c3, xb + 8 * g, wb + 8 * g, scale, minus, lane);
-            if (gi < 0) { if (lane == 0) atomicOr(status, ST_NO_NEIGHBOUR); gi_g[g] = 0; }
-            else gi_g[g] = gi;
-        }
-        if (lane == 0) {
-            if (!all_on) {
-                float sqx = 0, sq2 = 0;
-                for (int g = 0; g < SB / 8; ++g) {
-                    const bool minus = T == IQ1_S ? bk == 1 : (g == 0 ? bk >= 2 : (bk % 2) != 0);
-                    const uint32_t lev = __ldg(tab.glev + gi_g[g]);
-                    for (int j = 0; j < 8; ++j) {
-                        const float ww = wb[8 * g + j], q = lvl((lev >> (2 * j)) & 3u, minus);
-                        sqx += ww * q * xb[8 * g + j];
-                        sq2 += ww * q * q;
+            float best = -FLT_MAX;
+            int b1 = -1, b2 = -1, bk = -1;
+            scale = mx;
+            if constexpr (T == IQ1_S) {
+                st.px[0][0][lane] = 0.f;
+                st.pw[0][0][lane] = 0.f;
+                float sx = 0.f, sw = 0.f;
+                for (int j = 0; j < SB; ++j) {
+                    const int i = st.idx[j][lane];
+                    const float wi = st.w[i][lane];
+                    sx = sx + wi * st.x[i][lane];
+                    sw = sw + wi;
+                    st.px[0][j + 1][lane] = sx;
+                    st.pw[0][j + 1][lane] = sw;
+                }
+                const float tx = sx, tw = sw;
+                const float ap = lvl(0, false), bp = lvl(1, false), cp = lvl(2, false);
+                const float am = lvl(0, true), bm = lvl(1, true), cm = lvl(2, true);
+                for (int i1 = 0; i1 <= SB; ++i1) {
+                    const float x1 = st.px[0][i1][lane] - 0.f, w1 = st.pw[0][i1][lane] - 0.f;   // (sumx[i1] - sumx[0])
+                    const float sx1 = st.px[0][i1][lane], sw1 = st.pw[0][i1][lane];
+                    for (int i2 = i1; i2 <= SB; ++i2) {
+                        const float sx2 = st.px[0][i2][lane], sw2 = st.pw[0][i2][lane];
+                        const float dx = sx2 - sx1, dw = sw2 - sw1, ex = tx - sx2, ew = tw - sw2;
+                        float qx = x1 * ap + dx * bp + ex * cp;
+                        float q2 = w1 * ap * ap + dw * bp * bp + ew * cp * cp;
+                        if (q2 > 0 && qx * qx > best * q2) { scale = qx / q2; best = scale * qx; b1 = i1; b2 = i2; bk = 0; }
+                        qx = x1 * am + dx * bm + ex * cm;
+                        q2 = w1 * am * am + dw * bm * bm + ew * cm * cm;
+                        if (q2 > 0 && qx * qx > best * q2) { scale = qx / q2; best = scale * qx; b1 = i1; b2 = i2; bk = 1; }
                     }
                 }
-                if (sqx > 0 && sq2 > 0) scale = sqx / sq2;
-            }
-            for (int g = 0; g < SB / 8; ++g) st.gidx[ib][g] = (uint16_t) gi_g[g];
-            st.scales[ib] = scale;
-            st.shifts[ib] = (int8_t) (T == IQ1_S ? (bk == 1 ? -1 : 1) : bk);
-            max_scale = fmaxr(max_scale, scale);
-        }
-        __syncwarp();
-    }
-    // ---- block bytes (lane 0)
-    if (lane == 0) {
-        uint8_t * y = st.out;
-        for (int i = 0; i < block_bytes(T); ++i) y[i] = 0;
-        if constexpr (T == IQ1_S) {
-            uint16_t qh[8];
-            for (int ib = 0; ib < 8; ++ib) {
-                qh[ib] = 0;
-                if (st.gidx[ib][0] == 0xFFFF && st.scales[ib] == 0) continue;
-                for (int k = 0; k < 4; ++k) {
-                    y[2 + 4 * ib + k] = (uint8_t) (st.gidx[ib][k] & 255);
-                    qh[ib] |= (uint16_t) ((st.gidx[ib][k] >> 8) << (3 * k));
+            } else {
+                for (int h = 0; h < 2; ++h) { st.px[h][0][lane] = 0.f; st.pw[h][0][lane] = 0.f; }
+                float ax[2] = {0.f, 0.f}, aw[2] = {0.f, 0.f};
+                for (int j = 0; j < SB; ++j) {   // prefix sums split by half of the sub-block (gpuq.hip:559-571)
+                    const int i = st.idx[j][lane], h = i < SB / 2 ? 0 : 1;
+                    const float wi = st.w[i][lane];
+                    ax[h] = ax[h] + wi * st.x[i][lane];
+                    aw[h] = aw[h] + wi;
+                    st.px[0][j + 1][lane] = ax[0]; st.px[1][j + 1][lane] = ax[1];
+                    st.pw[0][j + 1][lane] = aw[0]; st.pw[1][j + 1][lane] = aw[1];
+                }
+                const float p2 = 1 + DELTA, m2 = 1 - DELTA;
+                const float cp1 = (-1 + DELTA) * (-1 + DELTA) - DELTA * DELTA, cp2 = DELTA * DELTA - (1 + DELTA) * (1 + DELTA);
+                const float cm1 = (-1 - DELTA) * (-1 - DELTA) - (-DELTA) * (-DELTA), cm2 = (-DELTA) * (-DELTA) - (1 - DELTA) * (1 - DELTA);
+                const float tx0 = ax[0], tx1 = ax[1], tw0 = aw[0], tw1 = aw[1];
+                const float txp0 = tx0 * p2, txp1 = tx1 * p2, txm0 = tx0 * m2, txm1 = tx1 * m2;
+                const float twp0 = tw0 * p2 * p2, twp1 = tw1 * p2 * p2, twm0 = tw0 * m2 * m2, twm1 = tw1 * m2 * m2;
+                for (int i1 = 0; i1 <= SB; ++i1) {
+                    const float a0 = st.px[0][i1][lane], a1 = st.px[1][i1][lane];
+                    const float c0 = st.pw[0][i1][lane], c1 = st.pw[1][i1][lane];
+                    const float c0p = c0 * cp1, c1p = c1 * cp1, c0m = c0 * cm1, c1m = c1 * cm1;
+                    for (int i2 = i1; i2 <= SB; ++i2) {
+                        const float sx0 = a0 + st.px[0][i2][lane], sx1 = a1 + st.px[1][i2][lane];
+                        const float e0 = st.pw[0][i2][lane], e1 = st.pw[1][i2][lane];
+                        const float qxp0 = txp0 - sx0, qxm0 = txm0 - sx0, qxp1 = txp1 - sx1, qxm1 = txm1 - sx1;
+                        const float q2p0 = twp0 + c0p + e0 * cp2, q2m0 = twm0 + c0m + e0 * cm2;
+                        const float q2p1 = twp1 + c1p + e1 * cp2, q2m1 = twm1 + c1m + e1 * cm2;
+                        const float sqx[4] = {qxp0 + qxp1, qxp0 + qxm1, qxm0 + qxp1, qxm0 + qxm1};
+                        const float sq2[4] = {q2p0 + q2p1, q2p0 + q2m1, q2m0 + q2p1, q2m0 + q2m1};
+#pragma unroll
+                        for (int c = 0; c < 4; ++c)
+                            if (sq2[c] > 0 && sqx[c] * sqx[c] > best * sq2[c]) {
+                                scale = sqx[c] / sq2[c]; best = scale * sqx[c]; b1 = i1; b2 = i2; bk = c;
+                            }
+                    }
                 }
             }
+            if (b1 >= 0) {
+                dropped = false;
+                for (int j = 0; j < SB; ++j) st.L[st.idx[j][lane]][lane] = (int8_t) (j < b1 ? 0 : j < b2 ? 1 : 2);
+                if (scale < 0) {
+                    for (int j = 0; j < SB; ++j) st.L[j][lane] = (int8_t) (2 - st.L[j][lane]);
+                    scale = -scale;
+                    bk = T == IQ1_S ? 1 - bk : 3 - bk;
+                }
+                // the codebook snap, group by group
+                bool all_on = true;
+                for (int g = 0; g < SB / 8; ++g) {
+                    int c3 = 0, p3 = 1;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) { c3 += st.L[8 * g + i][lane] * p3; p3 *= 3; }
+                    const int m = __ldg(tab.code3 + c3);
+                    const bool minus = T == IQ1_S ? bk == 1 : (g == 0 ? bk >= 2 : (bk % 2) != 0);
+                    int gi = m;
+                    if (m < 0) {
+                        all_on = false;
+                        gi = snap_group<T>(st, lane, g, m, scale, minus, tab);
+                        if (gi < 0) { atomicOr(status, ST_NO_NEIGHBOUR); gi = 0; }
+                    }
+                    st.gidx[g][lane] = (uint16_t) gi;
+                }
+                if (!all_on) {
+                    float sqx = 0, sq2 = 0;
+                    for (int g = 0; g < SB / 8; ++g) {
+                        const bool minus = T == IQ1_S ? bk == 1 : (g == 0 ? bk >= 2 : (bk % 2) != 0);
+                        const uint32_t lev = __ldg(tab.glev + st.gidx[g][lane]);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const float ww = st.w[8 * g + j][lane], q = lvl((lev >> (2 * j)) & 3u, minus);
+                            sqx += ww * q * st.x[8 * g + j][lane];
+                            sq2 += ww * q * q;
+                        }
+                    }
+                    if (sqx > 0 && sq2 > 0) scale = sqx / sq2;
+                }
+                shift = T == IQ1_S ? (bk == 1 ? -1 : 1) : bk;
+            } else {
+                scale = 0.f;
+            }
+        }
+    }
+    st.scales[lane] = dropped ? 0.f : scale;
+    st.shifts[lane] = (int8_t) shift;
+    st.dropped[lane] = (uint8_t) dropped;
+    __syncwarp();
+    // ---- the block bytes: each lane writes its sub-block's fields, one lane a super-block the scales
+    if (live) {
+        uint8_t * y = st.out[kb];
+        const int ib = lane % NSUB;
+        if constexpr (T == IQ1_S) {
+            uint16_t h = 0;
+            for (int k = 0; k < 4; ++k) {
+                const int gi = st.dropped[lane] ? 0 : st.gidx[k][lane];
+                y[2 + 4 * ib + k] = (uint8_t) (gi & 255);
+                h |= (uint16_t) ((gi >> 8) << (3 * k));
+            }
+            y[34 + 2 * ib] = (uint8_t) (h & 255);
+            y[35 + 2 * ib] = (uint8_t) (h >> 8);
+        } else {
+            const int g0 = st.dropped[lane] ? 0 : st.gidx[0][lane], g1 = st.dropped[lane] ? 0 : st.gidx[1][lane];
+            y[2 * ib] = (uint8_t) (g0 & 255);
+            y[2 * ib + 1] = (uint8_t) (g1 & 255);
+            y[32 + ib] = (uint8_t) ((g0 >> 8) | ((g1 >> 8) << 4));
+        }
+    }
+    __syncwarp();
+    if (lane < nb) {
+        uint8_t * y = st.out[lane];
+        const float * scl = st.scales + lane * NSUB;
+        float max_scale = 0;
+        for (int ib = 0; ib < NSUB; ++ib) if (!st.dropped[lane * NSUB + ib]) max_scale = fmaxr(max_scale, scl[ib]);
+        if constexpr (T == IQ1_S) {
+            y[0] = y[1] = 0;
             if (max_scale) {
                 const float d = max_scale / 15;
-                const uint16_t h = half_bits(d * 1.125f);
-                y[0] = h & 255; y[1] = h >> 8;
+                const uint16_t hd = half_bits(d * 1.125f);
+                y[0] = hd & 255; y[1] = hd >> 8;
                 const float id = 1 / d;
                 for (int ib = 0; ib < 8; ++ib) {
-                    int l = imax(0, imin(7, nearest_int(0.5f * (id * st.scales[ib] - 1))));
-                    if (st.shifts[ib] == -1) l |= 8;
-                    qh[ib] |= (uint16_t) (l << 12);
+                    int l = imax(0, imin(7, nearest_int(0.5f * (id * scl[ib] - 1))));
+                    if (st.shifts[lane * NSUB + ib] == -1) l |= 8;
+                    y[35 + 2 * ib] |= (uint8_t) ((l << 12) >> 8);
                 }
             }
-            for (int ib = 0; ib < 8; ++ib) { y[34 + 2 * ib] = qh[ib] & 255; y[35 + 2 * ib] = qh[ib] >> 8; }
         } else {
-            uint8_t * qs = y, * qh = y + 32;
-            for (int ib = 0; ib < 16; ++ib) {
-                if (st.gidx[ib][0] == 0xFFFF && st.scales[ib] == 0) continue;
-                qs[2 * ib] = (uint8_t) (st.gidx[ib][0] & 255);
-                qs[2 * ib + 1] = (uint8_t) (st.gidx[ib][1] & 255);
-                qh[ib] = (uint8_t) ((st.gidx[ib][0] >> 8) | ((st.gidx[ib][1] >> 8) << 4));
-            }
+            for (int i = 48; i < 56; ++i) y[i] = 0;
             if (max_scale) {
                 const uint8_t masks[4] = {0x00, 0x80, 0x08, 0x88};
                 uint16_t sc[4] = {0, 0, 0, 0};
@@ -375,18 +312,17 @@ __global__ void __launch_bounds__(128) k_iq1(const uint8_t * __restrict__ src, c
                 const float id = 1 / d;
                 float sqx = 0, sq2 = 0;
                 for (int ib = 0; ib < 16; ++ib) {
-                    const int l = imax(0, imin(7, nearest_int(0.5f * (id * st.scales[ib] - 1))));
+                    const int sl = lane * NSUB + ib;
+                    const int l = imax(0, imin(7, nearest_int(0.5f * (id * scl[ib] - 1))));
                     sc[ib / 4] |= (uint16_t) (l << (3 * (ib % 4)));
-                    qh[ib] |= masks[st.shifts[ib]];
-                    const float * xb = st.x + 16 * ib;
-                    const float * wb = st.w + 16 * ib;
+                    y[32 + ib] |= masks[st.shifts[sl]];
                     for (int k = 0; k < 2; ++k) {
-                        const bool minus = k == 0 ? st.shifts[ib] >= 2 : (st.shifts[ib] % 2) != 0;
-                        const int gi = qs[2 * ib + k] + ((qh[ib] << (8 - 4 * k)) & 0x700);
+                        const bool minus = k == 0 ? st.shifts[sl] >= 2 : (st.shifts[sl] % 2) != 0;
+                        const int gi = y[2 * ib + k] + ((y[32 + ib] << (8 - 4 * k)) & 0x700);
                         const uint32_t lev = __ldg(tab.glev + gi);
                         for (int j = 0; j < 8; ++j) {
-                            const float ww = wb[8 * k + j], q = lvl((lev >> (2 * j)) & 3u, minus) * (2 * l + 1);
-                            sqx += ww * q * xb[8 * k + j];
+                            const float ww = st.w[8 * k + j][sl], q = lvl((lev >> (2 * j)) & 3u, minus) * (2 * l + 1);
+                            sqx += ww * q * st.x[8 * k + j][sl];
                             sq2 += ww * q * q;
                         }
                     }
@@ -402,15 +338,19 @@ __global__ void __launch_bounds__(128) k_iq1(const uint8_t * __restrict__ src, c
         }
     }
     __syncwarp();
-    uint8_t * yo = out + b * block_bytes(T);
-    for (int i = lane; i < block_bytes(T); i += 32) yo[i] = st.out[i];
+    uint8_t * yo = out + b0 * BB;
+    for (int i = lane; i < nb * BB; i += 32) yo[i] = st.out[i / BB][i % BB];
 }
 
 template <int T, int SRC>
 cudaError_t launch_t(const LaunchArgs & a) {
-    constexpr int WARPS = 4;
-    const size_t smem = sizeof(IQ1State<T>) * WARPS;
-    const int64_t grid = (a.nblocks + WARPS - 1) / WARPS;
+    using W = IQ1Warp<T>;
+    constexpr int WARPS = IQ1<T>::WARPS;
+    const size_t smem = sizeof(W) * WARPS;
+    const cudaError_t e = cudaFuncSetAttribute(k_iq1<T, SRC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    if (e != cudaSuccess) return e;
+    const int64_t per_cta = (int64_t) WARPS * W::NSB;
+    const int64_t grid = (a.nblocks + per_cta - 1) / per_cta;
     k_iq1<T, SRC><<<(unsigned) grid, WARPS * 32, smem, a.stream>>>((const uint8_t *) a.src, a.qw, a.qw_mod, a.qw_div,
                                                                    a.qw_mat, (uint8_t *) a.out, a.nblocks, a.tab, a.status);
     return cudaGetLastError();
