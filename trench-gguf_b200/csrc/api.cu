@@ -117,6 +117,7 @@ bool convert_search(const HostRecord & r, HostSearch & h) {
             h.neigh.push_back(((uint32_t) gi << 16) | h.glev[gi]);
         }
     }
+    h.neigh.push_back(0);   // pad word: the searches load the entry after a list's last one ahead of time
     return true;
 }
 
@@ -187,7 +188,7 @@ int upload_tables(Device & d) {
         if (cudaMalloc(&s.code3, h.code3.size() * 4) != cudaSuccess || cudaMalloc(&s.neigh, h.neigh.size() * 4) != cudaSuccess ||
             cudaMalloc(&s.glev, h.glev.size() * 2) != cudaSuccess) return 4;
         cudaMemcpy(s.code3, h.code3.data(), h.code3.size() * 4, cudaMemcpyHostToDevice);
-        cudaMemcpy(s.neigh, h.neigh.data(), h.neigh.size() * 4, cudaMemcpyHostToDevice);
+        cudaMemcpy(s.neigh, h.neigh.data(), h.neigh.size() * 4, cudaMemcpyHostToDevice);   // (includes the pad word)
         cudaMemcpy(s.glev, h.glev.data(), h.glev.size() * 2, cudaMemcpyHostToDevice);
         s.tab = SearchTab{s.code3, s.neigh, s.glev, h.ngrid};
         d.search.push_back(s);

@@ -66,12 +66,13 @@ __device__ int snap_group(const IQ1Warp<T> & st, int lane, int g, int m, float s
     uint32_t bl = 0xFFFFFFFFu;
     uint32_t e = __ldg(lst + 1);
     for (int j = 1; j <= n; ++j) {
-        const uint32_t en = j < n ? __ldg(lst + j + 1) : 0u;
+        const uint32_t en = __ldg(lst + j + 1);   // (the table ends with a pad word: always in bounds)
         float d2 = 0.f;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            const uint32_t l = (e >> (2 * i)) & 3u;
-            d2 += l == 0 ? t0[i] : (l == 1 ? t1[i] : t2[i]);
+            // level 2 has bit 1 set, level 1 bit 0 (level 3 does not occur): two bit tests, two selects
+            const bool hi = e & (2u << (2 * i)), lo = e & (1u << (2 * i));
+            d2 += hi ? t2[i] : (lo ? t1[i] : t0[i]);
         }
         if (d2 < best) { best = d2; bl = e; }
         e = en;

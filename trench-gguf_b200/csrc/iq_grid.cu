@@ -198,12 +198,13 @@ __device__ uint32_t search_lane8(int m, const float * xv, const float * wa, floa
     uint32_t bl = NONE;
     uint32_t e = __ldg(lst + 1);
     for (int j = 1; j <= n; ++j) {
-        const uint32_t en = j < n ? __ldg(lst + j + 1) : 0u;   // the next entry, one step ahead
+        const uint32_t en = __ldg(lst + j + 1);   // (the table ends with a pad word: always in bounds)   // the next entry, one step ahead
         float d2 = 0.f;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            const uint32_t l = (e >> (2 * i)) & 3u;
-            d2 += l == 0 ? t0[i] : (l == 1 ? t1[i] : t2[i]);
+            // level 2 has bit 1 set, level 1 bit 0 (level 3 does not occur): two bit tests, two selects
+            const bool hi = e & (2u << (2 * i)), lo = e & (1u << (2 * i));
+            d2 += hi ? t2[i] : (lo ? t1[i] : t0[i]);
         }
         if (d2 < best) { best = d2; bl = e; }
         e = en;
