@@ -65,6 +65,7 @@ __device__ int snap_group(const IQ1Warp<T> & st, int lane, int g, int m, float s
     float best = FLT_MAX;
     uint32_t bl = 0xFFFFFFFFu;
     uint32_t e = __ldg(lst + 1);
+#pragma unroll 2
     for (int j = 1; j <= n; ++j) {
         const uint32_t en = __ldg(lst + j + 1);   // (the table ends with a pad word: always in bounds)
         float d2 = 0.f;

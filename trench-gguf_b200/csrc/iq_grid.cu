@@ -197,6 +197,7 @@ __device__ uint32_t search_lane8(int m, const float * xv, const float * wa, floa
     float best = FLT_MAX;
     uint32_t bl = NONE;
     uint32_t e = __ldg(lst + 1);
+#pragma unroll 2
     for (int j = 1; j <= n; ++j) {
         const uint32_t en = __ldg(lst + j + 1);   // (the table ends with a pad word: always in bounds)   // the next entry, one step ahead
         float d2 = 0.f;
