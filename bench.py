@@ -1,6 +1,6 @@
 """Benchmark of the B200 quantizer: Gweights/s quantized to IQ2_XXS and IQ1_M at 1/8 of a B200 box (one GPU).
 
-Workload (the metric's own configuration): the MoE expert tensor of 384 experts x 2048 x 7168
+Workload (the headline metric's own configuration, "config 2"): the MoE expert tensor of 384 experts x 2048 x 7168
 stored as MXFP4, sharded 48 experts a GPU (1/8 of the box). A step re-quantizes this GPU's 48 experts from their
 MXFP4 bytes to IQ2_XXS and to IQ1_M, each expert with its own imatrix row; the source is decoded inside the
 quantize kernels. Inputs are seeded synthetic data with the config's distributions (workloads.config2); 374 MB of
@@ -48,8 +48,8 @@ def parse():
     return ap.parse_args()
 
 
-def load_ops():
-    p = os.path.join(PKG, "op_counts.json")
+def load_json(name):
+    p = os.path.join(PKG, name)
     return json.load(open(p)) if os.path.exists(p) else {}
 
 
@@ -111,6 +111,8 @@ def cpu_baseline(types, sample_rows, seed=102):
     raw, im = workloads.config2(experts=1, rows=sample_rows, cols=COLS, seed=seed)
     x = chk.decode(39, raw, sample_rows * COLS).reshape(1, sample_rows, COLS)
     threads = os.cpu_count() or 1
+    for name in types:   # (warm-up: thread start, first touch of the tables)
+        chk.quantize(TYPES[name], x[:, :64], im, threads=threads)
     t0 = time.perf_counter()
     for name in types:
         chk.quantize(TYPES[name], x, im, threads=threads)
@@ -125,18 +127,18 @@ def run_reference(args, rank):
     if rank != 0:
         return
     for _ in range(args.warmup):
-        cpu_baseline(types, 64)
+        cpu_baseline(types, 256)
     vals = []
     for _ in range(args.steps):
-        vals.append(cpu_baseline(types, 256))
+        vals.append(cpu_baseline(types, ROWS))   # one whole expert a step
     v = statistics.median([r["value"] for r in vals])
     cb = dict(vals[-1])
     cb["value"] = v
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "Gweights/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * 256 * COLS * len(types) / (v * 1e9),
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * ROWS * COLS * len(types) / (v * 1e9),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (config 2 distributions, seeded)",
-            "config": {"workload": "config 2 sample: 256 rows of one 2048x7168 MXFP4 expert -> " + "+".join(types),
+            "config": {"workload": "config 2 sample: one 2048x7168 MXFP4 expert a step -> " + "+".join(types),
                        "threads": cb["cores"]},
             "cpu_baseline": cb, "e2e": {"value": v, "unit": "Gweights/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -169,6 +171,7 @@ def main():
     raw = torch.from_numpy(raw_np.reshape(-1)).to(dev)
     im = torch.from_numpy(im_np).to(dev)
     outs = {t: torch.empty(nw // 256 * g.block_bytes(TYPES[t]), dtype=torch.uint8, device=dev) for t in types}
+    block_b = {t: g.block_bytes(TYPES[t]) for t in types}
     stream = torch.cuda.Stream(device=dev)
     sh = stream.cuda_stream
 
@@ -251,7 +254,8 @@ def main():
         if dist:
             dist.destroy_process_group()
         return
-    ops = load_ops()
+    ops = load_json("op_counts.json")
+    traffic = load_json("dram_traffic.json")
     top = max(types, key=lambda t: per_type_ms[t])
     roof = None
     try:
@@ -262,11 +266,14 @@ def main():
     opw = ops.get(top.upper(), {}).get("ops_per_weight")
     if opw and peak:
         ach = opw * E * ROWS * COLS / (per_type_ms[top] / 1e3) / 1e12
+        tb = traffic.get(top.upper(), {}).get("dram_bytes_per_weight")
         roof = {"bound": "fp32", "kernel": top, "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
-                "peak_source": peak_src, "ops_per_weight": opw, "traffic": None}
+                "peak_source": peak_src, "ops_per_weight": opw,
+                "traffic": tb * E * ROWS * COLS if tb else None, "traffic_unit": "bytes a launch (ncu DRAM read+write, "
+                "scaled from a 4-expert capture)", "algorithmic_bytes": E * ROWS * COLS * (17 / 32 + block_b[top] / 256)}
     cb = None
     if not args.no_cpu and world == 1:
-        cb = cpu_baseline(types, 512)
+        cb = cpu_baseline(types, 2 * ROWS)   # two experts: seconds of work on all host cores
     line = {"metric": METRIC, "value": value, "unit": "Gweights/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (config 2 distributions, seeded per rank)",

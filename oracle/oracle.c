@@ -9,7 +9,7 @@
  *
  * Parity pin: the tests compare this restatement with (a) the reference's own block functions compiled on the
  * host from the reference sources (oracle/_ref, built by oracle/Makefile), block for block, on the reference
- * self-test's input recipe and the BASELINE configs' distributions; (b) gguf-py's ggml-exact Q8_0 quantizer and its
+ * self-test's input recipe and the benchmark configurations' distributions; (b) gguf-py's ggml-exact Q8_0 quantizer and its
  * dequantizers of every type; (c) the golden fixtures in tests/golden/ written from (a).
  *
  * Citations: "gpuq.hip:N" is trench-gguf gpuq/gpuq.hip line N.
