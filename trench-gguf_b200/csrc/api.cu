@@ -108,8 +108,11 @@ bool convert_search(const HostRecord & r, HostSearch & h) {
         if (off >= r.neigh.size() || off + 1 + r.neigh[off] > r.neigh.size() || r.neigh[off] == 0) {
             set_err("gpuq_init: type %d: neighbour list out of range", r.type); return false;
         }
-        h.code3[c] = -(int32_t) (h.neigh.size() + 1);
         const int n = r.neigh[off];
+        if (n >= (1 << LIST_CNT_BITS) || h.neigh.size() >= ((size_t) 1 << (30 - LIST_CNT_BITS))) {
+            set_err("gpuq_init: type %d: neighbour list too long for the device layout", r.type); return false;
+        }
+        h.code3[c] = -(int32_t) (((h.neigh.size() << LIST_CNT_BITS) | (size_t) n) + 1);
         h.neigh.push_back((uint32_t) n);
         for (int j = 1; j <= n; ++j) {
             const int gi = r.neigh[off + j];

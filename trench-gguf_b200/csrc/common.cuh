@@ -40,9 +40,10 @@ enum Status : unsigned { ST_OK = 0, ST_NO_NEIGHBOUR = 1u, ST_OFF_GRID = 2u, ST_B
 // ---------------------------------------------------------------------------------------------- search tables
 // Device layout of one codebook (built on the host from a gpuq_tables.bin record):
 //   code3[c]  for every reachable level code c (base-3 digits for the 8-d grids, base-8 for the 4-d IQ3 grids):
-//             >= 0: the grid index of the point with those levels; < 0: -(offset+1) into `neigh`
+//             >= 0: the grid index of the point with those levels; < 0: -(1 + (offset << 9 | count)) of the
+//             code's neighbour list in `neigh` (list_off / list_cnt)
 //   neigh     list = [count, entries...], entry = grid index << 16 | the point's packed levels
-//             (2 bits a dimension for 8-d grids, 3 bits for 4-d)
+//             (2 bits a dimension for 8-d grids, 3 bits for 4-d); one pad word after the last list
 //   glev[g]   packed levels of grid point g (same packing)
 struct SearchTab {
     const int32_t * code3;
@@ -50,6 +51,9 @@ struct SearchTab {
     const uint16_t * glev;
     int ngrid;
 };
+constexpr int LIST_CNT_BITS = 9;   // list lengths < 512 (the longest ggml list has 292 points)
+__device__ __forceinline__ int list_off(int m) { return (-m - 1) >> LIST_CNT_BITS; }
+__device__ __forceinline__ int list_cnt(int m) { return (-m - 1) & ((1 << LIST_CNT_BITS) - 1); }
 struct DequantTab { const uint64_t * grid; };   // ggml-common.h iq*_grid, 4-byte points zero-extended
 
 // ---------------------------------------------------------------------------------------------- scalar helpers

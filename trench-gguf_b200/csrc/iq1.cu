@@ -60,7 +60,7 @@ __device__ int snap_group(const IQ1Warp<T> & st, int lane, int g, int m, float s
         const float d0 = s * q0 - xi, d1 = s * q1 - xi, d2 = s * q2 - xi;
         t0[i] = wi * d0 * d0; t1[i] = wi * d1 * d1; t2[i] = wi * d2 * d2;
     }
-    const uint32_t * lst = tab.neigh + (-m - 1);
+    const uint32_t * lst = tab.neigh + list_off(m);
     const int n = (int) __ldg(lst);
     float best = FLT_MAX;
     uint32_t bl = 0xFFFFFFFFu;

@@ -12,13 +12,16 @@
 //   * the (sub-block, trial) pairs of make_qp_quants' trial scales (IQ2_XXS) and of the trial search (104..304 a
 //     super-block), each lane running its trial's groups and index-ordered sums exactly as ggml does,
 //   * the (sub-block, group) pairs of the re-gridding.
-// The neighbour searches dominate (8k..22k candidate points a super-block). Each lane searches its own group's
-// list: the 24 possible per-dimension terms w_i (s q - x_i)^2 (q in {1, 3, 5}) are formed once, so a candidate's
-// distance is 8 selects and ggml's 8 additions in ggml's order, with the next list entry loaded one step ahead.
+// The neighbour searches dominate (3k..22k candidate points a super-block). For the 8-d grids the 32 lanes' searches
+// of one group step run warp-balanced (search.cuh): the lists laid end to end, equal shares a lane, the per-dimension
+// terms w_i (s q - x_i)^2 (q in {1, 3, 5}) formed once a search and read from shared memory, ggml's 8 additions in
+// ggml's order. The 4-d grids' short lists run one a lane with the distance formed in place.
 // ggml's sequential decisions (which trial wins: a strict `>` scan in trial order) are replayed in trial order by
 // one lane per sub-block from the stored per-trial sums, so the choice is bit-identical. Sums that ggml runs in
 // index order (sumx2 over 256, the 16/32-weight sums) run in index order inside one lane.
+#include <type_traits>
 #include "common.cuh"
+#include "search.cuh"
 #include "source.cuh"
 #include "kernels.h"
 
@@ -63,15 +66,32 @@ template <int T> struct Shape {
     static constexpr int NSG = P::SB / 8;             // 8-weight sign bytes a sub-block
     static constexpr int NROUND = (NTASK + 31) / 32;  // rounds of 32 trials
     static constexpr int NRG = NSUB * NG;             // re-grid searches a super-block
+    // trial rounds scheduled together (their searches sorted by list length): at most 640 searches a batch
+    static constexpr int RB = NROUND < 640 / (32 * NG) ? NROUND : (640 / (32 * NG) > 0 ? 640 / (32 * NG) : 1);
+    static constexpr int NBKT = 128;                  // list-length buckets of the schedule
 };
+
+// list-length bucket: exact below 64, then 8 lengths a bucket
+__device__ __forceinline__ int len_bucket(int n) { return n < 64 ? n : imin(127, 64 + ((n - 64) >> 3)); }
 
 // per-warp shared state of one super-block
 template <int T> struct alignas(16) WarpState {
     using S = Shape<T>;
-    float x2[QK];                                     // x*x, for sumx2
+    struct QP { float mse[S::NSUB][9]; uint8_t L[S::NSUB][32]; };   // make_qp_quants' trials and levels (IQ2_XXS)
+    struct Sched {                                    // one batch of trial rounds
+        float ts[S::RB * 32];                         // a task's trial scale
+        uint16_t perm[S::RB * 32 * S::NG];            // the batch's searches, longest list first
+        uint8_t bkt[S::RB * 32 * S::NG];              // a (task, group)'s list-length bucket, 0xFF: on the grid
+        int hist[S::NBKT];                            // bucket counts, then cursors
+    };
+    union {                                           // (phase-disjoint uses of one buffer)
+        float x2[QK];                                 // x*x, for sumx2
+        QP qp;
+        Sched sch;
+        std::conditional_t<GT<T>::GD == 8, Search8Scratch, char> sc;   // the balanced searches of the 8-d grids
+    } u;
     float w[S::NSUB * S::PAD], wa[S::NSUB * S::PAD], xv[S::NSUB * S::PAD], wx[S::NSUB * S::PAD];
-    float qmse[S::NSUB][9];                           // make_qp_quants' trial errors (IQ2_XXS)
-    uint8_t qL[S::NSUB][32];                          // make_qp_quants' levels (IQ2_XXS)
+    float qmax[S::NSUB];                              // make_qp_quants' max (from 0)
     float t_sqx[S::NTASK], t_sq2[S::NTASK];
     uint16_t t_lev[S::NTASK][S::NG];
     uint8_t t_on[S::NTASK];
@@ -88,25 +108,18 @@ __device__ __forceinline__ int eidx(int sb, int pad, int e) { return (e / sb) * 
 
 // make_qp_quants (gpuq.hip:114-176), split in two. Trial k's weighted error over one sub-block: k = 0 the
 // initial inverse scale nmax/max (levels stored unclamped, as ggml), k = 1..8 the trial scales is = -4..-1, 1..4.
+// (one code path for all k, so the trial lanes do not diverge: k = 0 keeps ggml's uint8_t levels, the others
+// its MIN(nmax, l))
 template <int N>
 __device__ float qp_trial_mse(int k, int nmax, float mx, const float * x, const float * w) {
-    float mse = 0;
-    if (k == 0) {
-        const float iscale = nmax / mx;
-        const float scale = 1 / iscale;
-        for (int i = 0; i < N; ++i) {
-            const uint8_t L = (uint8_t) nearest_int(iscale * x[i]);
-            const float d = x[i] - scale * L;
-            mse += w[i] * d * d;
-        }
-        return mse;
-    }
     const int is = k <= 4 ? k - 5 : k - 4;
-    const float iscale_is = (0.1f * is + nmax) / mx;
-    const float scale_is = 1 / iscale_is;
+    const float iscale = (k == 0 ? (float) nmax : 0.1f * is + nmax) / mx;
+    const float scale = 1 / iscale;
+    float mse = 0;
     for (int i = 0; i < N; ++i) {
-        const int l = imin(nmax, nearest_int(iscale_is * x[i]));
-        const float d = x[i] - scale_is * l;
+        const int r = nearest_int(iscale * x[i]);
+        const int l = k == 0 ? (r & 255) : imin(nmax, r);
+        const float d = x[i] - scale * l;
         mse += w[i] * d * d;
     }
     return mse;
@@ -163,8 +176,6 @@ __device__ __forceinline__ int code3_of(uint32_t lev) {
     return c;
 }
 
-constexpr uint32_t NONE = 0xFFFFFFFFu;
-
 // ggml's rounding of one group at inverse scale id: l = clamp(nearest_int(0.5*(id*x - 1)), 0, kmaxq-1); returns
 // the packed levels and the grid-table entry of the code (>= 0 grid index, < 0 the neighbour list)
 template <int GD, int KMAXQ>
@@ -183,30 +194,21 @@ __device__ __forceinline__ uint32_t round_group(const float * xv, float id, cons
     return lev;
 }
 
-// the 8-d grids: one lane's own search (iq2_find_best_neighbour, gpuq.hip:178-197): d2 = 0; d2 += w_i (s q_i -
-// x_i)^2 for i in order, the first strict minimum in list order wins; NaN and values >= FLT_MAX never win
-__device__ uint32_t search_lane8(int m, const float * xv, const float * wa, float s, const SearchTab & tab) {
+// the 8-d grids: one lane's own search (iq2_find_best_neighbour, gpuq.hip:178-197): the 24 per-dimension terms
+// formed once, then per candidate 8 selects and ggml's 8 additions; the next entry loaded one step ahead
+__device__ __forceinline__ uint32_t search_lane8(int m, const float * xv, const float * wa, float s, const SearchTab & tab) {
     float t0[8], t1[8], t2[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const float d0 = s * 1.f - xv[i], d1 = s * 3.f - xv[i], d2 = s * 5.f - xv[i];
-        t0[i] = wa[i] * d0 * d0; t1[i] = wa[i] * d1 * d1; t2[i] = wa[i] * d2 * d2;
-    }
-    const uint32_t * lst = tab.neigh + (-m - 1);
-    const int n = (int) __ldg(lst);
+    for (int i = 0; i < 8; ++i) level_terms(wa[i], xv[i], s, 1.f, 3.f, 5.f, t0[i], t1[i], t2[i]);
+    const uint32_t * lst = tab.neigh + list_off(m) + 1;
+    const int n = list_cnt(m);
     float best = FLT_MAX;
     uint32_t bl = NONE;
-    uint32_t e = __ldg(lst + 1);
+    uint32_t e = __ldg(lst);
 #pragma unroll 2
-    for (int j = 1; j <= n; ++j) {
-        const uint32_t en = __ldg(lst + j + 1);   // (the table ends with a pad word: always in bounds)   // the next entry, one step ahead
-        float d2 = 0.f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            // level 2 has bit 1 set, level 1 bit 0 (level 3 does not occur): two bit tests, two selects
-            const bool hi = e & (2u << (2 * i)), lo = e & (1u << (2 * i));
-            d2 += hi ? t2[i] : (lo ? t1[i] : t0[i]);
-        }
+    for (int j = 0; j < n; ++j) {
+        const uint32_t en = __ldg(lst + j + 1);   // (one past a list: the next count word or the pad word)
+        const float d2 = cand_dist(e, t0, t1, t2);
         if (d2 < best) { best = d2; bl = e; }
         e = en;
     }
@@ -216,8 +218,8 @@ __device__ uint32_t search_lane8(int m, const float * xv, const float * wa, floa
 // the 4-d grids: one lane's own search (lists of 2..38 points), ggml's distance and first-minimum rule
 // (iq3_find_best_neighbour, gpuq.hip:972-992)
 __device__ uint32_t search_lane4(int m, const float * xv, const float * wa, float s, const SearchTab & tab) {
-    const uint32_t * lst = tab.neigh + (-m - 1);
-    const int n = (int) __ldg(lst);
+    const uint32_t * lst = tab.neigh + list_off(m);
+    const int n = list_cnt(m);
     float best = FLT_MAX;
     uint32_t bl = NONE;
     for (int j = 1; j <= n; ++j) {
@@ -233,7 +235,8 @@ __device__ uint32_t search_lane4(int m, const float * xv, const float * wa, floa
     return bl == NONE ? NONE : (bl & 0xFFFFu);
 }
 
-// A group's levels at inverse scale id / scale s: the rounding when on the grid, else the neighbour search.
+// A group's levels at inverse scale id / scale s: the rounding when on the grid, else the neighbour search
+// (warp-collective for the 8-d grids: every lane calls it).
 template <int T>
 __device__ __forceinline__ uint32_t group_levels(WarpState<T> & st, int lane, bool active, const float * xv,
                                                  const float * wa, float id, float s, const SearchTab & tab, unsigned * on) {
@@ -242,7 +245,16 @@ __device__ __forceinline__ uint32_t group_levels(WarpState<T> & st, int lane, bo
     uint32_t lev = 0;
     if (active) lev = round_group<P::GD, P::KMAXQ>(xv, id, tab, &m);
     *on = active && m >= 0;
-    if (active && m < 0) lev = P::GD == 8 ? search_lane8(m, xv, wa, s, tab) : search_lane4(m, xv, wa, s, tab);
+    if constexpr (P::GD == 8) {
+        float t0[8], t1[8], t2[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) level_terms(wa[i], xv[i], s, 1.f, 3.f, 5.f, t0[i], t1[i], t2[i]);
+        const bool req = active && m < 0;
+        const uint32_t e = search8_warp(st.u.sc, lane, req, req ? list_off(m) : 0, t0, t1, t2, tab);
+        if (req) lev = e == NONE ? NONE : (e & 0xFFFFu);
+    } else {
+        if (active && m < 0) lev = search_lane4(m, xv, wa, s, tab);
+    }
     return lev;
 }
 
@@ -265,7 +277,7 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
     decode8<SRC>(src, b * QK + lane * 8, xr);
     load8_f32(qw + ((b / qw_mat) * qw_mod + (b % qw_mod) / qw_div) * QK + lane * 8, qr);
     {
-        float4 * x2 = reinterpret_cast<float4 *>(st.x2 + lane * 8);
+        float4 * x2 = reinterpret_cast<float4 *>(st.u.x2 + lane * 8);
         x2[0] = make_float4(xr[0] * xr[0], xr[1] * xr[1], xr[2] * xr[2], xr[3] * xr[3]);
         x2[1] = make_float4(xr[4] * xr[4], xr[5] * xr[5], xr[6] * xr[6], xr[7] * xr[7]);
     }
@@ -273,7 +285,7 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
     // ---- P1: sumx2 in index order (one lane; the products were formed by their lanes)
     if (lane == 0) {
         float s2 = 0;
-        const float4 * x2 = reinterpret_cast<const float4 *>(st.x2);
+        const float4 * x2 = reinterpret_cast<const float4 *>(st.u.x2);
         for (int e = 0; e < QK / 4; ++e) { const float4 v = x2[e]; s2 += v.x; s2 += v.y; s2 += v.z; s2 += v.w; }
         st.sigma2 = P::SIGMA_X2 ? 2 * s2 / QK : s2 / QK;
     }
@@ -318,8 +330,9 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
     // ---- P4: sub-block guard and the trial range (IQ2_XXS: make_qp_quants, its 9 trials one a lane)
     if (lane < S::NSUB) {
         const float * xv = st.xv + lane * S::PAD;
-        float mx = xv[0];
-        for (int i = 1; i < P::SB; ++i) mx = fmaxr(mx, xv[i]);
+        float mx = xv[0], qm = fmaxr(0.f, xv[0]);   // (make_qp_quants' own max starts at 0)
+        for (int i = 1; i < P::SB; ++i) { mx = fmaxr(mx, xv[i]); qm = fmaxr(qm, xv[i]); }
+        st.qmax[lane] = qm;
         const int skip = P::EPS_ZERO ? !mx : mx < P::EPS;
         st.skip[lane] = (uint8_t) skip;
         st.denom[lane] = mx;
@@ -331,59 +344,118 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
         for (int task = lane; task < S::NSUB * 9; task += 32) {
             const int s = task / 9, k = task - s * 9;
             if (st.skip[s]) continue;
-            const float * xv = st.xv + s * S::PAD;
-            float qm = 0;   // (make_qp_quants' own max starts at 0)
-            for (int i = 0; i < P::SB; ++i) qm = fmaxr(qm, xv[i]);
-            st.qmse[s][k] = qp_trial_mse<P::SB>(k, NMAX, qm, xv, st.w + s * S::PAD);
+            st.u.qp.mse[s][k] = qp_trial_mse<P::SB>(k, NMAX, st.qmax[s], st.xv + s * S::PAD, st.w + s * S::PAD);
         }
         __syncwarp();
         if (lane < S::NSUB && !st.skip[lane]) {
             const float * xv = st.xv + lane * S::PAD;
-            float qm = 0;
-            for (int i = 0; i < P::SB; ++i) qm = fmaxr(qm, xv[i]);
-            const float scale = qm < 1e-15f ? 0.f : qp_finish<P::SB>(NMAX, qm, xv, st.w + lane * S::PAD, st.qmse[lane], st.qL[lane]);
+            const float qm = st.qmax[lane];
+            const float scale = qm < 1e-15f ? 0.f : qp_finish<P::SB>(NMAX, qm, xv, st.w + lane * S::PAD, st.u.qp.mse[lane], st.u.qp.L[lane]);
             st.scale[lane] = scale;
             st.denom[lane] = scale * P::KMAXQ;
             if (!(scale * P::KMAXQ > 0)) st.skip[lane] = 1;
         }
         __syncwarp();
     }
-    // ---- P5: the trials, one (sub-block, trial) a lane, 32 at a time; groups in order (their sums in index order)
-    for (int r = 0; r < S::NROUND; ++r) {
-        const int task = r * 32 + lane;
-        const int s = task < S::NTASK ? task / S::NT : 0, t = task - s * S::NT;
-        const bool live = task < S::NTASK && !st.skip[s];
-        const float id = live ? ((float) (2 * P::KMAXQ - 1) + (float) (t - P::NTR) * P::STEP) / st.denom[s] : 1.f;
-        const float ts = 1 / id;
-        const float * xv = st.xv + s * S::PAD;
-        const float * wa = st.wa + s * S::PAD;
-        const float * wx = st.wx + s * S::PAD;
-        const float * w = st.w + s * S::PAD;
-        float sqx = 0, sq2 = 0;
-        unsigned onb = 0;
-#pragma unroll 1
-        for (int g = 0; g < S::NG; ++g) {
-            unsigned on;
-            uint32_t lev = group_levels<T>(st, lane, live, xv + g * P::GD, wa + g * P::GD, id, ts, tab, &on);
-            if (!live) continue;
-            if (lev == NONE) { atomicOr(status, ST_NO_NEIGHBOUR); lev = 0; }
-            st.t_lev[task][g] = (uint16_t) lev;
-            onb |= on << g;
+    // ---- P5: the trials, (sub-block, trial) tasks 32 a round, in batches of RB rounds:
+    //   R  every task's groups rounded at the task's inverse scale (levels and on-grid flags kept); the groups
+    //      off the grid counted by the length of their neighbour list;
+    //   S  those searches ordered longest list first (a counting sort over list-length buckets);
+    //   Q  the searches 32 at a time in that order, one a lane, so the lanes of a step run lists of about the same
+    //      length (the order changes nothing in a result: every search is independent and exact);
+    //   M  each task's sums over its groups in index order.
+    for (int rb = 0; rb < S::NROUND; rb += S::RB) {
+        const int nr = S::NROUND - rb < S::RB ? S::NROUND - rb : S::RB;
+        auto & sch = st.u.sch;
+        for (int i = lane; i < S::NBKT; i += 32) sch.hist[i] = 0;
+        __syncwarp();
+        for (int r = 0; r < nr; ++r) {                                          // R
+            const int task = (rb + r) * 32 + lane;
+            const int s = task < S::NTASK ? task / S::NT : 0, t = task - s * S::NT;
+            const bool live = task < S::NTASK && !st.skip[s];
+            const float id = live ? ((float) (2 * P::KMAXQ - 1) + (float) (t - P::NTR) * P::STEP) / st.denom[s] : 1.f;
+            sch.ts[r * 32 + lane] = 1 / id;
+            const float * xv = st.xv + s * S::PAD;
+            unsigned onb = 0;
 #pragma unroll
-            for (int i = 0; i < P::GD; ++i) {
-                const float q = odd_level(level_of<P::GD>(lev, i));
-                const int e = g * P::GD + i;
-                sqx += wx[e] * q;
-                sq2 += w[e] * q * q;
+            for (int g = 0; g < S::NG; ++g) {
+                uint8_t bk = 0xFF;
+                if (live) {
+                    int m;
+                    st.t_lev[task][g] = (uint16_t) round_group<P::GD, P::KMAXQ>(xv + g * P::GD, id, tab, &m);
+                    if (m >= 0) {
+                        onb |= 1u << g;
+                    } else {
+                        bk = (uint8_t) len_bucket(list_cnt(m));
+                        atomicAdd(&sch.hist[bk], 1);
+                    }
+                }
+                sch.bkt[(r * 32 + lane) * S::NG + g] = bk;
+            }
+            if (task < S::NTASK) st.t_on[task] = (uint8_t) onb;
+        }
+        __syncwarp();
+        int nreq;                                                               // S
+        {
+            int c[4], local = 0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) { c[k] = sch.hist[S::NBKT - 1 - (4 * lane + k)]; local += c[k]; }
+            int incl = local;
+#pragma unroll
+            for (int d = 1; d < 32; d <<= 1) {
+                const int v = __shfl_up_sync(0xFFFFFFFFu, incl, d);
+                if (lane >= d) incl += v;
+            }
+            nreq = __shfl_sync(0xFFFFFFFFu, incl, 31);
+            int run = incl - local;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) { sch.hist[S::NBKT - 1 - (4 * lane + k)] = run; run += c[k]; }
+        }
+        __syncwarp();
+        for (int i = lane; i < nr * 32 * S::NG; i += 32) {
+            const int bk = sch.bkt[i];
+            if (bk != 0xFF) sch.perm[atomicAdd(&sch.hist[bk], 1)] = (uint16_t) i;
+        }
+        __syncwarp();
+        for (int k0 = 0; k0 < nreq; k0 += 32) {                                 // Q
+            if (k0 + lane < nreq) {
+                const int item = sch.perm[k0 + lane];
+                const int slot = item / S::NG, g = item - slot * S::NG;
+                const int task = rb * 32 + slot;
+                const int s = task / S::NT;
+                const float * xv = st.xv + s * S::PAD + g * P::GD;
+                const float * wa = st.wa + s * S::PAD + g * P::GD;
+                const int m = __ldg(tab.code3 + code3_of<P::GD>(st.t_lev[task][g]));
+                uint32_t lev = P::GD == 8 ? search_lane8(m, xv, wa, sch.ts[slot], tab) : search_lane4(m, xv, wa, sch.ts[slot], tab);
+                if (lev == NONE) { atomicOr(status, ST_NO_NEIGHBOUR); lev = 0; }
+                st.t_lev[task][g] = (uint16_t) lev;
             }
         }
-        if (task < S::NTASK) {
-            st.t_sqx[task] = live ? sqx : 0.f;
-            st.t_sq2[task] = live ? sq2 : 0.f;
-            st.t_on[task] = (uint8_t) onb;
+        __syncwarp();
+        for (int r = 0; r < nr; ++r) {                                          // M
+            const int task = (rb + r) * 32 + lane;
+            if (task >= S::NTASK) continue;
+            const int s = task / S::NT;
+            float sqx = 0, sq2 = 0;
+            if (!st.skip[s]) {
+                const float * wx = st.wx + s * S::PAD;
+                const float * w = st.w + s * S::PAD;
+                for (int g = 0; g < S::NG; ++g) {
+                    const uint32_t lev = st.t_lev[task][g];
+#pragma unroll
+                    for (int i = 0; i < P::GD; ++i) {
+                        const float q = odd_level(level_of<P::GD>(lev, i));
+                        const int e = g * P::GD + i;
+                        sqx += wx[e] * q;
+                        sq2 += w[e] * q * q;
+                    }
+                }
+            }
+            st.t_sqx[task] = sqx;
+            st.t_sq2[task] = sq2;
         }
+        __syncwarp();
     }
-    __syncwarp();
     // ---- P6: ggml's trial choice replayed in trial order; which groups to snap again
     constexpr unsigned ALL = (1u << S::NG) - 1;
     if (lane < S::NSUB) {
