@@ -17,6 +17,7 @@
 #include "common.cuh"
 #include "source.cuh"
 #include "kernels.h"
+#include "search.cuh"
 
 namespace gq {
 namespace {
@@ -28,9 +29,19 @@ template <> struct IQ1<IQ1_S> { static constexpr int SB = 32, WARPS = 2; static 
 template <> struct IQ1<IQ1_M> { static constexpr int SB = 16, WARPS = 4; static constexpr float EPS = 1e-7f; };
 
 template <int T> struct alignas(16) IQ1Warp {
-    static constexpr int SB = IQ1<T>::SB, NSUB = QK / SB, NSB = 32 / NSUB, NH = T == IQ1_M ? 2 : 1;
+    static constexpr int SB = IQ1<T>::SB, NSUB = QK / SB, NSB = 32 / NSUB, NH = T == IQ1_M ? 2 : 1, NG = SB / 8;
     float x[SB][32], w[SB][32];              // the lane's sub-block, element-major / lane-minor
-    float px[NH][SB + 1][32], pw[NH][SB + 1][32];   // prefix sums (IQ1_M: one pair a half of the sub-block)
+    struct Snap {                            // the snap's search schedule (after the scans)
+        int m[NG * 32];                      // a (group, lane)'s code3 entry
+        uint16_t perm[NG * 32];              // the searches, longest list first
+        uint8_t bkt[NG * 32];                // a (group, lane)'s list-length bucket, 0xFF: no search
+        int hist[NBKT];
+    };
+    union {
+        struct { float px[NH][SB + 1][32], pw[NH][SB + 1][32]; } p;   // prefix sums (IQ1_M: a pair a half)
+        Snap snap;
+    } u;
+    uint8_t bk[32];                          // the split scan's shift choice a lane
     uint8_t idx[SB][32];                     // stable ascending order of the sub-block's weights
     int8_t L[SB][32];
     float scales[32];
@@ -46,39 +57,23 @@ __device__ __forceinline__ float lvl(int l, bool minus) {
     return minus ? (l == 0 ? -1 - DELTA : (l == 1 ? -DELTA : 1 - DELTA)) : (l == 0 ? -1 + DELTA : (l == 1 ? DELTA : 1 + DELTA));
 }
 
-// nearest listed codebook point to the 8 weights of group g of this lane's sub-block, shifted levels (minus: x_m),
-// scale s (iq1_find_best_neighbour2, gpuq.hip:199-232): ggml's distance d2 = 0; d2 += w_i (s q_i - x_i)^2 in order,
-// the first strict minimum in list order. Returns the grid index, -1 if no listed candidate is finite (ggml would
-// then scan the whole grid reading past the group - reported as a device-status error instead).
+// the snap's search of group g of lane sl's sub-block (iq1_find_best_neighbour2, gpuq.hip:199-232): ggml's
+// distance d2 = 0; d2 += w_i (s q_i - x_i)^2 in order with the shifted levels q (minus: x_m), the first strict
+// minimum in list order. Returns the grid index, -1 if no listed candidate is finite (ggml would then scan the whole
+// grid reading past the group - reported as a device-status error instead).
 template <int T>
-__device__ int snap_group(const IQ1Warp<T> & st, int lane, int g, int m, float s, bool minus, const SearchTab & tab) {
+__device__ int snap_group(const IQ1Warp<T> & st, int sl, int g, int m, float s, bool minus, const SearchTab & tab) {
     float t0[8], t1[8], t2[8];
     const float q0 = lvl(0, minus), q1 = lvl(1, minus), q2 = lvl(2, minus);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const float xi = st.x[8 * g + i][lane], wi = st.w[8 * g + i][lane];
-        const float d0 = s * q0 - xi, d1 = s * q1 - xi, d2 = s * q2 - xi;
-        t0[i] = wi * d0 * d0; t1[i] = wi * d1 * d1; t2[i] = wi * d2 * d2;
-    }
-    const uint32_t * lst = tab.neigh + list_off(m);
-    const int n = (int) __ldg(lst);
-    float best = FLT_MAX;
-    uint32_t bl = 0xFFFFFFFFu;
-    uint32_t e = __ldg(lst + 1);
-#pragma unroll 2
-    for (int j = 1; j <= n; ++j) {
-        const uint32_t en = __ldg(lst + j + 1);   // (the table ends with a pad word: always in bounds)
-        float d2 = 0.f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            // level 2 has bit 1 set, level 1 bit 0 (level 3 does not occur): two bit tests, two selects
-            const bool hi = e & (2u << (2 * i)), lo = e & (1u << (2 * i));
-            d2 += hi ? t2[i] : (lo ? t1[i] : t0[i]);
-        }
-        if (d2 < best) { best = d2; bl = e; }
-        e = en;
-    }
-    return bl == 0xFFFFFFFFu ? -1 : (int) (bl >> 16);
+    for (int i = 0; i < 8; ++i) level_terms(st.w[8 * g + i][sl], st.x[8 * g + i][sl], s, q0, q1, q2, t0[i], t1[i], t2[i]);
+    const uint32_t bl = search_list8(m, t0, t1, t2, tab);
+    return bl == NONE ? -1 : (int) (bl >> 16);
+}
+
+// group g's levels take the minus shift (IQ1_S: one shift a sub-block; IQ1_M: one a half, bk's two bits)
+template <int T> __device__ __forceinline__ bool minus_of(int bk, int g) {
+    return T == IQ1_S ? bk == 1 : (g == 0 ? bk >= 2 : (bk % 2) != 0);
 }
 
 template <int T, int SRC>
@@ -135,7 +130,7 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
     const int kb = lane / NSUB;                        // super-block of this lane's sub-block
     const bool live = kb < nb;
     float scale = 0.f;
-    int shift = T == IQ1_S ? 1 : 0;
+    int shift = T == IQ1_S ? 1 : 0, bk = -1;
     bool dropped = true;
     if (live) {
         float mx = fabsf(st.x[0][lane]);
@@ -150,28 +145,28 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
                 st.idx[j + 1][lane] = (uint8_t) i;
             }
             float best = -FLT_MAX;
-            int b1 = -1, b2 = -1, bk = -1;
+            int b1 = -1, b2 = -1;
             scale = mx;
             if constexpr (T == IQ1_S) {
-                st.px[0][0][lane] = 0.f;
-                st.pw[0][0][lane] = 0.f;
+                st.u.p.px[0][0][lane] = 0.f;
+                st.u.p.pw[0][0][lane] = 0.f;
                 float sx = 0.f, sw = 0.f;
                 for (int j = 0; j < SB; ++j) {
                     const int i = st.idx[j][lane];
                     const float wi = st.w[i][lane];
                     sx = sx + wi * st.x[i][lane];
                     sw = sw + wi;
-                    st.px[0][j + 1][lane] = sx;
-                    st.pw[0][j + 1][lane] = sw;
+                    st.u.p.px[0][j + 1][lane] = sx;
+                    st.u.p.pw[0][j + 1][lane] = sw;
                 }
                 const float tx = sx, tw = sw;
                 const float ap = lvl(0, false), bp = lvl(1, false), cp = lvl(2, false);
                 const float am = lvl(0, true), bm = lvl(1, true), cm = lvl(2, true);
                 for (int i1 = 0; i1 <= SB; ++i1) {
-                    const float x1 = st.px[0][i1][lane] - 0.f, w1 = st.pw[0][i1][lane] - 0.f;   // (sumx[i1] - sumx[0])
-                    const float sx1 = st.px[0][i1][lane], sw1 = st.pw[0][i1][lane];
+                    const float x1 = st.u.p.px[0][i1][lane] - 0.f, w1 = st.u.p.pw[0][i1][lane] - 0.f;   // (sumx[i1] - sumx[0])
+                    const float sx1 = st.u.p.px[0][i1][lane], sw1 = st.u.p.pw[0][i1][lane];
                     for (int i2 = i1; i2 <= SB; ++i2) {
-                        const float sx2 = st.px[0][i2][lane], sw2 = st.pw[0][i2][lane];
+                        const float sx2 = st.u.p.px[0][i2][lane], sw2 = st.u.p.pw[0][i2][lane];
                         const float dx = sx2 - sx1, dw = sw2 - sw1, ex = tx - sx2, ew = tw - sw2;
                         float qx = x1 * ap + dx * bp + ex * cp;
                         float q2 = w1 * ap * ap + dw * bp * bp + ew * cp * cp;
@@ -182,15 +177,15 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
                     }
                 }
             } else {
-                for (int h = 0; h < 2; ++h) { st.px[h][0][lane] = 0.f; st.pw[h][0][lane] = 0.f; }
+                for (int h = 0; h < 2; ++h) { st.u.p.px[h][0][lane] = 0.f; st.u.p.pw[h][0][lane] = 0.f; }
                 float ax[2] = {0.f, 0.f}, aw[2] = {0.f, 0.f};
                 for (int j = 0; j < SB; ++j) {   // prefix sums split by half of the sub-block (gpuq.hip:559-571)
                     const int i = st.idx[j][lane], h = i < SB / 2 ? 0 : 1;
                     const float wi = st.w[i][lane];
                     ax[h] = ax[h] + wi * st.x[i][lane];
                     aw[h] = aw[h] + wi;
-                    st.px[0][j + 1][lane] = ax[0]; st.px[1][j + 1][lane] = ax[1];
-                    st.pw[0][j + 1][lane] = aw[0]; st.pw[1][j + 1][lane] = aw[1];
+                    st.u.p.px[0][j + 1][lane] = ax[0]; st.u.p.px[1][j + 1][lane] = ax[1];
+                    st.u.p.pw[0][j + 1][lane] = aw[0]; st.u.p.pw[1][j + 1][lane] = aw[1];
                 }
                 const float p2 = 1 + DELTA, m2 = 1 - DELTA;
                 const float cp1 = (-1 + DELTA) * (-1 + DELTA) - DELTA * DELTA, cp2 = DELTA * DELTA - (1 + DELTA) * (1 + DELTA);
@@ -199,12 +194,12 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
                 const float txp0 = tx0 * p2, txp1 = tx1 * p2, txm0 = tx0 * m2, txm1 = tx1 * m2;
                 const float twp0 = tw0 * p2 * p2, twp1 = tw1 * p2 * p2, twm0 = tw0 * m2 * m2, twm1 = tw1 * m2 * m2;
                 for (int i1 = 0; i1 <= SB; ++i1) {
-                    const float a0 = st.px[0][i1][lane], a1 = st.px[1][i1][lane];
-                    const float c0 = st.pw[0][i1][lane], c1 = st.pw[1][i1][lane];
+                    const float a0 = st.u.p.px[0][i1][lane], a1 = st.u.p.px[1][i1][lane];
+                    const float c0 = st.u.p.pw[0][i1][lane], c1 = st.u.p.pw[1][i1][lane];
                     const float c0p = c0 * cp1, c1p = c1 * cp1, c0m = c0 * cm1, c1m = c1 * cm1;
                     for (int i2 = i1; i2 <= SB; ++i2) {
-                        const float sx0 = a0 + st.px[0][i2][lane], sx1 = a1 + st.px[1][i2][lane];
-                        const float e0 = st.pw[0][i2][lane], e1 = st.pw[1][i2][lane];
+                        const float sx0 = a0 + st.u.p.px[0][i2][lane], sx1 = a1 + st.u.p.px[1][i2][lane];
+                        const float e0 = st.u.p.pw[0][i2][lane], e1 = st.u.p.pw[1][i2][lane];
                         const float qxp0 = txp0 - sx0, qxm0 = txm0 - sx0, qxp1 = txp1 - sx1, qxm1 = txm1 - sx1;
                         const float q2p0 = twp0 + c0p + e0 * cp2, q2m0 = twm0 + c0m + e0 * cm2;
                         const float q2p1 = twp1 + c1p + e1 * cp2, q2m1 = twm1 + c1m + e1 * cm2;
@@ -226,41 +221,74 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
                     scale = -scale;
                     bk = T == IQ1_S ? 1 - bk : 3 - bk;
                 }
-                // the codebook snap, group by group
-                bool all_on = true;
-                for (int g = 0; g < SB / 8; ++g) {
-                    int c3 = 0, p3 = 1;
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) { c3 += st.L[8 * g + i][lane] * p3; p3 *= 3; }
-                    const int m = __ldg(tab.code3 + c3);
-                    const bool minus = T == IQ1_S ? bk == 1 : (g == 0 ? bk >= 2 : (bk % 2) != 0);
-                    int gi = m;
-                    if (m < 0) {
-                        all_on = false;
-                        gi = snap_group<T>(st, lane, g, m, scale, minus, tab);
-                        if (gi < 0) { atomicOr(status, ST_NO_NEIGHBOUR); gi = 0; }
-                    }
-                    st.gidx[g][lane] = (uint16_t) gi;
-                }
-                if (!all_on) {
-                    float sqx = 0, sq2 = 0;
-                    for (int g = 0; g < SB / 8; ++g) {
-                        const bool minus = T == IQ1_S ? bk == 1 : (g == 0 ? bk >= 2 : (bk % 2) != 0);
-                        const uint32_t lev = __ldg(tab.glev + st.gidx[g][lane]);
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) {
-                            const float ww = st.w[8 * g + j][lane], q = lvl((lev >> (2 * j)) & 3u, minus);
-                            sqx += ww * q * st.x[8 * g + j][lane];
-                            sq2 += ww * q * q;
-                        }
-                    }
-                    if (sqx > 0 && sq2 > 0) scale = sqx / sq2;
-                }
-                shift = T == IQ1_S ? (bk == 1 ? -1 : 1) : bk;
             } else {
                 scale = 0.f;
             }
         }
+    }
+    // ---- the codebook snap of every group of the tile's 32 sub-blocks: the groups off the grid searched 32 at a
+    //      time, longest neighbour list first (independent exact searches: the order changes no result)
+    typename W::Snap & sn = st.u.snap;
+    __syncwarp();                                      // (the prefix sums are dead: their space holds the schedule)
+    for (int i = lane; i < NBKT; i += 32) sn.hist[i] = 0;
+    st.scales[lane] = scale;
+    st.bk[lane] = (uint8_t) bk;
+    __syncwarp();
+    bool all_on = true;
+#pragma unroll
+    for (int g = 0; g < W::NG; ++g) {
+        uint8_t b = 0xFF;
+        if (!dropped) {
+            int c3 = 0, p3 = 1;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) { c3 += st.L[8 * g + i][lane] * p3; p3 *= 3; }
+            const int m = __ldg(tab.code3 + c3);
+            sn.m[g * 32 + lane] = m;
+            if (m >= 0) {
+                st.gidx[g][lane] = (uint16_t) m;
+            } else {
+                all_on = false;
+                b = (uint8_t) len_bucket(list_cnt(m));
+                atomicAdd(&sn.hist[b], 1);
+            }
+        }
+        sn.bkt[g * 32 + lane] = b;
+    }
+    __syncwarp();
+    const int nreq = bucket_offsets(sn.hist, lane);
+    __syncwarp();
+#pragma unroll
+    for (int g = 0; g < W::NG; ++g) {
+        const int b = sn.bkt[g * 32 + lane];
+        if (b != 0xFF) sn.perm[atomicAdd(&sn.hist[b], 1)] = (uint16_t) (g * 32 + lane);
+    }
+    __syncwarp();
+    for (int k0 = 0; k0 < nreq; k0 += 32) {
+        if (k0 + lane < nreq) {
+            const int item = sn.perm[k0 + lane], g = item >> 5, sl = item & 31;
+            int gi = snap_group<T>(st, sl, g, sn.m[item], st.scales[sl], minus_of<T>(st.bk[sl], g), tab);
+            if (gi < 0) { atomicOr(status, ST_NO_NEIGHBOUR); gi = 0; }
+            st.gidx[g][sl] = (uint16_t) gi;
+        }
+    }
+    __syncwarp();
+    // ---- the refit over the snapped levels (when a group left the grid), the shift code
+    if (!dropped) {
+        if (!all_on) {
+            float sqx = 0, sq2 = 0;
+            for (int g = 0; g < W::NG; ++g) {
+                const bool minus = minus_of<T>(bk, g);
+                const uint32_t lev = __ldg(tab.glev + st.gidx[g][lane]);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float ww = st.w[8 * g + j][lane], q = lvl((lev >> (2 * j)) & 3u, minus);
+                    sqx += ww * q * st.x[8 * g + j][lane];
+                    sq2 += ww * q * q;
+                }
+            }
+            if (sqx > 0 && sq2 > 0) scale = sqx / sq2;
+        }
+        shift = T == IQ1_S ? (bk == 1 ? -1 : 1) : bk;
     }
     st.scales[lane] = dropped ? 0.f : scale;
     st.shifts[lane] = (int8_t) shift;

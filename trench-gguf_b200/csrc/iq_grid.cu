@@ -68,11 +68,7 @@ template <int T> struct Shape {
     static constexpr int NRG = NSUB * NG;             // re-grid searches a super-block
     // trial rounds scheduled together (their searches sorted by list length): at most 640 searches a batch
     static constexpr int RB = NROUND < 640 / (32 * NG) ? NROUND : (640 / (32 * NG) > 0 ? 640 / (32 * NG) : 1);
-    static constexpr int NBKT = 128;                  // list-length buckets of the schedule
 };
-
-// list-length bucket: exact below 64, then 8 lengths a bucket
-__device__ __forceinline__ int len_bucket(int n) { return n < 64 ? n : imin(127, 64 + ((n - 64) >> 3)); }
 
 // per-warp shared state of one super-block
 template <int T> struct alignas(16) WarpState {
@@ -82,7 +78,7 @@ template <int T> struct alignas(16) WarpState {
         float ts[S::RB * 32];                         // a task's trial scale
         uint16_t perm[S::RB * 32 * S::NG];            // the batch's searches, longest list first
         uint8_t bkt[S::RB * 32 * S::NG];              // a (task, group)'s list-length bucket, 0xFF: on the grid
-        int hist[S::NBKT];                            // bucket counts, then cursors
+        int hist[NBKT];                               // bucket counts, then cursors
     };
     union {                                           // (phase-disjoint uses of one buffer)
         float x2[QK];                                 // x*x, for sumx2
@@ -200,18 +196,7 @@ __device__ __forceinline__ uint32_t search_lane8(int m, const float * xv, const 
     float t0[8], t1[8], t2[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) level_terms(wa[i], xv[i], s, 1.f, 3.f, 5.f, t0[i], t1[i], t2[i]);
-    const uint32_t * lst = tab.neigh + list_off(m) + 1;
-    const int n = list_cnt(m);
-    float best = FLT_MAX;
-    uint32_t bl = NONE;
-    uint32_t e = __ldg(lst);
-#pragma unroll 2
-    for (int j = 0; j < n; ++j) {
-        const uint32_t en = __ldg(lst + j + 1);   // (one past a list: the next count word or the pad word)
-        const float d2 = cand_dist(e, t0, t1, t2);
-        if (d2 < best) { best = d2; bl = e; }
-        e = en;
-    }
+    const uint32_t bl = search_list8(m, t0, t1, t2, tab);
     return bl == NONE ? NONE : (bl & 0xFFFFu);
 }
 
@@ -367,7 +352,7 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
     for (int rb = 0; rb < S::NROUND; rb += S::RB) {
         const int nr = S::NROUND - rb < S::RB ? S::NROUND - rb : S::RB;
         auto & sch = st.u.sch;
-        for (int i = lane; i < S::NBKT; i += 32) sch.hist[i] = 0;
+        for (int i = lane; i < NBKT; i += 32) sch.hist[i] = 0;
         __syncwarp();
         for (int r = 0; r < nr; ++r) {                                          // R
             const int task = (rb + r) * 32 + lane;
@@ -395,22 +380,7 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
             if (task < S::NTASK) st.t_on[task] = (uint8_t) onb;
         }
         __syncwarp();
-        int nreq;                                                               // S
-        {
-            int c[4], local = 0;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) { c[k] = sch.hist[S::NBKT - 1 - (4 * lane + k)]; local += c[k]; }
-            int incl = local;
-#pragma unroll
-            for (int d = 1; d < 32; d <<= 1) {
-                const int v = __shfl_up_sync(0xFFFFFFFFu, incl, d);
-                if (lane >= d) incl += v;
-            }
-            nreq = __shfl_sync(0xFFFFFFFFu, incl, 31);
-            int run = incl - local;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) { sch.hist[S::NBKT - 1 - (4 * lane + k)] = run; run += c[k]; }
-        }
+        const int nreq = bucket_offsets(sch.hist, lane);                        // S
         __syncwarp();
         for (int i = lane; i < nr * 32 * S::NG; i += 32) {
             const int bk = sch.bkt[i];

@@ -51,6 +51,48 @@ __device__ __forceinline__ float cand_dist(uint32_t e, const float (&t0)[8], con
     return d2;
 }
 
+// one lane's whole list (code3 entry m < 0): the first strict minimum of ggml's distance in list order, the next
+// entry loaded one step ahead. Returns the winning entry, NONE if no distance is finite.
+__device__ __forceinline__ uint32_t search_list8(int m, const float (&t0)[8], const float (&t1)[8], const float (&t2)[8],
+                                                 const SearchTab & tab) {
+    const uint32_t * lst = tab.neigh + list_off(m) + 1;
+    const int n = list_cnt(m);
+    float best = FLT_MAX;
+    uint32_t bl = NONE;
+    uint32_t e = __ldg(lst);
+#pragma unroll 2
+    for (int j = 0; j < n; ++j) {
+        const uint32_t en = __ldg(lst + j + 1);   // (one past a list: the next count word or the pad word)
+        const float d2 = cand_dist(e, t0, t1, t2);
+        if (d2 < best) { best = d2; bl = e; }
+        e = en;
+    }
+    return bl;
+}
+
+// list-length bucket of a search schedule (longest first): exact below 64, then 8 lengths a bucket
+constexpr int NBKT = 128;
+__device__ __forceinline__ int len_bucket(int n) { return n < 64 ? n : min(127, 64 + ((n - 64) >> 3)); }
+
+// Warp-collective: the exclusive start of every bucket when the buckets are laid out longest first, written back
+// over the counts in hist[NBKT]; returns the number of items counted.
+__device__ __forceinline__ int bucket_offsets(int * hist, int lane) {
+    int c[4], local = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) { c[k] = hist[NBKT - 1 - (4 * lane + k)]; local += c[k]; }
+    int incl = local;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const int v = __shfl_up_sync(0xFFFFFFFFu, incl, d);
+        if (lane >= d) incl += v;
+    }
+    const int total = __shfl_sync(0xFFFFFFFFu, incl, 31);
+    int run = incl - local;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) { hist[NBKT - 1 - (4 * lane + k)] = run; run += c[k]; }
+    return total;
+}
+
 __device__ __forceinline__ unsigned long long best_key(float d2, int j) {
     return ((unsigned long long) f2u(d2) << 32) | (unsigned) j;
 }
