@@ -67,7 +67,7 @@ __device__ int snap_group(const IQ1Warp<T> & st, int sl, int g, int m, float s, 
     const float q0 = lvl(0, minus), q1 = lvl(1, minus), q2 = lvl(2, minus);
 #pragma unroll
     for (int i = 0; i < 8; ++i) level_terms(st.w[8 * g + i][sl], st.x[8 * g + i][sl], s, q0, q1, q2, t0[i], t1[i], t2[i]);
-    const uint32_t bl = search_list8(m, t0, t1, t2, tab);
+    const uint32_t bl = search_list8<false>(m, t0, t1, t2, tab);
     return bl == NONE ? -1 : (int) (bl >> 16);
 }
 

@@ -39,20 +39,36 @@ __device__ __forceinline__ void level_terms(float w, float x, float s, float q0,
     t2 = w * d2 * d2;
 }
 
-// ggml's distance of one candidate (entry: packed 2-bit levels in bits 0..15), additions in dimension order
+// ggml's distance of one candidate (entry: packed 2-bit levels in bits 0..15), additions in dimension order.
+// Level 2 has bit 1 set, level 1 bit 0 (level 3 does not occur). Per dimension: a select between the level-0 and
+// level-1 terms, then two additions predicated on bit 1 - exactly one of them executes, so d2 gets ggml's single
+// rounded addition of the chosen term - which puts two of the five instructions on the FMA pipe instead of the
+// integer pipe that a second select would use.
+// (PRED = false: two selects, for kernels where the predicated form costs registers)
+template <bool PRED = true>
 __device__ __forceinline__ float cand_dist(uint32_t e, const float (&t0)[8], const float (&t1)[8], const float (&t2)[8]) {
     float d2 = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        // level 2 has bit 1 set, level 1 bit 0 (level 3 does not occur): two bit tests, two selects
-        const bool hi = e & (2u << (2 * i)), lo = e & (1u << (2 * i));
-        d2 += hi ? t2[i] : (lo ? t1[i] : t0[i]);
+        if (!PRED) {
+            const bool hi = e & (2u << (2 * i)), lo = e & (1u << (2 * i));
+            d2 += hi ? t2[i] : (lo ? t1[i] : t0[i]);
+            continue;
+        }
+        const float t01 = (e & (1u << (2 * i))) ? t1[i] : t0[i];
+        asm("{\n\t.reg .pred ph;\n\t.reg .b32 m;\n\t"
+            "and.b32 m, %1, %4;\n\t"
+            "setp.ne.b32 ph, m, 0;\n\t"
+            "@ph add.rn.f32 %0, %0, %3;\n\t"
+            "@!ph add.rn.f32 %0, %0, %2;\n\t}"
+            : "+f"(d2) : "r"(e), "f"(t01), "f"(t2[i]), "r"(2u << (2 * i)));
     }
     return d2;
 }
 
 // one lane's whole list (code3 entry m < 0): the first strict minimum of ggml's distance in list order, the next
 // entry loaded one step ahead. Returns the winning entry, NONE if no distance is finite.
+template <bool PRED = true>
 __device__ __forceinline__ uint32_t search_list8(int m, const float (&t0)[8], const float (&t1)[8], const float (&t2)[8],
                                                  const SearchTab & tab) {
     const uint32_t * lst = tab.neigh + list_off(m) + 1;
@@ -63,7 +79,7 @@ __device__ __forceinline__ uint32_t search_list8(int m, const float (&t0)[8], co
 #pragma unroll 2
     for (int j = 0; j < n; ++j) {
         const uint32_t en = __ldg(lst + j + 1);   // (one past a list: the next count word or the pad word)
-        const float d2 = cand_dist(e, t0, t1, t2);
+        const float d2 = cand_dist<PRED>(e, t0, t1, t2);
         if (d2 < best) { best = d2; bl = e; }
         e = en;
     }
