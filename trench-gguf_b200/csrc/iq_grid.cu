@@ -73,7 +73,11 @@ template <int T> struct Shape {
 // per-warp shared state of one super-block
 template <int T> struct alignas(16) WarpState {
     using S = Shape<T>;
-    struct QP { float mse[S::NSUB][9]; uint8_t L[S::NSUB][32]; };   // make_qp_quants' trials and levels (IQ2_XXS)
+    struct QP {                                       // make_qp_quants (IQ2_XXS)
+        float mse[S::NSUB][9];                        // trial errors
+        float2 prod[S::NSUB][33];                     // an element's w*x*l and w*l*l at the chosen trial scale
+        float sums[S::NSUB][2];                       // sumlx, suml2
+    };
     struct Sched {                                    // one batch of trial rounds
         float ts[S::RB * 32];                         // a task's trial scale
         uint16_t perm[S::RB * 32 * S::NG];            // the batch's searches, longest list first
@@ -121,40 +125,54 @@ __device__ float qp_trial_mse(int k, int nmax, float mx, const float * x, const 
     return mse;
 }
 
-// ... then, one lane a sub-block: ggml's choice among the trials (first strict minimum in trial order), the levels,
-// and the coordinate descent; L in shared memory. Returns the scale.
-template <int N>
-__device__ float qp_finish(int nmax, float mx, const float * x, const float * w, const float * mse, uint8_t * L) {
+// ... then ggml's choice among the trials (first strict minimum in trial order) and its coordinate descent, with
+// the lanes over the 32 elements of one sub-block (warp-collective; every lane calls it with the same sub-block).
+// A pass of the descent visits the elements in order and changes element i only when its new level improves
+// sumlx^2/suml2; an element that does not change leaves the sums as they were, so all lanes test their element
+// against the current sums at once and the first lane whose test passes is the next change - ggml's sequential
+// pass exactly, in (changes + 1) rounds. sumlx and suml2 enter from the index-order sums of the signed levels,
+// while L holds them as ggml's uint8_t array does (a negative level, from the one sign-flipped weight of an odd
+// group, wraps), exactly as the reference's pass reads them. Returns the scale.
+__device__ float qp_descent_warp(int lane, int nmax, float mx, float x, float w, const float * mse, float sumlx,
+                                 float suml2, int L) {
+    for (int pass = 0; pass < 5; ++pass) {
+        int changed = 0, from = 0;
+        for (;;) {
+            float slx = sumlx - w * x * L;
+            float sl2 = suml2 - w * L * L;
+            int nl = L;
+            bool acc = false;
+            if (lane >= from && slx > 0 && sl2 > 0) {
+                nl = imin(nmax, nearest_int(x * sl2 / slx));
+                if (nl != L) {
+                    slx += w * x * nl;
+                    sl2 += w * nl * nl;
+                    acc = slx * slx * suml2 > sumlx * sumlx * sl2;
+                }
+            }
+            const unsigned hit = __ballot_sync(0xFFFFFFFFu, acc);
+            if (!hit) break;
+            const int f = __ffs(hit) - 1;
+            sumlx = __shfl_sync(0xFFFFFFFFu, slx, f);
+            suml2 = __shfl_sync(0xFFFFFFFFu, sl2, f);
+            if (lane == f) L = nl & 255;                // (ggml keeps the levels in uint8_t)
+            ++changed;
+            from = f + 1;
+        }
+        if (!changed) break;
+    }
+    return suml2 > 0.0f ? sumlx / suml2 : 0.0f;
+}
+
+// ggml's choice of make_qp_quants' inverse scale: the initial nmax/max, replaced by a later trial only on a strictly
+// smaller error
+__device__ __forceinline__ float qp_iscale(int nmax, float mx, const float * mse) {
     float iscale = nmax / mx, best_mse = mse[0];
     for (int k = 1; k <= 8; ++k) {
         const int is = k <= 4 ? k - 5 : k - 4;
         if (mse[k] < best_mse) { best_mse = mse[k]; iscale = (0.1f * is + nmax) / mx; }
     }
-    float sumlx = 0, suml2 = 0;
-    for (int i = 0; i < N; ++i) {
-        const int l = imin(nmax, nearest_int(iscale * x[i]));
-        L[i] = (uint8_t) l;
-        sumlx += w[i] * x[i] * l;
-        suml2 += w[i] * l * l;
-    }
-    for (int pass = 0; pass < 5; ++pass) {
-        int changed = 0;
-        for (int i = 0; i < N; ++i) {
-            const int Li = L[i];
-            float slx = sumlx - w[i] * x[i] * Li;
-            float sl2 = suml2 - w[i] * Li * Li;
-            if (slx > 0 && sl2 > 0) {
-                const int nl = imin(nmax, nearest_int(x[i] * sl2 / slx));
-                if (nl != Li) {
-                    slx += w[i] * x[i] * nl;
-                    sl2 += w[i] * nl * nl;
-                    if (slx * slx * suml2 > sumlx * sumlx * sl2) { L[i] = (uint8_t) nl; sumlx = slx; suml2 = sl2; ++changed; }
-                }
-            }
-        }
-        if (!changed) break;
-    }
-    return suml2 > 0.0f ? sumlx / suml2 : 0.0f;
+    return iscale;
 }
 
 // the lattice value 2l+1 of a 3-bit level, as a float, by the 2^23 bias (exact, full-rate FADD)
@@ -332,13 +350,37 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
             st.u.qp.mse[s][k] = qp_trial_mse<P::SB>(k, NMAX, st.qmax[s], st.xv + s * S::PAD, st.w + s * S::PAD);
         }
         __syncwarp();
-        if (lane < S::NSUB && !st.skip[lane]) {
-            const float * xv = st.xv + lane * S::PAD;
-            const float qm = st.qmax[lane];
-            const float scale = qm < 1e-15f ? 0.f : qp_finish<P::SB>(NMAX, qm, xv, st.w + lane * S::PAD, st.u.qp.mse[lane], st.u.qp.L[lane]);
-            st.scale[lane] = scale;
-            st.denom[lane] = scale * P::KMAXQ;
-            if (!(scale * P::KMAXQ > 0)) st.skip[lane] = 1;
+        // the levels at the chosen inverse scale and their products, lane = element; the sums in index order
+        // (one lane a sub-block); then the coordinate descent, one sub-block at a time
+        static_assert(P::SB == 32, "one lane an element");
+        for (int s = 0; s < S::NSUB; ++s) {
+            if (st.skip[s] || st.qmax[s] < 1e-15f) continue;
+            const float x = st.xv[s * S::PAD + lane], w = st.w[s * S::PAD + lane];
+            const int l = imin(NMAX, nearest_int(qp_iscale(NMAX, st.qmax[s], st.u.qp.mse[s]) * x));
+            st.u.qp.prod[s][lane] = make_float2(w * x * l, w * l * l);
+        }
+        __syncwarp();
+        if (lane < S::NSUB && !st.skip[lane] && !(st.qmax[lane] < 1e-15f)) {
+            float sumlx = 0, suml2 = 0;
+            for (int i = 0; i < 32; ++i) { const float2 v = st.u.qp.prod[lane][i]; sumlx += v.x; suml2 += v.y; }
+            st.u.qp.sums[lane][0] = sumlx;
+            st.u.qp.sums[lane][1] = suml2;
+        }
+        __syncwarp();
+        for (int s = 0; s < S::NSUB; ++s) {
+            if (st.skip[s]) continue;
+            const float qm = st.qmax[s];
+            float scale = 0.f;
+            if (!(qm < 1e-15f)) {
+                const float x = st.xv[s * S::PAD + lane], w = st.w[s * S::PAD + lane];
+                const int l = imin(NMAX, nearest_int(qp_iscale(NMAX, qm, st.u.qp.mse[s]) * x));
+                scale = qp_descent_warp(lane, NMAX, qm, x, w, st.u.qp.mse[s], st.u.qp.sums[s][0], st.u.qp.sums[s][1], l & 255);
+            }
+            if (lane == 0) {
+                st.scale[s] = scale;
+                st.denom[s] = scale * P::KMAXQ;
+                if (!(scale * P::KMAXQ > 0)) st.skip[s] = 1;
+            }
         }
         __syncwarp();
     }
