@@ -40,7 +40,9 @@ template <int T> struct alignas(16) IQ1Warp {
     union {
         struct { float px[NH][SB + 1][32], pw[NH][SB + 1][32]; } p;   // prefix sums (IQ1_M: a pair a half)
         Snap snap;
+        float2 prod[SB][32];                 // IQ1_M's super-block refit: an element's w*q*x and w*q*q
     } u;
+    float msc[NSB];                          // a super-block's max sub-block scale
     uint8_t bk[32];                          // the split scan's shift choice a lane
     uint8_t idx[SB][32];                     // stable ascending order of the sub-block's weights
     int8_t L[SB][32];
@@ -316,10 +318,38 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
     }
     __syncwarp();
     if (lane < nb) {
-        uint8_t * y = st.out[lane];
         const float * scl = st.scales + lane * NSUB;
         float max_scale = 0;
         for (int ib = 0; ib < NSUB; ++ib) if (!st.dropped[lane * NSUB + ib]) max_scale = fmaxr(max_scale, scl[ib]);
+        st.msc[lane] = max_scale;
+    }
+    __syncwarp();
+    if constexpr (T == IQ1_M) {
+        // the super-block refit's products, one lane a sub-block: q = x_shift(level) * (2 l + 1) with l the
+        // sub-block's 3-bit scale code; a dropped sub-block counts with grid point 0 and scale code 0, as ggml's
+        // zeroed block bytes make it (gpuq.hip:657-687)
+        const float ms = live ? st.msc[kb] : 0.f;
+        if (ms) {
+            const float id = 1 / (ms / 15);
+            const int l = imax(0, imin(7, nearest_int(0.5f * (id * st.scales[lane] - 1))));
+            const int sh = st.shifts[lane];
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                const bool minus = k == 0 ? sh >= 2 : (sh % 2) != 0;
+                const uint32_t lev = __ldg(tab.glev + (st.dropped[lane] ? 0 : st.gidx[k][lane]));
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float ww = st.w[8 * k + j][lane], q = lvl((lev >> (2 * j)) & 3u, minus) * (2 * l + 1);
+                    st.u.prod[8 * k + j][lane] = make_float2(ww * q * st.x[8 * k + j][lane], ww * q * q);
+                }
+            }
+        }
+        __syncwarp();
+    }
+    if (lane < nb) {
+        uint8_t * y = st.out[lane];
+        const float * scl = st.scales + lane * NSUB;
+        const float max_scale = st.msc[lane];
         if constexpr (T == IQ1_S) {
             y[0] = y[1] = 0;
             if (max_scale) {
@@ -346,16 +376,7 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
                     const int l = imax(0, imin(7, nearest_int(0.5f * (id * scl[ib] - 1))));
                     sc[ib / 4] |= (uint16_t) (l << (3 * (ib % 4)));
                     y[32 + ib] |= masks[st.shifts[sl]];
-                    for (int k = 0; k < 2; ++k) {
-                        const bool minus = k == 0 ? st.shifts[sl] >= 2 : (st.shifts[sl] % 2) != 0;
-                        const int gi = y[2 * ib + k] + ((y[32 + ib] << (8 - 4 * k)) & 0x700);
-                        const uint32_t lev = __ldg(tab.glev + gi);
-                        for (int j = 0; j < 8; ++j) {
-                            const float ww = st.w[8 * k + j][sl], q = lvl((lev >> (2 * j)) & 3u, minus) * (2 * l + 1);
-                            sqx += ww * q * st.x[8 * k + j][sl];
-                            sq2 += ww * q * q;
-                        }
-                    }
+                    for (int e = 0; e < 16; ++e) { const float2 v = st.u.prod[e][sl]; sqx += v.x; sq2 += v.y; }
                 }
                 if (sq2 > 0) d = sqx / sq2;
                 const uint16_t s = half_bits(d * 1.1125f);
