@@ -12,6 +12,9 @@ MXFP4 a GPU, larger than the 126 MB L2, so every step streams its input from HBM
 Multi-GPU (torchrun, one rank a GPU): each rank takes its own 48 experts, no collective on the data path
 ("scaling": "weak"); rank times are combined by max. `--impl reference` times the reference's own CPU code
 (trench-gguf's block functions compiled for the host, oracle/_ref) on a bounded sample with every host core.
+`--impl reference-gpu` (not part of the bench contract) times trench-gguf's own GPU library built for sm_100a
+(oracle/_ref/libgpuq_ref_cuda.so) on the same device-resident step - its decode kernel, then its quantize kernels -
+and checks its bytes against this library's.
 """
 import argparse
 import ctypes
@@ -41,7 +44,7 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-gpu"])
     ap.add_argument("--types", default="iq2_xxs,iq1_m")
     ap.add_argument("--experts", type=int, default=EXPERTS_PER_GPU)
     ap.add_argument("--no-e2e", action="store_true")
@@ -151,6 +154,91 @@ def run_reference(args, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_reference_gpu(args, rank, local):
+    """the reference's own kernels on this GPU: gpuq_dequantize_src_dev (MXFP4 -> f32, once a step) and
+    gpuq_quantize_dev for each type, one launch an expert (its imatrix row addressing: block b reads
+    qw + ((b % qw_mod) / qw_div) * 256, so an expert's 28 blocks a row take qw_mod = 28, qw_div = 1)"""
+    path = os.path.join(ROOT, "oracle", "_ref", "libgpuq_ref_cuda.so")
+    if not os.path.exists(path):
+        if rank == 0:
+            print(json.dumps({"impl": "reference-gpu", "unavailable": "oracle/_ref/libgpuq_ref_cuda.so not built"}))
+        return
+    import torch
+    import gpuq
+    import workloads
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    R = ctypes.CDLL(path)
+    c = ctypes
+    R.gpuq_init.argtypes = [c.c_char_p, c.c_int]
+    R.gpuq_block_bytes.restype = c.c_size_t; R.gpuq_block_bytes.argtypes = [c.c_int]
+    R.gpuq_quantize_dev.restype = c.c_size_t
+    R.gpuq_quantize_dev.argtypes = [c.c_int, c.c_void_p, c.c_void_p, c.c_int64, c.c_void_p, c.c_int64, c.c_int64, c.c_void_p]
+    R.gpuq_dequantize_src_dev.restype = c.c_size_t
+    R.gpuq_dequantize_src_dev.argtypes = [c.c_int, c.c_void_p, c.c_void_p, c.c_int64, c.c_void_p]
+    if R.gpuq_init(os.path.join(PKG, "gpuq_tables.bin").encode(), local) != 0:
+        raise RuntimeError("reference gpuq_init failed")
+    types = args.types.split(",")
+    E = args.experts
+    raw_np, im_np = workloads.config2(experts=E, rows=ROWS, cols=COLS, seed=102 + rank)
+    nw = E * ROWS * COLS
+    raw = torch.from_numpy(raw_np.reshape(-1)).to(dev)
+    im = torch.from_numpy(im_np).to(dev)
+    x = torch.empty(nw, dtype=torch.float32, device=dev)
+    bpr = COLS // 256
+    outs = {t: torch.empty(nw // 256 * R.gpuq_block_bytes(TYPES[t]), dtype=torch.uint8, device=dev) for t in types}
+    stream = torch.cuda.Stream(device=dev)
+    sh = c.c_void_p(stream.cuda_stream)
+
+    def step(ev=None):
+        if R.gpuq_dequantize_src_dev(39, raw.data_ptr(), x.data_ptr(), nw, sh) != nw * 4:
+            raise RuntimeError("reference gpuq_dequantize_src_dev failed")
+        for t in types:
+            bb = R.gpuq_block_bytes(TYPES[t])
+            if ev:
+                ev[t][0].record(stream)
+            for e in range(E):
+                n = R.gpuq_quantize_dev(TYPES[t], x.data_ptr() + e * ROWS * COLS * 4, outs[t].data_ptr() + e * ROWS * bpr * bb,
+                                        ROWS * bpr, im.data_ptr() + e * COLS * 4, bpr, 1, sh)
+                if n != ROWS * bpr * bb:
+                    raise RuntimeError("reference gpuq_quantize_dev failed")
+            if ev:
+                ev[t][1].record(stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    torch.cuda.synchronize()
+    ev = [{t: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for t in types}
+          for _ in range(args.steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for k in range(args.steps):
+            step(ev[k])
+        stop.record(stream)
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(stop) / args.steps
+    per_type = {t: sum(e[t][0].elapsed_time(e[t][1]) for e in ev) / args.steps for t in types}
+    # the same bytes from this library
+    g = gpuq.Gpuq(device=local)
+    same = {}
+    for t in types:
+        mine = torch.empty_like(outs[t])
+        n = g.lib.gpuq_requantize_dev(39, c.c_void_p(raw.data_ptr()), TYPES[t], c.c_void_p(mine.data_ptr()), E, ROWS, COLS,
+                                      c.c_void_p(im.data_ptr()), c.c_void_p(torch.cuda.current_stream().cuda_stream))
+        torch.cuda.synchronize()
+        same[t] = bool(n == mine.numel() and torch.equal(mine, outs[t]))
+    line = {"impl": "reference-gpu", "metric": METRIC, "value": E * ROWS * COLS * len(types) / (ms / 1e3) / 1e9,
+            "unit": "Gweights/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "dtype": "f32", "data": "synthetic (config 2 distributions, seeded)",
+            "config": {"workload": "config 2 shard: %d experts x %d x %d MXFP4 -> %s" % (E, ROWS, COLS, "+".join(types)),
+                       "library": "trench-gguf gpuq.hip, nvcc -O3 -fmad=false -prec-div=true -prec-sqrt=true sm_100a",
+                       "path": "gpuq_dequantize_src_dev once a step + gpuq_quantize_dev an expert a launch"},
+            "per_type_ms": per_type, "identical_to_ours": same}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -158,6 +246,8 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         return run_reference(args, rank)
+    if args.impl == "reference-gpu":
+        return run_reference_gpu(args, rank, int(os.environ.get("LOCAL_RANK", "0")))
     import torch
     import gpuq
     import workloads
