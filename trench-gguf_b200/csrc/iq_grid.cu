@@ -88,9 +88,8 @@ template <int T> struct alignas(16) WarpState {
         float x2[QK];                                 // x*x, for sumx2
         QP qp;
         Sched sch;
-        std::conditional_t<GT<T>::GD == 8, Search8Scratch, char> sc;   // the balanced searches of the 8-d grids
     } u;
-    float w[S::NSUB * S::PAD], wa[S::NSUB * S::PAD], xv[S::NSUB * S::PAD], wx[S::NSUB * S::PAD];
+    float w[S::NSUB * S::PAD], wa[S::NSUB * S::PAD], xv[S::NSUB * S::PAD];
     float qmax[S::NSUB];                              // make_qp_quants' max (from 0)
     float t_sqx[S::NTASK], t_sq2[S::NTASK];
     uint16_t t_lev[S::NTASK][S::NG];
@@ -248,16 +247,7 @@ __device__ __forceinline__ uint32_t group_levels(WarpState<T> & st, int lane, bo
     uint32_t lev = 0;
     if (active) lev = round_group<P::GD, P::KMAXQ>(xv, id, tab, &m);
     *on = active && m >= 0;
-    if constexpr (P::GD == 8) {
-        float t0[8], t1[8], t2[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) level_terms(wa[i], xv[i], s, 1.f, 3.f, 5.f, t0[i], t1[i], t2[i]);
-        const bool req = active && m < 0;
-        const uint32_t e = search8_warp(st.u.sc, lane, req, req ? list_off(m) : 0, t0, t1, t2, tab);
-        if (req) lev = e == NONE ? NONE : (e & 0xFFFFu);
-    } else {
-        if (active && m < 0) lev = search_lane4(m, xv, wa, s, tab);
-    }
+    if (active && m < 0) lev = P::GD == 8 ? search_lane8(m, xv, wa, s, tab) : search_lane4(m, xv, wa, s, tab);
     return lev;
 }
 
@@ -324,7 +314,6 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
         for (int j = 0; j < 8; ++j) {
             const int ei = eidx(P::SB, S::PAD, lane * 8 + j);
             st.xv[ei] = xv[j];
-            st.wx[ei] = wr[j] * xv[j];   // (w*x, the first product of ggml's w*x*q)
         }
         const int e0 = lane * 8;
         st.signs[e0 / P::SB][(e0 % P::SB) / 8] = (uint8_t) (P::PARITY ? (sg & 127u) : sg);
@@ -450,7 +439,7 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
             const int s = task / S::NT;
             float sqx = 0, sq2 = 0;
             if (!st.skip[s]) {
-                const float * wx = st.wx + s * S::PAD;
+                const float * xs = st.xv + s * S::PAD;
                 const float * w = st.w + s * S::PAD;
                 for (int g = 0; g < S::NG; ++g) {
                     const uint32_t lev = st.t_lev[task][g];
@@ -458,7 +447,7 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
                     for (int i = 0; i < P::GD; ++i) {
                         const float q = odd_level(level_of<P::GD>(lev, i));
                         const int e = g * P::GD + i;
-                        sqx += wx[e] * q;
+                        sqx += w[e] * xs[e] * q;   // (ggml's w*x*q, in that order)
                         sq2 += w[e] * q * q;
                     }
                 }
@@ -511,12 +500,12 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
         if (!st.skip[s]) {
             float scale = st.scale[s];
             if (st.regrid[s]) {
-                const float * wx = st.wx + s * S::PAD;
+                const float * xs = st.xv + s * S::PAD;
                 const float * w = st.w + s * S::PAD;
                 float sqx = 0, sq2 = 0;
                 for (int e = 0; e < P::SB; ++e) {
                     const float q = odd_level(level_of<P::GD>(st.lev[s][e / P::GD], e % P::GD));
-                    sqx += wx[e] * q;
+                    sqx += w[e] * xs[e] * q;
                     sq2 += w[e] * q * q;
                 }
                 if (sq2 > 0) scale = sqx / sq2;
