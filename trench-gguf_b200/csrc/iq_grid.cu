@@ -75,11 +75,9 @@ template <int T> struct alignas(16) WarpState {
     using S = Shape<T>;
     struct QP {                                       // make_qp_quants (IQ2_XXS)
         float mse[S::NSUB][9];                        // trial errors
-        float2 prod[S::NSUB][33];                     // an element's w*x*l and w*l*l at the chosen trial scale
-        float sums[S::NSUB][2];                       // sumlx, suml2
+        float sums[S::NSUB][2];                       // sumlx, suml2 at the chosen trial scale
     };
     struct Sched {                                    // one batch of trial rounds
-        float ts[S::RB * 32];                         // a task's trial scale
         uint16_t perm[S::RB * 32 * S::NG];            // the batch's searches, longest list first
         uint8_t bkt[S::RB * 32 * S::NG];              // a (task, group)'s list-length bucket, 0xFF: on the grid
         int hist[NBKT];                               // bucket counts, then cursors
@@ -187,6 +185,12 @@ __device__ __forceinline__ int code3_of(uint32_t lev) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) { c += (int) ((lev >> (2 * i)) & 3u) * p; p *= 3; }
     return c;
+}
+
+// a trial's inverse scale: (2 kmaxq - 1 + is * step) / denom, is = t - ntrial (ggml's expression)
+template <int T>
+__device__ __forceinline__ float trial_id(int t, float denom) {
+    return ((float) (2 * GT<T>::KMAXQ - 1) + (float) (t - GT<T>::NTR) * GT<T>::STEP) / denom;
 }
 
 // ggml's rounding of one group at inverse scale id: l = clamp(nearest_int(0.5*(id*x - 1)), 0, kmaxq-1); returns
@@ -339,19 +343,19 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
             st.u.qp.mse[s][k] = qp_trial_mse<P::SB>(k, NMAX, st.qmax[s], st.xv + s * S::PAD, st.w + s * S::PAD);
         }
         __syncwarp();
-        // the levels at the chosen inverse scale and their products, lane = element; the sums in index order
-        // (one lane a sub-block); then the coordinate descent, one sub-block at a time
+        // the levels at the chosen inverse scale and their sums in index order (one lane a sub-block); then the
+        // coordinate descent, one sub-block at a time with the lanes over its elements
         static_assert(P::SB == 32, "one lane an element");
-        for (int s = 0; s < S::NSUB; ++s) {
-            if (st.skip[s] || st.qmax[s] < 1e-15f) continue;
-            const float x = st.xv[s * S::PAD + lane], w = st.w[s * S::PAD + lane];
-            const int l = imin(NMAX, nearest_int(qp_iscale(NMAX, st.qmax[s], st.u.qp.mse[s]) * x));
-            st.u.qp.prod[s][lane] = make_float2(w * x * l, w * l * l);
-        }
-        __syncwarp();
         if (lane < S::NSUB && !st.skip[lane] && !(st.qmax[lane] < 1e-15f)) {
+            const float * xs = st.xv + lane * S::PAD;
+            const float * ws = st.w + lane * S::PAD;
+            const float iscale = qp_iscale(NMAX, st.qmax[lane], st.u.qp.mse[lane]);
             float sumlx = 0, suml2 = 0;
-            for (int i = 0; i < 32; ++i) { const float2 v = st.u.qp.prod[lane][i]; sumlx += v.x; suml2 += v.y; }
+            for (int i = 0; i < 32; ++i) {
+                const int l = imin(NMAX, nearest_int(iscale * xs[i]));
+                sumlx += ws[i] * xs[i] * l;
+                suml2 += ws[i] * l * l;
+            }
             st.u.qp.sums[lane][0] = sumlx;
             st.u.qp.sums[lane][1] = suml2;
         }
@@ -389,8 +393,7 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
             const int task = (rb + r) * 32 + lane;
             const int s = task < S::NTASK ? task / S::NT : 0, t = task - s * S::NT;
             const bool live = task < S::NTASK && !st.skip[s];
-            const float id = live ? ((float) (2 * P::KMAXQ - 1) + (float) (t - P::NTR) * P::STEP) / st.denom[s] : 1.f;
-            sch.ts[r * 32 + lane] = 1 / id;
+            const float id = live ? trial_id<T>(t, st.denom[s]) : 1.f;
             const float * xv = st.xv + s * S::PAD;
             unsigned onb = 0;
 #pragma unroll
@@ -424,10 +427,11 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
                 const int slot = item / S::NG, g = item - slot * S::NG;
                 const int task = rb * 32 + slot;
                 const int s = task / S::NT;
+                const float ts = 1 / trial_id<T>(task - s * S::NT, st.denom[s]);
                 const float * xv = st.xv + s * S::PAD + g * P::GD;
                 const float * wa = st.wa + s * S::PAD + g * P::GD;
                 const int m = __ldg(tab.code3 + code3_of<P::GD>(st.t_lev[task][g]));
-                uint32_t lev = P::GD == 8 ? search_lane8(m, xv, wa, sch.ts[slot], tab) : search_lane4(m, xv, wa, sch.ts[slot], tab);
+                uint32_t lev = P::GD == 8 ? search_lane8(m, xv, wa, ts, tab) : search_lane4(m, xv, wa, ts, tab);
                 if (lev == NONE) { atomicOr(status, ST_NO_NEIGHBOUR); lev = 0; }
                 st.t_lev[task][g] = (uint16_t) lev;
             }
