@@ -14,6 +14,7 @@
 // sub-blocks side by side (the reference runs one super-block a thread). Per-lane arrays live in shared memory
 // lane-minor ([element][lane]): every access of the warp hits 32 different banks. One lane a super-block computes
 // sumx2 and the super-block scale in index order; the bytes leave through coalesced stores.
+#include <type_traits>
 #include "common.cuh"
 #include "source.cuh"
 #include "kernels.h"
@@ -37,8 +38,10 @@ template <int T> struct alignas(16) IQ1Warp {
         uint8_t bkt[NG * 32];                // a (group, lane)'s list-length bucket, 0xFF: no search
         int hist[NBKT];
     };
+    struct PS { float px[SB + 1][32], pw[SB + 1][32]; };
     union {
-        struct { float px[NH][SB + 1][32], pw[NH][SB + 1][32]; } p;   // prefix sums (IQ1_M: a pair a half)
+        std::conditional_t<T == IQ1_S, PS, char> p;   // IQ1_S: prefix sums
+        float2 sv[SB][32];                   // IQ1_M: (w*x, w) of the sorted elements, for running prefix sums
         Snap snap;
         float2 prod[SB][32];                 // IQ1_M's super-block refit: an element's w*q*x and w*q*q
     } u;
@@ -150,25 +153,25 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
             int b1 = -1, b2 = -1;
             scale = mx;
             if constexpr (T == IQ1_S) {
-                st.u.p.px[0][0][lane] = 0.f;
-                st.u.p.pw[0][0][lane] = 0.f;
+                st.u.p.px[0][lane] = 0.f;
+                st.u.p.pw[0][lane] = 0.f;
                 float sx = 0.f, sw = 0.f;
                 for (int j = 0; j < SB; ++j) {
                     const int i = st.idx[j][lane];
                     const float wi = st.w[i][lane];
                     sx = sx + wi * st.x[i][lane];
                     sw = sw + wi;
-                    st.u.p.px[0][j + 1][lane] = sx;
-                    st.u.p.pw[0][j + 1][lane] = sw;
+                    st.u.p.px[j + 1][lane] = sx;
+                    st.u.p.pw[j + 1][lane] = sw;
                 }
                 const float tx = sx, tw = sw;
                 const float ap = lvl(0, false), bp = lvl(1, false), cp = lvl(2, false);
                 const float am = lvl(0, true), bm = lvl(1, true), cm = lvl(2, true);
                 for (int i1 = 0; i1 <= SB; ++i1) {
-                    const float x1 = st.u.p.px[0][i1][lane] - 0.f, w1 = st.u.p.pw[0][i1][lane] - 0.f;   // (sumx[i1] - sumx[0])
-                    const float sx1 = st.u.p.px[0][i1][lane], sw1 = st.u.p.pw[0][i1][lane];
+                    const float x1 = st.u.p.px[i1][lane] - 0.f, w1 = st.u.p.pw[i1][lane] - 0.f;   // (sumx[i1] - sumx[0])
+                    const float sx1 = st.u.p.px[i1][lane], sw1 = st.u.p.pw[i1][lane];
                     for (int i2 = i1; i2 <= SB; ++i2) {
-                        const float sx2 = st.u.p.px[0][i2][lane], sw2 = st.u.p.pw[0][i2][lane];
+                        const float sx2 = st.u.p.px[i2][lane], sw2 = st.u.p.pw[i2][lane];
                         const float dx = sx2 - sx1, dw = sw2 - sw1, ex = tx - sx2, ew = tw - sw2;
                         float qx = x1 * ap + dx * bp + ex * cp;
                         float q2 = w1 * ap * ap + dw * bp * bp + ew * cp * cp;
@@ -179,15 +182,18 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
                     }
                 }
             } else {
-                for (int h = 0; h < 2; ++h) { st.u.p.px[h][0][lane] = 0.f; st.u.p.pw[h][0][lane] = 0.f; }
+                // the prefix sums split by half of the sub-block (gpuq.hip:559-571) are not stored: both scan loops
+                // run them forward from the sorted elements' (w*x, w), the same additions in the same order (a
+                // half's sum only moves at its own elements; adding +0 to the other half changes nothing)
                 float ax[2] = {0.f, 0.f}, aw[2] = {0.f, 0.f};
-                for (int j = 0; j < SB; ++j) {   // prefix sums split by half of the sub-block (gpuq.hip:559-571)
+                unsigned hmask = 0;                    // bit j: sorted element j is in the second half
+                for (int j = 0; j < SB; ++j) {
                     const int i = st.idx[j][lane], h = i < SB / 2 ? 0 : 1;
-                    const float wi = st.w[i][lane];
-                    ax[h] = ax[h] + wi * st.x[i][lane];
+                    const float wi = st.w[i][lane], wx = wi * st.x[i][lane];
+                    st.u.sv[j][lane] = make_float2(wx, wi);
+                    hmask |= (unsigned) h << j;
+                    ax[h] = ax[h] + wx;
                     aw[h] = aw[h] + wi;
-                    st.u.p.px[0][j + 1][lane] = ax[0]; st.u.p.px[1][j + 1][lane] = ax[1];
-                    st.u.p.pw[0][j + 1][lane] = aw[0]; st.u.p.pw[1][j + 1][lane] = aw[1];
                 }
                 const float p2 = 1 + DELTA, m2 = 1 - DELTA;
                 const float cp1 = (-1 + DELTA) * (-1 + DELTA) - DELTA * DELTA, cp2 = DELTA * DELTA - (1 + DELTA) * (1 + DELTA);
@@ -195,13 +201,12 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
                 const float tx0 = ax[0], tx1 = ax[1], tw0 = aw[0], tw1 = aw[1];
                 const float txp0 = tx0 * p2, txp1 = tx1 * p2, txm0 = tx0 * m2, txm1 = tx1 * m2;
                 const float twp0 = tw0 * p2 * p2, twp1 = tw1 * p2 * p2, twm0 = tw0 * m2 * m2, twm1 = tw1 * m2 * m2;
+                float a0 = 0.f, a1 = 0.f, c0 = 0.f, c1 = 0.f;          // px[h][i1], pw[h][i1]
                 for (int i1 = 0; i1 <= SB; ++i1) {
-                    const float a0 = st.u.p.px[0][i1][lane], a1 = st.u.p.px[1][i1][lane];
-                    const float c0 = st.u.p.pw[0][i1][lane], c1 = st.u.p.pw[1][i1][lane];
                     const float c0p = c0 * cp1, c1p = c1 * cp1, c0m = c0 * cm1, c1m = c1 * cm1;
+                    float r0 = a0, r1 = a1, e0 = c0, e1 = c1;           // px[h][i2], pw[h][i2]
                     for (int i2 = i1; i2 <= SB; ++i2) {
-                        const float sx0 = a0 + st.u.p.px[0][i2][lane], sx1 = a1 + st.u.p.px[1][i2][lane];
-                        const float e0 = st.u.p.pw[0][i2][lane], e1 = st.u.p.pw[1][i2][lane];
+                        const float sx0 = a0 + r0, sx1 = a1 + r1;
                         const float qxp0 = txp0 - sx0, qxm0 = txm0 - sx0, qxp1 = txp1 - sx1, qxm1 = txm1 - sx1;
                         const float q2p0 = twp0 + c0p + e0 * cp2, q2m0 = twm0 + c0m + e0 * cm2;
                         const float q2p1 = twp1 + c1p + e1 * cp2, q2m1 = twm1 + c1m + e1 * cm2;
@@ -212,6 +217,18 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
                             if (sq2[c] > 0 && sqx[c] * sqx[c] > best * sq2[c]) {
                                 scale = sqx[c] / sq2[c]; best = scale * sqx[c]; b1 = i1; b2 = i2; bk = c;
                             }
+                        if (i2 < SB) {                             // on to prefix i2 + 1
+                            const float2 v = st.u.sv[i2][lane];
+                            const bool h = (hmask >> i2) & 1u;
+                            r0 += h ? 0.f : v.x; e0 += h ? 0.f : v.y;
+                            r1 += h ? v.x : 0.f; e1 += h ? v.y : 0.f;
+                        }
+                    }
+                    if (i1 < SB) {                                 // on to prefix i1 + 1
+                        const float2 v = st.u.sv[i1][lane];
+                        const bool h = (hmask >> i1) & 1u;
+                        a0 += h ? 0.f : v.x; c0 += h ? 0.f : v.y;
+                        a1 += h ? v.x : 0.f; c1 += h ? v.y : 0.f;
                     }
                 }
             }
