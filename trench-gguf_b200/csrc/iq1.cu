@@ -48,7 +48,6 @@ template <int T> struct alignas(16) IQ1Warp {
     float msc[NSB];                          // a super-block's max sub-block scale
     uint8_t bk[32];                          // the split scan's shift choice a lane
     uint8_t idx[SB][32];                     // stable ascending order of the sub-block's weights
-    int8_t L[SB][32];
     float scales[32];
     int8_t shifts[32];
     uint8_t dropped[32];                     // sub-block skipped by ggml: nothing written for it
@@ -136,6 +135,7 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
     const bool live = kb < nb;
     float scale = 0.f;
     int shift = T == IQ1_S ? 1 : 0, bk = -1;
+    uint64_t lv = 0;                                   // the sub-block's levels, 2 bits an element
     bool dropped = true;
     if (live) {
         float mx = fabsf(st.x[0][lane]);
@@ -234,9 +234,9 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
             }
             if (b1 >= 0) {
                 dropped = false;
-                for (int j = 0; j < SB; ++j) st.L[st.idx[j][lane]][lane] = (int8_t) (j < b1 ? 0 : j < b2 ? 1 : 2);
+                for (int j = 0; j < SB; ++j) lv |= (uint64_t) (j < b1 ? 0 : j < b2 ? 1 : 2) << (2 * st.idx[j][lane]);
                 if (scale < 0) {
-                    for (int j = 0; j < SB; ++j) st.L[j][lane] = (int8_t) (2 - st.L[j][lane]);
+                    lv = (0xAAAAAAAAAAAAAAAAull >> (64 - 2 * SB)) - lv;   // every level l -> 2 - l (no borrows)
                     scale = -scale;
                     bk = T == IQ1_S ? 1 - bk : 3 - bk;
                 }
@@ -260,7 +260,7 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
         if (!dropped) {
             int c3 = 0, p3 = 1;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) { c3 += st.L[8 * g + i][lane] * p3; p3 *= 3; }
+            for (int i = 0; i < 8; ++i) { c3 += (int) ((lv >> (2 * (8 * g + i))) & 3u) * p3; p3 *= 3; }
             const int m = __ldg(tab.code3 + c3);
             sn.m[g * 32 + lane] = m;
             if (m >= 0) {
