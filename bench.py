@@ -256,7 +256,8 @@ def main():
         import datetime
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        os.environ.setdefault("NCCL_DEBUG", "WARN")   # (rank 0's stdout carries only the JSON line)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     types = args.types.split(",")
