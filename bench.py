@@ -49,6 +49,9 @@ def parse():
     ap.add_argument("--experts", type=int, default=EXPERTS_PER_GPU)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5],
+                    help="2 (default): the metric's own workload; 1, 3, 4, 5: the other benchmark configurations, "
+                         "one GPU, one JSON line each (measurement modes beside the contract)")
     return ap.parse_args()
 
 
@@ -239,8 +242,176 @@ def run_reference_gpu(args, rank, local):
     print(json.dumps(line), flush=True)
 
 
+QTYPES = {"IQ2_XXS": 16, "IQ2_XS": 17, "IQ2_S": 22, "Q2_K": 10, "Q3_K": 11, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14,
+          "Q8_0": 8}
+SRC_BYTES = {0: 4.0, 30: 2.0, 39: 17 / 32}
+
+
+def run_config(args):
+    """Configurations 1, 3, 4 (quantization) and 5 (LDLQ) on one GPU. Each type is timed device resident (CUDA
+    events over `steps` launches through gpuq_requantize_dev, source and imatrix in HBM) and end to end through the
+    host C ABI from pinned memory, the two outputs compared byte for byte; the roofline of each type is given
+    against both bounds: the measured FP32 issue rate (FP32 operations a weight from the oracle's counter,
+    trench-gguf_b200/op_counts.json) and the measured HBM bandwidth (source bytes + block bytes a weight)."""
+    import torch
+    import gpuq
+    import workloads
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    g = gpuq.Gpuq(device=0)
+    L = g.lib
+    ops = load_json("op_counts.json")
+    peaks = load_json(os.path.join("..", "MEASURED_PEAKS.json"))
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    fp32 = fp32_peak_tflops(0)
+    stream = torch.cuda.Stream(device=dev)
+    sh = stream.cuda_stream
+    cfg = args.config
+    if cfg == 5:
+        return run_ldlq(args, g, dev, stream, fp32)
+    if cfg == 1:
+        w, im = workloads.config1(seed=101)
+        jobs = [("IQ2_XXS", 0, w, im[None], (1, w.shape[0], w.shape[1]), "IQ2_XXS@config1")]
+        workload = "config 1: IQ2_XXS of a dense f32 4096 x 14336 tensor, t(5) + 0.1 % outliers x10"
+    elif cfg == 3:
+        E = args.experts
+        raw, im = workloads.config3(experts=E, rows=ROWS, cols=COLS, seed=103)
+        rawd, imd = workloads.config3(experts=E, rows=COLS, cols=ROWS, seed=1031)
+        jobs = []
+        for t in ("IQ2_XS", "IQ2_S"):
+            jobs.append((t, 30, raw, im, (E, ROWS, COLS), t + "@config3"))
+            jobs.append((t + " down", 30, rawd, imd, (E, COLS, ROWS), t + "@config3d"))
+        workload = "config 3: %d BF16 experts, 2048 x 7168 (gate/up) and 7168 x 2048 (down) -> IQ2_XS, IQ2_S" % E
+    else:
+        raw, im = workloads.config4(seed=104)
+        shape = (1, raw.shape[0], raw.shape[1])
+        jobs = []
+        for t in ("Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K"):
+            jobs.append((t + "+im", 30, raw, im[None], shape, t + "+im"))
+            jobs.append((t, 30, raw, None, shape, t))
+        jobs.append(("Q8_0", 30, raw, None, shape, "Q8_0"))
+        workload = "config 4: BF16 8192 x 28672 -> Q2_K..Q6_K with and without imatrix, Q8_0"
+    results = {}
+    total_w = 0
+    total_ms = 0.0
+    e2e_s = 0.0
+    h2d = d2h = 0
+    with Clocks(0) as clk:
+        for name, src, host_raw, host_im, (nmat, nrow, npr), key in jobs:
+            t = QTYPES[name.split()[0].split("+")[0]]
+            nw = nmat * nrow * npr
+            blen = 32 if t == 8 else 256
+            nbytes = nw // blen * g.block_bytes(t)
+            d_raw = torch.from_numpy(np.ascontiguousarray(host_raw).reshape(-1).view(np.uint8)).to(dev)
+            d_im = torch.from_numpy(np.ascontiguousarray(host_im)).to(dev) if host_im is not None else None
+            out = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+
+            def launch():
+                n = L.gpuq_requantize_dev(src, ctypes.c_void_p(d_raw.data_ptr()), t, ctypes.c_void_p(out.data_ptr()), nmat,
+                                          nrow, npr, ctypes.c_void_p(d_im.data_ptr()) if d_im is not None else None, sh)
+                if n != nbytes:
+                    raise RuntimeError("%s: %s" % (name, g.error()))
+            with torch.cuda.stream(stream):
+                for _ in range(args.warmup):
+                    launch()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                for _ in range(args.steps):
+                    launch()
+                b.record(stream)
+            torch.cuda.synchronize()
+            ms = a.elapsed_time(b) / args.steps
+            # end to end through the host ABI, pinned buffers
+            hsrc = torch.from_numpy(np.ascontiguousarray(host_raw).reshape(-1).view(np.uint8)).pin_memory()
+            hout = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+            him = np.ascontiguousarray(host_im) if host_im is not None else None
+
+            def host_call():
+                n = L.gpuq_requantize_batch(src, ctypes.c_void_p(hsrc.data_ptr()), t, ctypes.c_void_p(hout.data_ptr()),
+                                            nmat, nrow, npr, him.ctypes.data if him is not None else None)
+                if n != nbytes:
+                    raise RuntimeError("%s host: %s" % (name, g.error()))
+            host_call()
+            t0 = time.perf_counter()
+            for _ in range(args.steps):
+                host_call()
+            dt = (time.perf_counter() - t0) / args.steps
+            if not torch.equal(hout, out.cpu()):
+                raise RuntimeError("%s: host and device paths differ" % name)
+            opw = ops.get(key, {}).get("ops_per_weight")
+            bpw = SRC_BYTES[src] + g.block_bytes(t) / blen
+            gws = nw / (ms / 1e3) / 1e9
+            results[name] = {"ms": ms, "gweights_s": gws, "e2e_gweights_s": nw / dt / 1e9,
+                             "fp32_frac": (opw * gws / 1e3) / fp32 if opw else None, "ops_per_weight": opw,
+                             "hbm_frac": bpw * gws / hbm, "bytes_per_weight": bpw}
+            total_w += nw
+            total_ms += ms
+            e2e_s += dt
+            h2d += hsrc.numel() + (him.nbytes if him is not None else 0)
+            d2h += nbytes
+            del d_raw, d_im, out
+    if L.gpuq_status(1) != 0:
+        raise RuntimeError("device status set during the measurement")
+    line = {"metric": "Gweights/s quantized, config %d" % cfg, "value": total_w / (total_ms / 1e3) / 1e9,
+            "unit": "Gweights/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms,
+            "higher_is_better": True, "dtype": "f32", "data": "synthetic (config %d distributions, seeded)" % cfg,
+            "config": {"workload": workload, "l2": "every source larger than L2"}, "per_type": results,
+            "e2e": {"value": total_w / e2e_s / 1e9, "unit": "Gweights/s", "timing": "host clock, one call a type",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "roofline_peaks": {"fp32_tops": fp32, "hbm_gbs": hbm, "source": "peak.cu measured in this run; "
+                               "MEASURED_PEAKS.json hbm_gbs"}, "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+
+
+def run_ldlq(args, g, dev, stream, fp32):
+    """config 5: LDLQ re-quantization of experts 2048 x 7168 to IQ2_XXS with their own Hessians
+    H = X^T X / n + 0.01 mean(diag) I (X = (Z + A B) diag(g), n = 4096, rank-32 structure, built on the GPU), timed
+    per expert from the Hessian's factorisation through the 28-block feedback loop (ldlq_gpu.py)."""
+    import torch
+    import ldlq_gpu
+    E = args.experts if args.experts != EXPERTS_PER_GPU else 8
+    n, rank, ne1, ne0 = 4096, 32, ROWS, COLS
+    gen = torch.Generator(device=dev).manual_seed(105)
+    torch.manual_seed(105)
+    gqt = ldlq_gpu.GpuQuant(g.lib, 16)
+    times, losses = [], []
+    for e in range(E):
+        Z = torch.randn(n, ne0, device=dev, generator=gen)
+        A = torch.randn(n, rank, device=dev, generator=gen)
+        B = torch.randn(rank, ne0, device=dev, generator=gen) / rank ** 0.5
+        gain = torch.exp(torch.randn(ne0, device=dev, generator=gen))
+        X = (Z + A @ B) * gain[None]
+        H = X.double().T @ X.double()
+        im = (torch.diagonal(H) / n).float()[None].contiguous()
+        W = (torch.distributions.StudentT(5.0).sample((1, ne1, ne0)).to(dev) * 0.02 / (5.0 / 3.0) ** 0.5).float()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            a.record(stream)
+            U, perm, diag_n, dead = ldlq_gpu.prepare_hessian_torch(H, n, device=dev, out="torch")
+            q = ldlq_gpu.quantize_matrix_torch(W.clone(), gqt, U=U, perm=perm, diag_n=diag_n, imatrix=im)
+            b.record(stream)
+        torch.cuda.synchronize()
+        if e >= min(1, E - 1):               # the first expert warms the library and cuSOLVER up
+            times.append(a.elapsed_time(b))
+        deq = gqt.dequant(q.reshape(1, -1, gqt.tsize)).reshape(ne1, ne0)
+        D = (W[0] - deq).double()
+        losses.append(float(((D @ H) * D).sum()) / n)          # ldlq.py:110-113's proxy loss, on the GPU
+        del Z, A, B, X, H
+    ms = statistics.mean(times)
+    line = {"metric": "Gweights/s LDLQ-requantized to IQ2_XXS, config 5", "value": ne1 * ne0 / (ms / 1e3) / 1e9,
+            "unit": "Gweights/s", "n_gpus": 1, "steps": len(times), "warmup": 1, "ms_per_step": ms,
+            "higher_is_better": True, "dtype": "f32 weights, f64 feedback", "data": "synthetic (config 5, seeded)",
+            "config": {"workload": "config 5: %d experts 2048 x 7168 -> IQ2_XXS, own Hessian each (7168^2), "
+                       "act order seq, imatrix weights, f64 update; a step = one expert" % E},
+            "proxy_loss_mean": statistics.mean(losses)}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
+    if args.config != 2:
+        return run_config(args)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

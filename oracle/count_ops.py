@@ -48,6 +48,13 @@ def main():
         count(name, orc.TYPES[name], x2, im, s2)
     w1, im1 = workloads.config1(rows=16, cols=14336, seed=101)
     count("IQ2_XXS@config1", 16, w1[None], im1[None], "config 1: 16 rows x 14336 dense f32, t(5) + outliers")
+    raw3, im3 = workloads.config3(experts=1, rows=32, cols=7168, seed=103)
+    x3 = c.decode(30, raw3, raw3.size).reshape(1, 32, 7168)
+    raw3d, im3d = workloads.config3(experts=1, rows=64, cols=2048, seed=103)
+    x3d = c.decode(30, raw3d, raw3d.size).reshape(1, 64, 2048)
+    for name in ("IQ2_XS", "IQ2_S"):
+        count(name + "@config3", orc.TYPES[name], x3, im3, "config 3: 32 rows x 7168 of a BF16 expert, N(0,0.015) + t tail")
+        count(name + "@config3d", orc.TYPES[name], x3d, im3d, "config 3 down shape: 64 rows x 2048 of a BF16 expert")
     raw4, im4 = workloads.config4(rows=16, cols=28672, seed=104)
     x4 = c.decode(30, raw4, raw4.size).reshape(1, 16, 28672)
     s4 = "config 4: 16 rows x 28672 BF16 N(0,0.02)"
