@@ -78,7 +78,7 @@ template <int T> struct alignas(16) WarpState {
         float sums[S::NSUB][2];                       // sumlx, suml2 at the chosen trial scale
     };
     struct Sched {                                    // one batch of trial rounds
-        uint16_t perm[S::RB * 32 * S::NG];            // the batch's searches, longest list first
+        uint16_t perm[(S::RB * 32 < S::NTASK ? S::RB * 32 : S::NTASK) * S::NG];   // the batch's searches, longest first
         uint8_t bkt[S::RB * 32 * S::NG];              // a (task, group)'s list-length bucket, 0xFF: on the grid
         int hist[NBKT];                               // bucket counts, then cursors
     };
@@ -86,6 +86,7 @@ template <int T> struct alignas(16) WarpState {
         float x2[QK];                                 // x*x, for sumx2
         QP qp;
         Sched sch;
+        uint8_t out[112];                             // the block's bytes (after the trials)
     } u;
     float w[S::NSUB * S::PAD], wa[S::NSUB * S::PAD], xv[S::NSUB * S::PAD];
     float qmax[S::NSUB];                              // make_qp_quants' max (from 0)
@@ -97,7 +98,6 @@ template <int T> struct alignas(16) WarpState {
     int32_t gidx[S::NSUB][S::NG];
     uint8_t signs[S::NSUB][S::NSG];
     uint8_t skip[S::NSUB], regrid[S::NSUB];
-    uint8_t out[112];
     float sigma2;
 };
 
@@ -532,7 +532,7 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
     __syncwarp();
     // ---- P9: super-block scale and the block bytes (lane 0), then a coalesced store
     if (lane == 0) {
-        uint8_t * y = st.out;
+        uint8_t * y = st.u.out;
         for (int i = 0; i < block_bytes(T); ++i) y[i] = 0;
         float max_scale = 0;
         for (int s = 0; s < S::NSUB; ++s) if (!st.skip[s]) max_scale = fmaxr(max_scale, st.scale[s]);
@@ -615,7 +615,7 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
     }
     __syncwarp();
     uint8_t * yo = out + b * block_bytes(T);
-    for (int i = lane; i < block_bytes(T); i += 32) yo[i] = st.out[i];
+    for (int i = lane; i < block_bytes(T); i += 32) yo[i] = st.u.out[i];
 }
 
 template <int T, int SRC>

@@ -86,16 +86,17 @@ __device__ __forceinline__ uint32_t search_list8(int m, const float (&t0)[8], co
     return bl;
 }
 
-// list-length bucket of a search schedule (longest first): exact below 64, then 8 lengths a bucket
-constexpr int NBKT = 128;
-__device__ __forceinline__ int len_bucket(int n) { return n < 64 ? n : min(127, 64 + ((n - 64) >> 3)); }
+// list-length bucket of a search schedule (longest first): exact below 48, then 8 lengths a bucket (lists of 176
+// points and more share the last one)
+constexpr int NBKT = 64, BKT_PER_LANE = NBKT / 32;
+__device__ __forceinline__ int len_bucket(int n) { return n < 48 ? n : min(NBKT - 1, 48 + ((n - 48) >> 3)); }
 
 // Warp-collective: the exclusive start of every bucket when the buckets are laid out longest first, written back
 // over the counts in hist[NBKT]; returns the number of items counted.
 __device__ __forceinline__ int bucket_offsets(int * hist, int lane) {
-    int c[4], local = 0;
+    int c[BKT_PER_LANE], local = 0;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) { c[k] = hist[NBKT - 1 - (4 * lane + k)]; local += c[k]; }
+    for (int k = 0; k < BKT_PER_LANE; ++k) { c[k] = hist[NBKT - 1 - (BKT_PER_LANE * lane + k)]; local += c[k]; }
     int incl = local;
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
@@ -105,7 +106,7 @@ __device__ __forceinline__ int bucket_offsets(int * hist, int lane) {
     const int total = __shfl_sync(0xFFFFFFFFu, incl, 31);
     int run = incl - local;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) { hist[NBKT - 1 - (4 * lane + k)] = run; run += c[k]; }
+    for (int k = 0; k < BKT_PER_LANE; ++k) { hist[NBKT - 1 - (BKT_PER_LANE * lane + k)] = run; run += c[k]; }
     return total;
 }
 
