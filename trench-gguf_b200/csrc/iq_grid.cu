@@ -196,17 +196,24 @@ __device__ __forceinline__ float trial_id(int t, float denom) {
 // ggml's rounding of one group at inverse scale id: l = clamp(nearest_int(0.5*(id*x - 1)), 0, kmaxq-1); returns
 // the packed levels and the grid-table entry of the code (>= 0 grid index, < 0 the neighbour list)
 template <int GD, int KMAXQ>
-__device__ __forceinline__ uint32_t round_group(const float * xv, float id, const SearchTab & tab, int * m) {
+__device__ __forceinline__ uint32_t round_levels(const float * xv, float id, int * c3) {
     constexpr int BITS = GD == 8 ? 2 : 3;
     uint32_t lev = 0;
-    int c3 = 0, p3 = 1;
+    int c = 0, p3 = 1;
 #pragma unroll
     for (int i = 0; i < GD; ++i) {
         const int l = imax(0, imin(KMAXQ - 1, nearest_int(0.5f * (id * xv[i] - 1))));
         lev |= (uint32_t) l << (BITS * i);
-        c3 += l * p3;
+        c += l * p3;
         p3 *= (GD == 8 ? 3 : 8);
     }
+    *c3 = c;
+    return lev;
+}
+template <int GD, int KMAXQ>
+__device__ __forceinline__ uint32_t round_group(const float * xv, float id, const SearchTab & tab, int * m) {
+    int c3;
+    const uint32_t lev = round_levels<GD, KMAXQ>(xv, id, &c3);
     *m = __ldg(tab.code3 + c3);
     return lev;
 }
@@ -395,17 +402,24 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
             const bool live = task < S::NTASK && !st.skip[s];
             const float id = live ? trial_id<T>(t, st.denom[s]) : 1.f;
             const float * xv = st.xv + s * S::PAD;
+            // all the task's codes first, then their table loads together (in flight at once), then the bookkeeping
+            int c3[S::NG], m[S::NG];
+#pragma unroll
+            for (int g = 0; g < S::NG; ++g) {
+                const uint32_t lev = round_levels<P::GD, P::KMAXQ>(xv + g * P::GD, id, &c3[g]);
+                if (live) st.t_lev[task][g] = (uint16_t) lev;
+            }
+#pragma unroll
+            for (int g = 0; g < S::NG; ++g) m[g] = live ? __ldg(tab.code3 + c3[g]) : 0;
             unsigned onb = 0;
 #pragma unroll
             for (int g = 0; g < S::NG; ++g) {
                 uint8_t bk = 0xFF;
                 if (live) {
-                    int m;
-                    st.t_lev[task][g] = (uint16_t) round_group<P::GD, P::KMAXQ>(xv + g * P::GD, id, tab, &m);
-                    if (m >= 0) {
+                    if (m[g] >= 0) {
                         onb |= 1u << g;
                     } else {
-                        bk = (uint8_t) len_bucket(list_cnt(m));
+                        bk = (uint8_t) len_bucket(list_cnt(m[g]));
                         atomicAdd(&sch.hist[bk], 1);
                     }
                 }
