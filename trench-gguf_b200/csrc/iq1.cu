@@ -8,10 +8,11 @@
 // codebook (nearest listed neighbour with the shifted level values), the scale refit, and the scales coded
 // (IQ1_M also refits the super-block scale over all 256 weights, skipped sub-blocks included).
 //
-// sm_100a mapping: one warp a tile of 32 sub-blocks (4 IQ1_S or 2 IQ1_M super-blocks), ONE LANE A SUB-BLOCK.
-// Every lane runs its sub-block's sort, prefix sums, split scan, codebook snap and refit exactly as ggml does -
-// sequential order inside the lane, so the decisions are ggml's by construction - and the 32 lanes run 32
-// sub-blocks side by side (the reference runs one super-block a thread). Per-lane arrays live in shared memory
+// sm_100a mapping: one warp a tile of 32 sub-blocks (4 IQ1_S or 2 IQ1_M super-blocks), ONE LANE A SUB-BLOCK for
+// ggml's sequential work: the stable sort, the prefix sums (IQ1_M: run forward inside the scan), the split scan and
+// the refit run in ggml's order inside the lane, so the decisions are ggml's by construction, 32 sub-blocks side by
+// side (the reference runs one super-block a thread). The codebook snap is a warp phase: every off-grid group of
+// the tile searched 32 at a time, longest neighbour list first (search.cuh). Per-lane arrays live in shared memory
 // lane-minor ([element][lane]): every access of the warp hits 32 different banks. One lane a super-block computes
 // sumx2 and the super-block scale in index order; the bytes leave through coalesced stores.
 #include <type_traits>

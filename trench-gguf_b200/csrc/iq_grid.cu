@@ -9,16 +9,15 @@
 //
 // How it runs on sm_100a: one warp a super-block, FP32-ALU bound. Lanes own independent work only:
 //   * elementwise weights and sign groups (8 weights a lane),
-//   * the (sub-block, trial) pairs of make_qp_quants' trial scales (IQ2_XXS) and of the trial search (104..304 a
-//     super-block), each lane running its trial's groups and index-ordered sums exactly as ggml does,
+//   * make_qp_quants (IQ2_XXS): its trial scales one a lane, its coordinate descent with the lanes over the 32
+//     elements (the first lane whose test passes is ggml's next change),
+//   * the trials: every (sub-block, trial) task's groups rounded, then the batch's neighbour searches sorted by
+//     list length and run 32 at a time, one whole list a lane (search.cuh), then each task's sums in index order,
 //   * the (sub-block, group) pairs of the re-gridding.
-// The neighbour searches dominate (3k..22k candidate points a super-block). For the 8-d grids the 32 lanes' searches
-// of one group step run warp-balanced (search.cuh): the lists laid end to end, equal shares a lane, the per-dimension
-// terms w_i (s q - x_i)^2 (q in {1, 3, 5}) formed once a search and read from shared memory, ggml's 8 additions in
-// ggml's order. The 4-d grids' short lists run one a lane with the distance formed in place.
-// ggml's sequential decisions (which trial wins: a strict `>` scan in trial order) are replayed in trial order by
-// one lane per sub-block from the stored per-trial sums, so the choice is bit-identical. Sums that ggml runs in
-// index order (sumx2 over 256, the 16/32-weight sums) run in index order inside one lane.
+// The neighbour searches dominate (3k..22k candidate points a super-block). ggml's sequential decisions (which
+// trial wins: a strict `>` scan in trial order) are replayed in trial order by one lane per sub-block from the stored
+// per-trial sums, so the choice is bit-identical. Sums that ggml runs in index order (sumx2 over 256, the
+// 16/32-weight sums) run in index order inside one lane.
 #include <type_traits>
 #include "common.cuh"
 #include "search.cuh"
