@@ -427,8 +427,18 @@ def main():
         import datetime
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        os.environ.setdefault("NCCL_DEBUG", "WARN")   # (rank 0's stdout carries only the JSON line)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+        # the communicator is set up here (eager, bound to the device); anything NCCL prints meanwhile goes to stderr,
+        # so rank 0's stdout carries the JSON line alone
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+            dist.barrier()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved, 1)
+            os.close(saved)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     types = args.types.split(",")
