@@ -321,21 +321,31 @@ __device__ float qp_levels(int nmax, const float * x, uint8_t * Lo, const float 
     return suml2 > 0.0f ? sumlx / suml2 : 0.0f;
 }
 
+// The IQ4 levels as floats and, for every integer k in [-127, 112], mu(k) = #{v <= k}: per CTA in shared memory
+// (each lane indexes its own level: shared memory serves 16 distinct words without a conflict, where the constant
+// cache would serialise them)
+struct IQ4Tab { float v[16]; uint8_t mu[240]; };
+__device__ __forceinline__ void iq4_tab_init(IQ4Tab & t) {
+    for (int i = threadIdx.x; i < 240; i += blockDim.x) {
+        int mu = 0;
+        for (int j = 0; j < 16; ++j) mu += (i - 127) >= c_iq4[j];
+        t.mu[i] = (uint8_t) mu;
+    }
+    if (threadIdx.x < 16) t.v[threadIdx.x] = (float) c_iq4[threadIdx.x];
+}
+
 // nearest of the 16 IQ4 levels (best_index_int8, gpuq.hip:1286-1295): x strictly inside the range lies in
 // [v[mu-1], v[mu]) with mu = #{v <= x}; the levels are integers, so mu = #{v <= floor(x)}
-__device__ __forceinline__ int iq4_index(float x) {
+__device__ __forceinline__ int iq4_index(float x, const IQ4Tab & t) {
     if (x <= -127.f) return 0;
     if (x >= 113.f) return 15;
     if (!(x == x)) return 15;   // (NaN: the reference's search ends on the last bracket)
-    const float f = floorf(x);
-    int mu = 0;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) mu += f >= (float) c_iq4[j];
-    return x - (float) c_iq4[mu - 1] < (float) c_iq4[mu] - x ? mu - 1 : mu;
+    const int mu = t.mu[__float2int_rd(x) + 127];
+    return x - t.v[mu - 1] < t.v[mu] - x ? mu - 1 : mu;
 }
 
 // one IQ4 sub-block's scale search (gpuq.hip:1311-1359), one lane: returns d (0 when skipped)
-__device__ float iq4_sub(const float * xb, const float * w) {
+__device__ float iq4_sub(const float * xb, const float * w, const IQ4Tab & tb) {
     float amax = 0, mx = 0;
     for (int j = 0; j < 32; ++j) { const float ax = fabsf(xb[j]); if (ax > amax) { amax = ax; mx = xb[j]; } }
     if (amax < 1e-15f) return 0.f;
@@ -343,7 +353,7 @@ __device__ float iq4_sub(const float * xb, const float * w) {
     float id = 1 / d;
     float sqx = 0, sq2 = 0;
     for (int j = 0; j < 32; ++j) {
-        const float q = c_iq4[iq4_index(id * xb[j])];
+        const float q = tb.v[iq4_index(id * xb[j], tb)];
         sqx += w[j] * q * xb[j];
         sq2 += w[j] * q * q;
     }
@@ -353,7 +363,7 @@ __device__ float iq4_sub(const float * xb, const float * w) {
         id = (t + -127) / mx;
         sqx = sq2 = 0;
         for (int j = 0; j < 32; ++j) {
-            const float q = c_iq4[iq4_index(id * xb[j])];
+            const float q = tb.v[iq4_index(id * xb[j], tb)];
             sqx += w[j] * q * xb[j];
             sq2 += w[j] * q * q;
         }
@@ -370,8 +380,13 @@ __global__ void __launch_bounds__(128) k_kquant(const uint8_t * __restrict__ src
     using S = KState<T>;
     constexpr int BL = S::BL, SB = S::SB, NB = S::NB, NSUBB = S::NSUBB, TILE = S::TILE, BB = block_bytes(T);
     extern __shared__ __align__(16) unsigned char smem_raw[];
+    __shared__ IQ4Tab s_iq4;
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     S & st = reinterpret_cast<S *>(smem_raw)[wid];
+    if constexpr (T == IQ4_NL || T == IQ4_XS) {    // (before any warp leaves: every thread reaches the barrier)
+        iq4_tab_init(s_iq4);
+        __syncthreads();
+    }
     const int64_t b0 = ((int64_t) blockIdx.x * (blockDim.x >> 5) + wid) * NB;   // first block of this warp's tile
     if (b0 >= nblocks) return;
     const int nb = (int) (nblocks - b0 < NB ? nblocks - b0 : NB);                // blocks in this tile
@@ -466,7 +481,7 @@ __global__ void __launch_bounds__(128) k_kquant(const uint8_t * __restrict__ src
             } else if constexpr (T == Q6_K) {
                 scale = sym_levels<16>(32, xb, Lb, IMAT ? wb : nullptr);
             } else {   // IQ4_NL / IQ4_XS
-                scale = iq4_sub(xb, wb);
+                scale = iq4_sub(xb, wb, s_iq4);
             }
         }
         st.scales[s] = scale;
@@ -635,11 +650,11 @@ __global__ void __launch_bounds__(128) k_kquant(const uint8_t * __restrict__ src
             } else if constexpr (T == IQ4_XS) {
                 const float dl = st.mins[k * 8 + j];
                 const float idl = dl ? 1 / dl : 0.f;
-                st.L[e] = (uint8_t) iq4_index(idl * xv);
+                st.L[e] = (uint8_t) iq4_index(idl * xv, s_iq4);
             } else {
                 const float s0 = st.scales[k];
                 const float id = s0 ? 1 / s0 : 0;
-                st.L[e] = (uint8_t) iq4_index(id * xv);
+                st.L[e] = (uint8_t) iq4_index(id * xv, s_iq4);
             }
         }
     }
