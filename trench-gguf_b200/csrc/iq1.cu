@@ -142,13 +142,34 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
         float mx = fabsf(st.x[0][lane]);
         for (int i = 1; i < SB; ++i) mx = fmaxr(mx, fabsf(st.x[i][lane]));
         if (!(mx < IQ1<T>::EPS)) {
-            // insertion sort of the indices by weight (glibc's stable qsort order: ties keep index order)
-            st.idx[0][lane] = 0;
-            for (int i = 1; i < SB; ++i) {
-                const float k = st.x[i][lane];
-                int j = i - 1;
-                while (j >= 0 && st.x[st.idx[j][lane]][lane] > k) { st.idx[j + 1][lane] = st.idx[j][lane]; --j; }
-                st.idx[j + 1][lane] = (uint8_t) i;
+            // the stable ascending order of the weights (the reference's insertion sort, gpuq.hip:236-243: ties keep
+            // index order). Without NaN it is a rank: element i goes after every j < i with x_j <= x_i and every
+            // j > i with x_j < x_i - independent comparisons instead of the insertion's dependent chain. A NaN
+            // compares false everywhere and stalls the insertion in place, so a sub-block holding one is sorted by
+            // the insertion itself.
+            float xs[SB];
+            bool nan = false;
+#pragma unroll
+            for (int i = 0; i < SB; ++i) { xs[i] = st.x[i][lane]; nan |= !(xs[i] == xs[i]); }
+            if (!nan) {
+#pragma unroll
+                for (int i = 0; i < SB; ++i) {
+                    int r = 0;
+#pragma unroll
+                    for (int j = 0; j < SB; ++j) {
+                        if (j < i) r += xs[j] <= xs[i];
+                        else if (j > i) r += xs[j] < xs[i];
+                    }
+                    st.idx[r][lane] = (uint8_t) i;
+                }
+            } else {
+                st.idx[0][lane] = 0;
+                for (int i = 1; i < SB; ++i) {
+                    const float k = st.x[i][lane];
+                    int j = i - 1;
+                    while (j >= 0 && st.x[st.idx[j][lane]][lane] > k) { st.idx[j + 1][lane] = st.idx[j][lane]; --j; }
+                    st.idx[j + 1][lane] = (uint8_t) i;
+                }
             }
             float best = -FLT_MAX;
             int b1 = -1, b2 = -1;
