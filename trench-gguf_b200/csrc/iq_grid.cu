@@ -543,8 +543,34 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
         }
     }
     __syncwarp();
-    // ---- P9: super-block scale and the block bytes (lane 0), then a coalesced store
-    if (lane == 0) {
+    // ---- P9: super-block scale and the block bytes, then a coalesced store. IQ2_XXS: lane 0 the super-block scale
+    //      (ggml's max in sub-block order), one lane a sub-block its 8 bytes; the other types: lane 0 all of it
+    if constexpr (T == IQ2_XXS) {
+        if (lane == 0) {
+            float max_scale = 0;
+            for (int s = 0; s < S::NSUB; ++s) if (!st.skip[s]) max_scale = fmaxr(max_scale, st.scale[s]);
+            st.sigma2 = max_scale;   // (sigma2 is dead: it carries the max to the other lanes)
+        }
+        __syncwarp();
+        const float max_scale = st.sigma2;
+        uint8_t * y = st.u.out;
+        if (lane < S::NSUB) {
+            const int s = lane;
+            uint32_t q0 = 0, q1 = 0;
+            if (max_scale) {
+                const float d = max_scale / 31;
+                const float idd = 1 / d;
+                if (!st.skip[s]) {
+                    for (int k = 0; k < 4; ++k) { q0 |= (uint32_t) st.gidx[s][k] << (8 * k); q1 |= (uint32_t) st.signs[s][k] << (7 * k); }
+                }
+                q1 |= (uint32_t) imax(0, imin(15, nearest_int(0.5f * (idd * st.scale[s] - 1)))) << 28;
+                if (s == 0) { const uint16_t h = half_bits(d); y[0] = h & 255; y[1] = h >> 8; }
+            } else if (s == 0) {
+                y[0] = y[1] = 0;
+            }
+            for (int j = 0; j < 4; ++j) { y[2 + 8 * s + j] = (q0 >> (8 * j)) & 255; y[6 + 8 * s + j] = (q1 >> (8 * j)) & 255; }
+        }
+    } else if (lane == 0) {
         uint8_t * y = st.u.out;
         for (int i = 0; i < block_bytes(T); ++i) y[i] = 0;
         float max_scale = 0;
@@ -552,20 +578,7 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
         const float d = max_scale / 31;
         const float idd = 1 / d;
         auto scale4 = [&](int s) { return imax(0, imin(15, nearest_int(0.5f * (idd * st.scale[s] - 1)))); };
-        if constexpr (T == IQ2_XXS) {
-            if (max_scale) {
-                const uint16_t h = half_bits(d);
-                y[0] = h & 255; y[1] = h >> 8;
-                for (int s = 0; s < 8; ++s) {
-                    uint32_t q0 = 0, q1 = 0;
-                    if (!st.skip[s]) {
-                        for (int k = 0; k < 4; ++k) { q0 |= (uint32_t) st.gidx[s][k] << (8 * k); q1 |= (uint32_t) st.signs[s][k] << (7 * k); }
-                    }
-                    q1 |= (uint32_t) scale4(s) << 28;
-                    for (int j = 0; j < 4; ++j) { y[2 + 8 * s + j] = (q0 >> (8 * j)) & 255; y[6 + 8 * s + j] = (q1 >> (8 * j)) & 255; }
-                }
-            }
-        } else if constexpr (T == IQ2_XS) {
+        if constexpr (T == IQ2_XS) {
             if (max_scale) {
                 const uint16_t h = half_bits(d);
                 y[0] = h & 255; y[1] = h >> 8;
