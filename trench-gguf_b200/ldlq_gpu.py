@@ -109,7 +109,7 @@ def prepare_hessian_torch(H, n, damp=0.01, order="seq", bs=QK, device="cuda", ou
     else:
         blk_order = torch.arange(nblk, device=device)
     perm = (blk_order[:, None] * bs + torch.arange(bs, device=device)[None]).reshape(-1)
-    Hp64 = Hn[perm][:, perm]
+    Hp64 = Hn[perm][:, perm] if order == "act" else Hn   # (the sequential order's permutation is the identity)
     mean_d = float(torch.diagonal(Hp64).mean())
 
     def factor(dtype, extra):
