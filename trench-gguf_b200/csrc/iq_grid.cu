@@ -112,6 +112,7 @@ __device__ float qp_trial_mse(int k, int nmax, float mx, const float * x, const 
     const float iscale = (k == 0 ? (float) nmax : 0.1f * is + nmax) / mx;
     const float scale = 1 / iscale;
     float mse = 0;
+#pragma unroll 1
     for (int i = 0; i < N; ++i) {
         const int r = nearest_int(iscale * x[i]);
         const int l = k == 0 ? (r & 255) : imin(nmax, r);
@@ -289,6 +290,7 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
     if (lane == 0) {
         float s2 = 0;
         const float4 * x2 = reinterpret_cast<const float4 *>(st.u.x2);
+#pragma unroll 1
         for (int e = 0; e < QK / 4; ++e) { const float4 v = x2[e]; s2 += v.x; s2 += v.y; s2 += v.z; s2 += v.w; }
         st.sigma2 = P::SIGMA_X2 ? 2 * s2 / QK : s2 / QK;
     }
@@ -333,6 +335,7 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
     if (lane < S::NSUB) {
         const float * xv = st.xv + lane * S::PAD;
         float mx = xv[0], qm = fmaxr(0.f, xv[0]);   // (make_qp_quants' own max starts at 0)
+#pragma unroll 1
         for (int i = 1; i < P::SB; ++i) { mx = fmaxr(mx, xv[i]); qm = fmaxr(qm, xv[i]); }
         st.qmax[lane] = qm;
         const int skip = P::EPS_ZERO ? !mx : mx < P::EPS;
@@ -357,6 +360,7 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
             const float * ws = st.w + lane * S::PAD;
             const float iscale = qp_iscale(NMAX, st.qmax[lane], st.u.qp.mse[lane]);
             float sumlx = 0, suml2 = 0;
+#pragma unroll 1
             for (int i = 0; i < 32; ++i) {
                 const int l = imin(NMAX, nearest_int(iscale * xs[i]));
                 sumlx += ws[i] * xs[i] * l;
@@ -366,6 +370,7 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
             st.u.qp.sums[lane][1] = suml2;
         }
         __syncwarp();
+#pragma unroll 1
         for (int s = 0; s < S::NSUB; ++s) {
             if (st.skip[s]) continue;
             const float qm = st.qmax[s];
@@ -450,6 +455,7 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
             }
         }
         __syncwarp();
+#pragma unroll 1
         for (int r = 0; r < nr; ++r) {                                          // M
             const int task = (rb + r) * 32 + lane;
             if (task >= S::NTASK) continue;
@@ -458,6 +464,7 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
             if (!st.skip[s]) {
                 const float * xs = st.xv + s * S::PAD;
                 const float * w = st.w + s * S::PAD;
+#pragma unroll 1
                 for (int g = 0; g < S::NG; ++g) {
                     const uint32_t lev = st.t_lev[task][g];
 #pragma unroll
@@ -482,11 +489,13 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
         if (!st.skip[s]) {
             float scale = st.scale[s], best = 0;
             int win = -1;
+#pragma unroll 1
             for (int t = 0; t < S::NT; ++t) {
                 const float sqx = st.t_sqx[s * S::NT + t], sq2 = st.t_sq2[s * S::NT + t];
                 if (sq2 > 0 && sqx * sqx > best * sq2) { scale = sqx / sq2; best = scale * sqx; win = t; }
             }
             unsigned on = P::INIT_ON ? ALL : 0u;
+#pragma unroll 1
             for (int g = 0; g < S::NG; ++g) st.lev[s][g] = win >= 0 ? st.t_lev[s * S::NT + win][g] : 0;
             if (win >= 0) on = st.t_on[s * S::NT + win];
             const int n_off = __popc(~on & ALL);
@@ -520,6 +529,7 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
                 const float * xs = st.xv + s * S::PAD;
                 const float * w = st.w + s * S::PAD;
                 float sqx = 0, sq2 = 0;
+#pragma unroll 1
                 for (int e = 0; e < P::SB; ++e) {
                     const float q = odd_level(level_of<P::GD>(st.lev[s][e / P::GD], e % P::GD));
                     sqx += w[e] * xs[e] * q;
@@ -532,6 +542,7 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
                 for (int k = 0; k < S::NSG; ++k)
                     st.signs[s][k] = (uint8_t) (P::PARITY ? (~st.signs[s][k]) & 127 : (uint8_t) ~st.signs[s][k]);
             }
+#pragma unroll 1
             for (int g = 0; g < S::NG; ++g) {
                 const int gi = __ldg(tab.code3 + code3_of<P::GD>(st.lev[s][g]));
                 if (gi < 0) atomicOr(status, ST_OFF_GRID);
@@ -548,6 +559,7 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
     if constexpr (T == IQ2_XXS) {
         if (lane == 0) {
             float max_scale = 0;
+#pragma unroll 1
             for (int s = 0; s < S::NSUB; ++s) if (!st.skip[s]) max_scale = fmaxr(max_scale, st.scale[s]);
             st.sigma2 = max_scale;   // (sigma2 is dead: it carries the max to the other lanes)
         }
@@ -561,6 +573,7 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
                 const float d = max_scale / 31;
                 const float idd = 1 / d;
                 if (!st.skip[s]) {
+#pragma unroll 1
                     for (int k = 0; k < 4; ++k) { q0 |= (uint32_t) st.gidx[s][k] << (8 * k); q1 |= (uint32_t) st.signs[s][k] << (7 * k); }
                 }
                 q1 |= (uint32_t) imax(0, imin(15, nearest_int(0.5f * (idd * st.scale[s] - 1)))) << 28;
@@ -568,12 +581,14 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
             } else if (s == 0) {
                 y[0] = y[1] = 0;
             }
+#pragma unroll 1
             for (int j = 0; j < 4; ++j) { y[2 + 8 * s + j] = (q0 >> (8 * j)) & 255; y[6 + 8 * s + j] = (q1 >> (8 * j)) & 255; }
         }
     } else if (lane == 0) {
         uint8_t * y = st.u.out;
         for (int i = 0; i < block_bytes(T); ++i) y[i] = 0;
         float max_scale = 0;
+#pragma unroll 1
         for (int s = 0; s < S::NSUB; ++s) if (!st.skip[s]) max_scale = fmaxr(max_scale, st.scale[s]);
         const float d = max_scale / 31;
         const float idd = 1 / d;
