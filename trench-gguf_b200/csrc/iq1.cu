@@ -116,6 +116,7 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
     // ---- sumx2 in index order, one lane a super-block
     if (lane < NSB) {
         float s2 = 0;
+#pragma unroll 16
         for (int e = 0; e < QK; ++e) { const float v = st.x[e % SB][lane * NSUB + e / SB]; s2 += v * v; }
         st.sigma2[lane] = 2 * s2 / QK;
     }
@@ -140,6 +141,7 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
     bool dropped = true;
     if (live) {
         float mx = fabsf(st.x[0][lane]);
+#pragma unroll 1
         for (int i = 1; i < SB; ++i) mx = fmaxr(mx, fabsf(st.x[i][lane]));
         if (!(mx < IQ1<T>::EPS)) {
             // the stable ascending order of the weights (the reference's insertion sort, gpuq.hip:236-243: ties keep
@@ -164,6 +166,7 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
                 }
             } else {
                 st.idx[0][lane] = 0;
+#pragma unroll 1
                 for (int i = 1; i < SB; ++i) {
                     const float k = st.x[i][lane];
                     int j = i - 1;
@@ -178,6 +181,7 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
                 st.u.p.px[0][lane] = 0.f;
                 st.u.p.pw[0][lane] = 0.f;
                 float sx = 0.f, sw = 0.f;
+#pragma unroll 1
                 for (int j = 0; j < SB; ++j) {
                     const int i = st.idx[j][lane];
                     const float wi = st.w[i][lane];
@@ -256,6 +260,7 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
             }
             if (b1 >= 0) {
                 dropped = false;
+#pragma unroll 1
                 for (int j = 0; j < SB; ++j) lv |= (uint64_t) (j < b1 ? 0 : j < b2 ? 1 : 2) << (2 * st.idx[j][lane]);
                 if (scale < 0) {
                     lv = (0xAAAAAAAAAAAAAAAAull >> (64 - 2 * SB)) - lv;   // every level l -> 2 - l (no borrows)
@@ -317,6 +322,7 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
     if (!dropped) {
         if (!all_on) {
             float sqx = 0, sq2 = 0;
+#pragma unroll 1
             for (int g = 0; g < W::NG; ++g) {
                 const bool minus = minus_of<T>(bk, g);
                 const uint32_t lev = __ldg(tab.glev + st.gidx[g][lane]);
@@ -359,6 +365,7 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
     if (lane < nb) {
         const float * scl = st.scales + lane * NSUB;
         float max_scale = 0;
+#pragma unroll 1
         for (int ib = 0; ib < NSUB; ++ib) if (!st.dropped[lane * NSUB + ib]) max_scale = fmaxr(max_scale, scl[ib]);
         st.msc[lane] = max_scale;
     }
@@ -396,6 +403,7 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
                 const uint16_t hd = half_bits(d * 1.125f);
                 y[0] = hd & 255; y[1] = hd >> 8;
                 const float id = 1 / d;
+#pragma unroll 1
                 for (int ib = 0; ib < 8; ++ib) {
                     int l = imax(0, imin(7, nearest_int(0.5f * (id * scl[ib] - 1))));
                     if (st.shifts[lane * NSUB + ib] == -1) l |= 8;
