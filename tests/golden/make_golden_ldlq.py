@@ -1,6 +1,6 @@
 """Writes tests/golden/ldlq_golden.npz: the reference's own LDLQ loop on a small case.
 
-Imports trench-gguf's tools/ldlq.py (REF=<checkout>, default /root/reference) and runs its prepare_hessian and
+Imports trench-gguf's tools/ldlq.py (REF=<trench-gguf checkout>) and runs its prepare_hessian and
 quantize_matrix with the block quantizer / dequantizer bound to the reference's own block functions compiled for
 the host (oracle/_ref). Stores the inputs (W, H, n, imatrix) and the outputs (bytes and proxy losses of plain
 rounding and of feedback) for IQ2_XXS and IQ1_M. The fixture pins oracle/ldlq_oracle.py (CPU tests) and the GPU
