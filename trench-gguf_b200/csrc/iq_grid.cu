@@ -290,7 +290,7 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
     if (lane == 0) {
         float s2 = 0;
         const float4 * x2 = reinterpret_cast<const float4 *>(st.u.x2);
-#pragma unroll 1
+#pragma unroll 8
         for (int e = 0; e < QK / 4; ++e) { const float4 v = x2[e]; s2 += v.x; s2 += v.y; s2 += v.z; s2 += v.w; }
         st.sigma2 = P::SIGMA_X2 ? 2 * s2 / QK : s2 / QK;
     }
