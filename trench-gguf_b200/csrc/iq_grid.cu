@@ -529,7 +529,7 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
                 const float * xs = st.xv + s * S::PAD;
                 const float * w = st.w + s * S::PAD;
                 float sqx = 0, sq2 = 0;
-#pragma unroll 1
+#pragma unroll 4
                 for (int e = 0; e < P::SB; ++e) {
                     const float q = odd_level(level_of<P::GD>(st.lev[s][e / P::GD], e % P::GD));
                     sqx += w[e] * xs[e] * q;
