@@ -196,3 +196,22 @@ def test_argument_errors(gpuq):
     assert L.gpuq_quantize(99, x.ctypes.data, y.ctypes.data, 2, 256, None) == 0
     assert L.gpuq_requantize(16, x.ctypes.data, 8, y.ctypes.data, 2, 256, None) == 0          # F16? no: src 16
     assert L.gpuq_can_quantize(16, 0) == 0 and L.gpuq_can_quantize(16, 1) == 1 and L.gpuq_can_quantize(12, 0) == 1
+
+
+@pytest.mark.gpu
+def test_nonfinite_inputs(gpuq, oracle):
+    """NaN / +-inf weights: the bytes of every type whose searches still find a finite candidate equal the oracle's
+    (which equals the reference build, tests/test_oracle.py); the others - where the reference traps - return 0 with
+    a reason, and the next call on the device works"""
+    import gpuq as G
+    from test_oracle import NONFINITE_FAIL, NONFINITE_OK, nonfinite_inputs
+    x, im = nonfinite_inputs()
+    for name in NONFINITE_OK:
+        t = TYPES[name]
+        assert np.array_equal(gpuq.quantize(t, x, im[None]), oracle.quantize(t, x, im[None])), name
+    ok = np.nan_to_num(x, nan=0.0, posinf=0.0, neginf=0.0)
+    for name in NONFINITE_FAIL:
+        t = TYPES[name]
+        with pytest.raises(G.GpuqError, match="status"):
+            gpuq.quantize(t, x, im[None])
+        assert np.array_equal(gpuq.quantize(t, ok, im[None]), oracle.quantize(t, ok, im[None])), name

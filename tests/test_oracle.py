@@ -108,3 +108,31 @@ def test_oracle_device_addressing_matches_reference(oracle, reference):
     for t in (16, 29, 23):
         a = oracle.quantize_blocks(t, x, qw, 12, 4)
         assert np.array_equal(a, reference.quantize_blocks(t, x, qw, 12, 4))
+
+
+# non-finite weights (NaN, +-inf in a few super-blocks): the types whose searches still find a finite candidate
+# produce bytes, the others have no finite neighbour distance, where the reference traps and the oracle fails
+NONFINITE_OK = ["IQ2_XXS", "IQ1_S", "IQ1_M", "IQ4_NL", "IQ4_XS", "Q8_0", "Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K"]
+NONFINITE_FAIL = ["IQ2_XS", "IQ2_S", "IQ3_XXS", "IQ3_S"]
+
+
+def nonfinite_inputs():
+    rng = np.random.default_rng(5)
+    x = (rng.standard_normal((4, 512)) * 0.02).astype(np.float32)
+    x[0, 3] = np.nan
+    x[1, 300] = np.nan
+    x[2, 17] = np.inf
+    x[3, 40] = -np.inf
+    return x, rng.gamma(1.0, 1.0, 512).astype(np.float32)
+
+
+@pytest.mark.parametrize("name", NONFINITE_OK + NONFINITE_FAIL)
+def test_oracle_nonfinite_matches_reference(oracle, reference, name):
+    x, im = nonfinite_inputs()
+    t = TYPES[name]
+    if name in NONFINITE_OK:
+        assert np.array_equal(oracle.quantize(t, x, im[None]), reference.quantize(t, x, im[None]))
+    else:
+        for c in (oracle, reference):
+            with pytest.raises(RuntimeError):
+                c.quantize(t, x, im[None])
