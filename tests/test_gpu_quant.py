@@ -200,15 +200,28 @@ def test_argument_errors(gpuq):
 
 @pytest.mark.gpu
 def test_nonfinite_inputs(gpuq, oracle):
-    """NaN / +-inf weights: the bytes of every type whose searches still find a finite candidate equal the oracle's
-    (which equals the reference build, tests/test_oracle.py); the others - where the reference traps - return 0 with
-    a reason, and the next call on the device works"""
+    """NaN / +-inf weights. For every type whose searches still find a finite candidate the call succeeds and every
+    block whose 32 or 256 weights are all finite equals the oracle's (which equals the reference build,
+    tests/test_oracle.py); IQ2_XXS, IQ1_S and IQ1_M equal it in every block. The bytes of a block that holds a
+    NaN or an infinity are not compared for the other types: they depend on the platform, not on the algorithm.
+    x86 makes the NaN of an invalid operation (inf * 0, inf - inf) negative and turns a NaN into INT_MIN when it
+    converts it to int; the GPU (and AArch64) make it positive and turn it into 0, so ggml's own C code writes
+    different fp16 scales (0xFE00 against 0x7E00) and levels for such blocks on an x86 and on an AArch64 host. The other types -
+    where the reference traps - return 0 with a reason, and the next call on the device works"""
     import gpuq as G
-    from test_oracle import NONFINITE_FAIL, NONFINITE_OK, nonfinite_inputs
+    from test_oracle import NONFINITE_EXACT, NONFINITE_FAIL, NONFINITE_OK, nonfinite_inputs
     x, im = nonfinite_inputs()
     for name in NONFINITE_OK:
         t = TYPES[name]
-        assert np.array_equal(gpuq.quantize(t, x, im[None]), oracle.quantize(t, x, im[None])), name
+        got, want = gpuq.quantize(t, x, im[None]), oracle.quantize(t, x, im[None])
+        if name in NONFINITE_EXACT:
+            assert np.array_equal(got, want), name
+            continue
+        nb = x.size // G.BLOCK_LEN[t]
+        finite = np.isfinite(x.reshape(nb, -1)).all(1)
+        assert 0 < finite.sum() < nb
+        got, want = got.reshape(nb, -1), want.reshape(nb, -1)
+        assert np.array_equal(got[finite], want[finite]), name
     ok = np.nan_to_num(x, nan=0.0, posinf=0.0, neginf=0.0)
     for name in NONFINITE_FAIL:
         t = TYPES[name]

@@ -114,6 +114,7 @@ def test_oracle_device_addressing_matches_reference(oracle, reference):
 # produce bytes, the others have no finite neighbour distance, where the reference traps and the oracle fails
 NONFINITE_OK = ["IQ2_XXS", "IQ1_S", "IQ1_M", "IQ4_NL", "IQ4_XS", "Q8_0", "Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K"]
 NONFINITE_FAIL = ["IQ2_XS", "IQ2_S", "IQ3_XXS", "IQ3_S"]
+NONFINITE_EXACT = ["IQ2_XXS", "IQ1_S", "IQ1_M"]
 
 
 def nonfinite_inputs():
