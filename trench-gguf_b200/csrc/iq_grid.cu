@@ -75,6 +75,14 @@ template <int T> struct alignas(16) WarpState {
     struct QP {                                       // make_qp_quants (IQ2_XXS)
         float mse[S::NSUB][9];                        // trial errors
         float sums[S::NSUB][2];                       // sumlx, suml2 at the chosen trial scale
+        float isc[S::NSUB];                           // the chosen inverse scale
+        float res[S::NSUB];                           // the descent's scale, where it ran
+    };
+    struct Regrid {                                   // the re-grid's searches, split into runs
+        int m[32];                                    // a search's code3 entry (its lane)
+        uint16_t owner[32];                           // a run's search lane | run index << 5
+        float bd[32];                                 // a run's best distance and entry
+        uint32_t be[32];
     };
     struct Sched {                                    // one batch of trial rounds
         uint16_t perm[(S::RB * 32 < S::NTASK ? S::RB * 32 : S::NTASK) * S::NG];   // the batch's searches, longest first
@@ -85,6 +93,7 @@ template <int T> struct alignas(16) WarpState {
         float x2[QK];                                 // x*x, for sumx2
         QP qp;
         Sched sch;
+        Regrid rg;
         uint8_t out[112];                             // the block's bytes (after the trials)
     } u;
     float w[S::NSUB * S::PAD], wa[S::NSUB * S::PAD], xv[S::NSUB * S::PAD];
@@ -129,24 +138,35 @@ __device__ float qp_trial_mse(int k, int nmax, float mx, const float * x, const 
 // against the current sums at once and the first lane whose test passes is the next change - ggml's sequential
 // pass exactly, in (changes + 1) rounds. sumlx and suml2 enter from the index-order sums of the signed levels,
 // while L holds them as ggml's uint8_t array does (a negative level, from the one sign-flipped weight of an odd
-// group, wraps), exactly as the reference's pass reads them. Returns the scale.
-__device__ float qp_descent_warp(int lane, int nmax, float mx, float x, float w, const float * mse, float sumlx,
-                                 float suml2, int L) {
+// group, wraps), exactly as the reference's pass reads them.
+//
+// One element's test (gpuq.hip:156-170): its level against the current sums with itself taken out, and whether
+// ggml takes the new level (the sums with it put back in are returned for that case).
+__device__ __forceinline__ bool qp_try(int nmax, float x, float w, int L, float sumlx, float suml2, bool on, int & nl,
+                                       float & slx, float & sl2) {
+    slx = sumlx - w * x * L;
+    sl2 = suml2 - w * L * L;
+    nl = L;
+    bool acc = false;
+    if (on && slx > 0 && sl2 > 0) {
+        nl = imin(nmax, nearest_int(x * sl2 / slx));
+        if (nl != L) {
+            slx += w * x * nl;
+            sl2 += w * nl * nl;
+            acc = slx * slx * suml2 > sumlx * sumlx * sl2;
+        }
+    }
+    return acc;
+}
+
+// The whole descent of one sub-block; returns the scale.
+__device__ float qp_descent_warp(int lane, int nmax, float x, float w, float sumlx, float suml2, int L) {
     for (int pass = 0; pass < 5; ++pass) {
         int changed = 0, from = 0;
         for (;;) {
-            float slx = sumlx - w * x * L;
-            float sl2 = suml2 - w * L * L;
-            int nl = L;
-            bool acc = false;
-            if (lane >= from && slx > 0 && sl2 > 0) {
-                nl = imin(nmax, nearest_int(x * sl2 / slx));
-                if (nl != L) {
-                    slx += w * x * nl;
-                    sl2 += w * nl * nl;
-                    acc = slx * slx * suml2 > sumlx * sumlx * sl2;
-                }
-            }
+            float slx, sl2;
+            int nl;
+            const bool acc = qp_try(nmax, x, w, L, sumlx, suml2, lane >= from, nl, slx, sl2);
             const unsigned hit = __ballot_sync(0xFFFFFFFFu, acc);
             if (!hit) break;
             const int f = __ffs(hit) - 1;
@@ -228,14 +248,13 @@ __device__ __forceinline__ uint32_t search_lane8(int m, const float * xv, const 
     return bl == NONE ? NONE : (bl & 0xFFFFu);
 }
 
-// the 4-d grids: one lane's own search (lists of 2..38 points), ggml's distance and first-minimum rule
-// (iq3_find_best_neighbour, gpuq.hip:972-992)
-__device__ uint32_t search_lane4(int m, const float * xv, const float * wa, float s, const SearchTab & tab) {
-    const uint32_t * lst = tab.neigh + list_off(m);
-    const int n = list_cnt(m);
-    float best = FLT_MAX;
+// the 4-d grids: cnt consecutive entries of a list (lists of 2..38 points), ggml's distance and first-minimum rule
+// (iq3_find_best_neighbour, gpuq.hip:972-992). Returns the winning entry (NONE if none is below FLT_MAX), its
+// distance in best.
+__device__ uint32_t search_run4(const uint32_t * lst, int cnt, const float * xv, const float * wa, float s, float & best) {
+    best = FLT_MAX;
     uint32_t bl = NONE;
-    for (int j = 1; j <= n; ++j) {
+    for (int j = 0; j < cnt; ++j) {
         const uint32_t e = __ldg(lst + j);
         float d2 = 0.f;
 #pragma unroll
@@ -245,21 +264,26 @@ __device__ uint32_t search_lane4(int m, const float * xv, const float * wa, floa
         }
         if (d2 < best) { best = d2; bl = e; }
     }
+    return bl;
+}
+__device__ uint32_t search_lane4(int m, const float * xv, const float * wa, float s, const SearchTab & tab) {
+    float best;
+    const uint32_t bl = search_run4(tab.neigh + list_off(m) + 1, list_cnt(m), xv, wa, s, best);
     return bl == NONE ? NONE : (bl & 0xFFFFu);
 }
 
-// A group's levels at inverse scale id / scale s: the rounding when on the grid, else the neighbour search
-// (warp-collective for the 8-d grids: every lane calls it).
-template <int T>
-__device__ __forceinline__ uint32_t group_levels(WarpState<T> & st, int lane, bool active, const float * xv,
-                                                 const float * wa, float id, float s, const SearchTab & tab, unsigned * on) {
-    using P = GT<T>;
-    int m = 0;
-    uint32_t lev = 0;
-    if (active) lev = round_group<P::GD, P::KMAXQ>(xv, id, tab, &m);
-    *on = active && m >= 0;
-    if (active && m < 0) lev = P::GD == 8 ? search_lane8(m, xv, wa, s, tab) : search_lane4(m, xv, wa, s, tab);
-    return lev;
+// cnt entries of a list from lst, either grid; the terms of the 8-d grids formed here
+template <int GD>
+__device__ __forceinline__ uint32_t search_run(const uint32_t * lst, int cnt, const float * xv, const float * wa, float s,
+                                               float & best) {
+    if constexpr (GD == 8) {
+        float t0[8], t1[8], t2[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) level_terms(wa[i], xv[i], s, 1.f, 3.f, 5.f, t0[i], t1[i], t2[i]);
+        return search_run8(lst, cnt, t0, t1, t2, best);
+    } else {
+        return search_run4(lst, cnt, xv, wa, s, best);
+    }
 }
 
 // ------------------------------------------------------------------------------------------------ the kernel
@@ -352,39 +376,60 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
             st.u.qp.mse[s][k] = qp_trial_mse<P::SB>(k, NMAX, st.qmax[s], st.xv + s * S::PAD, st.w + s * S::PAD);
         }
         __syncwarp();
-        // the levels at the chosen inverse scale and their sums in index order (one lane a sub-block); then the
-        // coordinate descent, one sub-block at a time with the lanes over its elements
-        static_assert(P::SB == 32, "one lane an element");
-        if (lane < S::NSUB && !st.skip[lane] && !(st.qmax[lane] < 1e-15f)) {
-            const float * xs = st.xv + lane * S::PAD;
-            const float * ws = st.w + lane * S::PAD;
-            const float iscale = qp_iscale(NMAX, st.qmax[lane], st.u.qp.mse[lane]);
-            float sumlx = 0, suml2 = 0;
-#pragma unroll 1
-            for (int i = 0; i < 32; ++i) {
-                const int l = imin(NMAX, nearest_int(iscale * xs[i]));
-                sumlx += ws[i] * xs[i] * l;
-                suml2 += ws[i] * l * l;
+        // the chosen inverse scale and the two sums at it in index order (sumlx on lanes 0..7, suml2 on lanes
+        // 8..15, one sub-block a lane): both are (w * y) * l, y = x or l
+        static_assert(P::SB == 32 && S::NSUB == 8, "one lane an element, 16 sum lanes");
+        if (lane < 2 * S::NSUB) {
+            const int s = lane & 7, which = lane >> 3;
+            if (!st.skip[s] && !(st.qmax[s] < 1e-15f)) {
+                const float * xs = st.xv + s * S::PAD;
+                const float * ws = st.w + s * S::PAD;
+                const float iscale = qp_iscale(NMAX, st.qmax[s], st.u.qp.mse[s]);
+                if (!which) st.u.qp.isc[s] = iscale;
+                float sum = 0;
+#pragma unroll 4
+                for (int i = 0; i < 32; ++i) {
+                    const float l = (float) imin(NMAX, nearest_int(iscale * xs[i]));
+                    sum += ws[i] * (which ? l : xs[i]) * l;
+                }
+                st.u.qp.sums[s][which] = sum;
             }
-            st.u.qp.sums[lane][0] = sumlx;
-            st.u.qp.sums[lane][1] = suml2;
         }
         __syncwarp();
+        // the descent, lanes over the 32 elements: the first pass's first test of every sub-block at once; a
+        // sub-block where no element changes is done (almost all of them), the others run the whole descent
+        unsigned moved = 0;
 #pragma unroll 1
         for (int s = 0; s < S::NSUB; ++s) {
-            if (st.skip[s]) continue;
-            const float qm = st.qmax[s];
+            if (st.skip[s] || st.qmax[s] < 1e-15f) continue;
+            const float x = st.xv[s * S::PAD + lane], w = st.w[s * S::PAD + lane];
+            const int L = imin(NMAX, nearest_int(st.u.qp.isc[s] * x)) & 255;
+            float slx, sl2;
+            int nl;
+            if (__ballot_sync(0xFFFFFFFFu, qp_try(NMAX, x, w, L, st.u.qp.sums[s][0], st.u.qp.sums[s][1], true, nl, slx, sl2)))
+                moved |= 1u << s;
+        }
+#pragma unroll 1
+        for (int s = 0; s < S::NSUB; ++s) {
+            if (!(moved & (1u << s))) continue;
+            const float x = st.xv[s * S::PAD + lane], w = st.w[s * S::PAD + lane];
+            const int L = imin(NMAX, nearest_int(st.u.qp.isc[s] * x)) & 255;
+            const float scale = qp_descent_warp(lane, NMAX, x, w, st.u.qp.sums[s][0], st.u.qp.sums[s][1], L);
+            if (lane == 0) st.u.qp.res[s] = scale;
+        }
+        __syncwarp();
+        if (lane < S::NSUB && !st.skip[lane]) {
+            const int s = lane;
             float scale = 0.f;
-            if (!(qm < 1e-15f)) {
-                const float x = st.xv[s * S::PAD + lane], w = st.w[s * S::PAD + lane];
-                const int l = imin(NMAX, nearest_int(qp_iscale(NMAX, qm, st.u.qp.mse[s]) * x));
-                scale = qp_descent_warp(lane, NMAX, qm, x, w, st.u.qp.mse[s], st.u.qp.sums[s][0], st.u.qp.sums[s][1], l & 255);
+            if (moved & (1u << s)) {
+                scale = st.u.qp.res[s];
+            } else if (!(st.qmax[s] < 1e-15f)) {
+                const float sumlx = st.u.qp.sums[s][0], suml2 = st.u.qp.sums[s][1];
+                scale = suml2 > 0.0f ? sumlx / suml2 : 0.0f;
             }
-            if (lane == 0) {
-                st.scale[s] = scale;
-                st.denom[s] = scale * P::KMAXQ;
-                if (!(scale * P::KMAXQ > 0)) st.skip[s] = 1;
-            }
+            st.scale[s] = scale;
+            st.denom[s] = scale * P::KMAXQ;
+            if (!(scale * P::KMAXQ > 0)) st.skip[s] = 1;
         }
         __syncwarp();
     }
@@ -505,15 +550,47 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
         st.regrid[s] = rg;
     }
     __syncwarp();
-    // ---- P7: snap the chosen groups again with the final scale, one (sub-block, group) a lane
+    // ---- P7: snap the chosen groups again with the final scale, one (sub-block, group) a lane. The 8-d searches of
+    //      a round are split into at most 32 runs of about equal length, one a lane, and each search takes the first
+    //      strict minimum over its runs in list order (the same candidates and distances as one lane's whole list)
+    auto & rg = st.u.rg;
     for (int r0 = 0; r0 < S::NRG; r0 += 32) {
         const int r = r0 + lane;
         const int s = r < S::NRG ? r / S::NG : 0, g = r - s * S::NG;
         const bool act = r < S::NRG && (st.regrid[s] & (1u << g));
         const float scale = act ? st.scale[s] : 1.f;
-        unsigned on;
-        uint32_t lev = group_levels<T>(st, lane, act, st.xv + s * S::PAD + g * P::GD, st.wa + s * S::PAD + g * P::GD,
-                                       1 / scale, scale, tab, &on);
+        int m = 0;
+        uint32_t lev = 0;
+        if (act) lev = round_group<P::GD, P::KMAXQ>(st.xv + s * S::PAD + g * P::GD, 1 / scale, tab, &m);
+        const int n = act && m < 0 ? list_cnt(m) : 0;
+        if constexpr (P::GD == 4) {   // (the 4-d lists are short: one lane a list)
+            if (n) lev = search_lane4(m, st.xv + s * S::PAD + g * P::GD, st.wa + s * S::PAD + g * P::GD, scale, tab);
+        }
+        int run = 0, first = 0, nrun = 0;
+        const int nruns = P::GD == 8 ? split_runs(n, lane, &run, &first, &nrun) : 0;
+        if (nruns) {
+            rg.m[lane] = m;
+            for (int c = 0; c < nrun; ++c) rg.owner[first + c] = (uint16_t) (lane | (c << 5));
+            __syncwarp();
+            if (lane < nruns) {
+                const int o = rg.owner[lane], ol = o & 31, c = o >> 5;
+                const int orr = r0 + ol, os = orr / S::NG, og = orr - os * S::NG;
+                const int om = rg.m[ol], j0 = c * run, cnt = imin(list_cnt(om), j0 + run) - j0;
+                float bd;
+                rg.be[lane] = search_run<P::GD>(tab.neigh + list_off(om) + 1 + j0, cnt, st.xv + os * S::PAD + og * P::GD,
+                                                st.wa + os * S::PAD + og * P::GD, st.scale[os], bd);
+                rg.bd[lane] = bd;
+            }
+            __syncwarp();
+            if (n) {
+                float best = FLT_MAX;
+                uint32_t bl = NONE;
+                for (int c = 0; c < nrun; ++c)
+                    if (rg.bd[first + c] < best) { best = rg.bd[first + c]; bl = rg.be[first + c]; }
+                lev = bl == NONE ? NONE : (bl & 0xFFFFu);
+            }
+            __syncwarp();
+        }
         if (act) {
             if (lev == NONE) { atomicOr(status, ST_NO_NEIGHBOUR); lev = 0; }
             st.lev[s][g] = (uint16_t) lev;

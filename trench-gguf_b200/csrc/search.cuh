@@ -54,24 +54,62 @@ __device__ __forceinline__ float cand_dist(uint32_t e, const float (&t0)[8], con
     return d2;
 }
 
-// one lane's whole list (code3 entry m < 0): the first strict minimum of ggml's distance in list order, the next
-// entry loaded one step ahead. Returns the winning entry, NONE if no distance is finite.
+// one lane's run over cnt consecutive entries of a list (lst: the first of them): the first strict minimum of
+// ggml's distance in list order, the next entry loaded one step ahead. Returns the winning entry (NONE if no
+// distance is below FLT_MAX) and its distance in best.
 template <bool PRED = true>
-__device__ __forceinline__ uint32_t search_list8(int m, const float (&t0)[8], const float (&t1)[8], const float (&t2)[8],
-                                                 const SearchTab & tab) {
-    const uint32_t * lst = tab.neigh + list_off(m) + 1;
-    const int n = list_cnt(m);
-    float best = FLT_MAX;
+__device__ __forceinline__ uint32_t search_run8(const uint32_t * lst, int cnt, const float (&t0)[8], const float (&t1)[8],
+                                                const float (&t2)[8], float & best) {
+    best = FLT_MAX;
     uint32_t bl = NONE;
     uint32_t e = __ldg(lst);
 #pragma unroll 2
-    for (int j = 0; j < n; ++j) {
-        const uint32_t en = __ldg(lst + j + 1);   // (one past a list: the next count word or the pad word)
+    for (int j = 0; j < cnt; ++j) {
+        const uint32_t en = __ldg(lst + j + 1);   // (one past a run: the list's next entry, its count word or the pad word)
         const float d2 = cand_dist<PRED>(e, t0, t1, t2);
         if (d2 < best) { best = d2; bl = e; }
         e = en;
     }
     return bl;
+}
+
+// one lane's whole list (code3 entry m < 0). Returns the winning entry, NONE if no distance is finite.
+template <bool PRED = true>
+__device__ __forceinline__ uint32_t search_list8(int m, const float (&t0)[8], const float (&t1)[8], const float (&t2)[8],
+                                                 const SearchTab & tab) {
+    float best;
+    return search_run8<PRED>(tab.neigh + list_off(m) + 1, list_cnt(m), t0, t1, t2, best);
+}
+
+// Warp-collective sums and exclusive prefix sums of one int a lane
+__device__ __forceinline__ int warp_sum(int v) { return (int) __reduce_add_sync(0xFFFFFFFFu, (unsigned) v); }
+__device__ __forceinline__ int warp_excl_prefix(int v, int lane) {
+    int incl = v;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const int u = __shfl_up_sync(0xFFFFFFFFu, incl, d);
+        if (lane >= d) incl += u;
+    }
+    return incl - v;
+}
+
+// Warp-collective split of up to 32 searches (lane i: a list of n >= 0 entries) into at most 32 runs of at most
+// *run entries, a search's runs on consecutive lanes from *first: the smallest run length tried (from the even
+// split up, by quarters) that needs no more than 32 runs. Returns the number of runs; 0 when there is no search.
+__device__ __forceinline__ int split_runs(int n, int lane, int * run, int * first, int * nruns) {
+    const int total = warp_sum(n);
+    if (!total) return 0;
+    int len = (total + 31) / 32, cnt;
+    for (;;) {
+        cnt = warp_sum(n ? (n + len - 1) / len : 0);
+        if (cnt <= 32) break;
+        len += (len + 3) / 4;
+    }
+    const int k = n ? (n + len - 1) / len : 0;
+    *run = len;
+    *nruns = k;
+    *first = warp_excl_prefix(k, lane);
+    return cnt;
 }
 
 // list-length bucket of a search schedule (longest first): exact below 48, then 8 lengths a bucket (lists of 176
