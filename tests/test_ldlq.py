@@ -49,6 +49,22 @@ def test_prepare_hessian_dead_columns_and_act_order():
     assert np.allclose(U, np.triu(U))
 
 
+def test_prepare_hessian_torch_equals_restatement():
+    """ldlq_gpu's factorisation (one Cholesky of the order-reversed matrix and a triangular inverse by halves) gives
+    the restatement's U = cholesky(inverse(cholesky(Hp)))^T in float64, with dead columns and act order"""
+    pytest.importorskip("torch")
+    import ldlq_gpu
+    H, _ = LO.synthetic_hessian(1536, 2048, seed=7)
+    H[11, :] = 0
+    H[:, 11] = 0
+    for order in ("seq", "act"):
+        U0, p0, d0, dead0 = LO.prepare_hessian(H, 2048, order=order)
+        U1, p1, d1, dead1 = ldlq_gpu.prepare_hessian_torch(H, 2048, order=order, device="cpu")
+        assert np.array_equal(p0, p1) and np.array_equal(dead0, dead1) and np.allclose(d0, d1, rtol=1e-12)
+        assert np.abs(U1 - U0).max() <= 1e-10 * np.abs(U0).max()
+        assert np.array_equal(U1, np.triu(U1))
+
+
 # ------------------------------------------------------------------------------------------------ GPU
 def _gpu_setup(tables):
     import torch
@@ -95,6 +111,27 @@ def test_gpu_ldlq_against_reference_loop(tables, oracle, golden, name):
     assert same >= IDENTICAL_MIN
     deq = oracle.dequantize(G.TYPES[name], fb).reshape(W.shape)
     loss, want = ldlq_gpu.proxy_loss(W, deq, H, n), float(gd["%s_loss_fb" % name])
+    assert abs(loss - want) <= LOSS_RTOL * want
+
+
+@pytest.mark.gpu
+def test_gpu_prepare_and_ldlq_against_reference_loop(tables, oracle, golden):
+    """the whole GPU path - the float32 factorisation on the GPU, then the feedback loop - against the restatement's
+    float64 path (its own U): the reference's tolerance"""
+    torch, G, ldlq_gpu, g = _gpu_setup(tables)
+    gd = golden
+    W, H, n, im = gd["W"], gd["H"], int(gd["n"]), gd["imatrix"]
+    gqt = ldlq_gpu.GpuQuant(g, G.TYPES["IQ2_XXS"])
+    dev = torch.device("cuda")
+    U, perm, diag_n, _ = ldlq_gpu.prepare_hessian_torch(torch.from_numpy(H).to(dev), n, device=dev, out="torch")
+    fb = ldlq_gpu.quantize_matrix_torch(torch.from_numpy(W[None].copy()).to(dev), gqt, U=U, perm=perm, diag_n=diag_n,
+                                        imatrix=torch.from_numpy(im[None].copy()).to(dev), weights="imatrix",
+                                        feedback=True, f64=True).cpu().numpy()[0]
+    tsize = gqt.tsize
+    same = (fb.reshape(W.shape[0], -1, tsize) == gd["IQ2_XXS_fb"].reshape(W.shape[0], -1, tsize)).all(-1).mean()
+    assert same >= IDENTICAL_MIN
+    deq = oracle.dequantize(G.TYPES["IQ2_XXS"], fb).reshape(W.shape)
+    loss, want = ldlq_gpu.proxy_loss(W, deq, H, n), float(gd["IQ2_XXS_loss_fb"])
     assert abs(loss - want) <= LOSS_RTOL * want
 
 

@@ -85,6 +85,23 @@ class GpuQuant:
         return f
 
 
+def tri_inv_lower(L, leaf=1024):
+    """Inverse of a lower-triangular matrix by halves: [[A, 0], [B, C]]^-1 = [[A^-1, 0], [-C^-1 B A^-1, C^-1]], the
+    off-diagonal block two GEMMs, the leaves (<= leaf rows) triangular solves against the identity."""
+    import torch
+    m = L.shape[0]
+    if m <= leaf:
+        return torch.linalg.solve_triangular(L, torch.eye(m, dtype=L.dtype, device=L.device), upper=False)
+    h = (m // 2 + QK - 1) // QK * QK
+    Ai = tri_inv_lower(L[:h, :h], leaf)
+    Ci = tri_inv_lower(L[h:, h:], leaf)
+    out = torch.zeros_like(L)
+    out[:h, :h] = Ai
+    out[h:, h:] = Ci
+    out[h:, :h] = -(Ci @ L[h:, :h]) @ Ai
+    return out
+
+
 def prepare_hessian_torch(H, n, damp=0.01, order="seq", bs=QK, device="cuda", out="numpy"):
     """ldlq.py:275-323: normalised, dead columns zeroed, optional act-order block permutation, damped; U the upper
     Cholesky factor of the inverse (float32 on the GPU first; float64 and more ridge when it does not factor).
@@ -113,12 +130,14 @@ def prepare_hessian_torch(H, n, damp=0.01, order="seq", bs=QK, device="cuda", ou
     mean_d = float(torch.diagonal(Hp64).mean())
 
     def factor(dtype, extra):
+        # U is the upper factor of Hp^-1 = U^T U. With J the order reversal, J Hp J = Lr Lr^T (lower Cholesky), so
+        # Hp = R R^T with R = J Lr J upper and Hp^-1 = R^-T R^-1: U = R^-1 = J Lr^-1 J (upper, positive diagonal,
+        # hence the same factor as ldlq.py's cholesky(cholesky_inverse(cholesky(Hp)), upper) up to rounding), for
+        # one factorisation and one triangular inverse instead of three factor/inverse passes.
         Hp = Hp64.to(dtype).clone()
         Hp.diagonal().add_((damp + extra) * mean_d)
-        Lc = torch.linalg.cholesky(Hp)
-        Hinv = torch.cholesky_inverse(Lc)
-        Hinv = 0.5 * (Hinv + Hinv.T)
-        return torch.linalg.cholesky(Hinv, upper=True)
+        Lr = torch.linalg.cholesky(Hp.flip(0, 1))
+        return tri_inv_lower(Lr).flip(0, 1)
 
     U = None
     for dtype, extra in ((dt, 0.0), (torch.float64, 0.0), (torch.float64, 10 * damp), (torch.float64, 100 * damp)):
