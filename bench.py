@@ -49,8 +49,9 @@ def parse():
     ap.add_argument("--experts", type=int, default=EXPERTS_PER_GPU)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--ldlq-streams", type=int, default=1,
-                    help="config 5: experts in flight (host threads); 1 = one expert after another on one stream")
+    ap.add_argument("--ldlq-streams", type=int, default=4,
+                    help="config 5: CUDA streams the experts alternate over (the next expert's factorisation runs "
+                         "beside this one's loop); 1 = one expert after another on one stream")
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5],
                     help="2 (default): the metric's own workload; 1, 3, 4, 5: the other benchmark configurations, "
                          "one GPU, one JSON line each (measurement modes beside the contract)")
@@ -369,10 +370,10 @@ def run_ldlq(args, g, dev, stream, fp32):
     """config 5: LDLQ re-quantization of experts 2048 x 7168 to IQ2_XXS with their own Hessians
     H = X^T X / n + 0.01 mean(diag) I (X = (Z + A B) diag(g), n = 4096, rank-32 structure, built on the GPU before the
     timing), from the Hessian's factorisation through the 28-block feedback loop (ldlq_gpu.py). Timed twice: one expert
-    at a time on one stream (the latency of an expert), and the experts spread over --ldlq-streams host threads with a
-    CUDA stream each (the reference's --gpu-threads): the quantize launches of one 2048-row block column fill part
-    of the GPU, so experts overlap. The concurrent bytes must equal the sequential ones."""
-    import threading
+    at a time on one stream (the latency of an expert), and the experts alternating over --ldlq-streams CUDA streams
+    from one host thread (ldlq_gpu.ldlq_experts_torch; the reference overlaps experts with --gpu-threads): the next
+    expert's factorisation runs while this one's loop of small quantize launches leaves most of the GPU idle. The
+    pipelined bytes must equal the sequential ones."""
     import torch
     import ldlq_gpu
     E = args.experts if args.experts != EXPERTS_PER_GPU else 8
@@ -414,35 +415,29 @@ def run_ldlq(args, g, dev, stream, fp32):
         deq = gqt.dequant(seq[e].reshape(1, -1, gqt.tsize)).reshape(ne1, ne0)
         D = (Ws[e][0] - deq).double()
         losses.append(float(((D @ Hs[e]) * D).sum()) / n)          # ldlq.py:110-113's proxy loss, on the GPU
-    par = [None] * E
     streams = [torch.cuda.Stream(device=dev) for _ in range(K)]
-
-    def worker(k):
-        with torch.cuda.stream(streams[k]):
-            for e in range(k, E, K):
-                par[e] = one(e)
-        streams[k].synchronize()
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    th = [threading.Thread(target=worker, args=(k,)) for k in range(K)]
-    for t in th:
-        t.start()
-    for t in th:
-        t.join()
-    torch.cuda.synchronize()
-    wall = time.perf_counter() - t0
+    for rep in range(2):                     # (the first pass warms the streams' allocations and library handles up)
+        Wc = [w.clone() for w in Ws]
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        par = ldlq_gpu.ldlq_experts_torch(Wc, Hs, [n] * E, gqt, ims, streams)
+        b.record()
+        torch.cuda.synchronize()
+        wall = a.elapsed_time(b) / 1e3
+        del Wc
     if not all(torch.equal(par[e], seq[e]) for e in range(E)):
-        raise RuntimeError("LDLQ bytes differ between the sequential and the concurrent runs")
+        raise RuntimeError("LDLQ bytes differ between the sequential and the pipelined runs")
     ms = statistics.mean(times)
-    # one stream: the experts' device time (CUDA events, the first expert left out as warm-up); several: the wall
-    # time of the concurrent pass
+    # one stream: the experts' device time (CUDA events, the first expert left out as warm-up); several: the whole
+    # pipelined pass (CUDA events around it, every stream joined)
     rate = ne1 * ne0 / (ms / 1e3) / 1e9 if K == 1 else E * ne1 * ne0 / wall / 1e9
     line = {"metric": "Gweights/s LDLQ-requantized to IQ2_XXS, config 5", "value": rate,
             "unit": "Gweights/s", "n_gpus": 1, "steps": E, "warmup": 1, "ms_per_step": ne1 * ne0 / rate / 1e6,
             "higher_is_better": True, "dtype": "f32 weights, f64 feedback", "data": "synthetic (config 5, seeded)",
             "config": {"workload": "config 5: %d experts 2048 x 7168 -> IQ2_XXS, own Hessian each (7168^2), "
                        "act order seq, imatrix weights, f64 update; %s" % (
-                           E, "one stream" if K == 1 else "%d host threads a CUDA stream each" % K)},
+                           E, "one stream" if K == 1 else "experts alternating over %d CUDA streams" % K)},
             "expert_latency_ms": ms, "sequential_gweights_s": ne1 * ne0 / (ms / 1e3) / 1e9,
             "proxy_loss_mean": statistics.mean(losses)}
     print(json.dumps(line), flush=True)

@@ -102,10 +102,12 @@ def tri_inv_lower(L, leaf=1024):
     return out
 
 
-def prepare_hessian_torch(H, n, damp=0.01, order="seq", bs=QK, device="cuda", out="numpy"):
+def prepare_hessian_torch(H, n, damp=0.01, order="seq", bs=QK, device="cuda", out="numpy", check=True):
     """ldlq.py:275-323: normalised, dead columns zeroed, optional act-order block permutation, damped; U the upper
     Cholesky factor of the inverse (float32 on the GPU first; float64 and more ridge when it does not factor).
-    Returns (U float64, perm, diag_n, dead) as numpy arrays, or with out="torch" as tensors on `device`."""
+    Returns (U float64, perm, diag_n, dead) as numpy arrays, or with out="torch" as tensors on `device`.
+    Nothing here waits for the device except the factorisation's success check; check=False leaves that out too
+    (only the first rung of the ladder runs) and returns the factorisation's status tensor last (0: factored)."""
     import torch
     dt = torch.float64 if device == "cpu" else torch.float32
     ne0 = H.shape[0]
@@ -113,13 +115,11 @@ def prepare_hessian_torch(H, n, damp=0.01, order="seq", bs=QK, device="cuda", ou
         Hn = H.to(device=device, dtype=torch.float64) / max(float(n), 1.0)
     else:
         Hn = torch.as_tensor(np.asarray(H), dtype=torch.float64).to(device) / max(float(n), 1.0)
+    dead = torch.diagonal(Hn) <= 0
+    keep = ~dead
+    Hn = torch.where(keep[:, None] & keep[None, :], Hn, 0.0)   # dead rows and columns zeroed, their diagonal 1
+    Hn.diagonal().add_(dead.to(Hn.dtype))
     d = torch.diagonal(Hn).clone()
-    dead = d <= 0
-    if bool(dead.any()):
-        Hn[dead, :] = 0
-        Hn[:, dead] = 0
-        Hn[dead, dead] = 1.0
-        d = torch.diagonal(Hn).clone()
     nblk = ne0 // bs
     if order == "act":
         blk_order = torch.argsort(-d.reshape(nblk, bs).sum(1), stable=True)
@@ -127,7 +127,7 @@ def prepare_hessian_torch(H, n, damp=0.01, order="seq", bs=QK, device="cuda", ou
         blk_order = torch.arange(nblk, device=device)
     perm = (blk_order[:, None] * bs + torch.arange(bs, device=device)[None]).reshape(-1)
     Hp64 = Hn[perm][:, perm] if order == "act" else Hn   # (the sequential order's permutation is the identity)
-    mean_d = float(torch.diagonal(Hp64).mean())
+    mean_d = torch.diagonal(Hp64).mean()
 
     def factor(dtype, extra):
         # U is the upper factor of Hp^-1 = U^T U. With J the order reversal, J Hp J = Lr Lr^T (lower Cholesky), so
@@ -136,16 +136,19 @@ def prepare_hessian_torch(H, n, damp=0.01, order="seq", bs=QK, device="cuda", ou
         # one factorisation and one triangular inverse instead of three factor/inverse passes.
         Hp = Hp64.to(dtype).clone()
         Hp.diagonal().add_((damp + extra) * mean_d)
-        Lr = torch.linalg.cholesky(Hp.flip(0, 1))
-        return tri_inv_lower(Lr).flip(0, 1)
+        Lr, info = torch.linalg.cholesky_ex(Hp.flip(0, 1))
+        return tri_inv_lower(Lr).flip(0, 1), info
 
+    if not check:
+        U, info = factor(dt, 0.0)
+        res = (U.double(), perm, d[perm], dead)
+        return (res if out == "torch" else tuple(t.cpu().numpy() for t in res)) + (info,)
     U = None
     for dtype, extra in ((dt, 0.0), (torch.float64, 0.0), (torch.float64, 10 * damp), (torch.float64, 100 * damp)):
-        try:
-            U = factor(dtype, extra)
+        Uc, info = factor(dtype, extra)
+        if int(info) == 0 and bool(torch.isfinite(torch.diagonal(Uc)).all()):
+            U = Uc
             break
-        except Exception:
-            continue
     if U is None:
         raise RuntimeError("Hessian could not be factored even with %.0f%% ridge" % (100 * (damp + 100 * damp)))
     if out == "torch":
@@ -166,17 +169,20 @@ def quantize_matrix_torch(W, gqt, U=None, perm=None, diag_n=None, imatrix=None, 
     if perm is None:
         perm = torch.arange(ne0, device=dev)
     Wp = W.index_select(2, perm).contiguous()
-    Ud = None
+    Ud = Uinv = None
     if feedback:
         Ud = U.to(torch.float64 if f64 else torch.float32)
+        # the diagonal blocks' inverses, all in one batched solve (E U_BB^-1 is then one small GEMM a block)
+        Ubb = torch.stack([Ud[k * bs:(k + 1) * bs, k * bs:(k + 1) * bs] for k in range(nblk - 1)]) if nblk > 1 else None
+        if Ubb is not None:
+            Uinv = torch.linalg.solve_triangular(Ubb, torch.eye(bs, dtype=Ud.dtype, device=dev).expand_as(Ubb), upper=True)
     if weights == "imatrix":
         imp = imatrix.index_select(1, perm).contiguous()
     elif weights == "diag":
         imp = diag_n.to(torch.float32)[None].expand(B, ne0).contiguous()
     elif weights != "schur":
         raise ValueError(weights)
-    blk_order = (perm.view(nblk, bs)[:, 0] // bs).tolist()
-    out = torch.empty((nblk, B, ne1, tsize), dtype=torch.uint8, device=dev)
+    out = torch.empty((nblk, B, ne1, tsize), dtype=torch.uint8, device=dev)   # in the permuted block order
     for k in range(nblk):
         c0, c1 = k * bs, (k + 1) * bs
         blk = Wp[:, :, c0:c1].contiguous()
@@ -185,13 +191,49 @@ def quantize_matrix_torch(W, gqt, U=None, perm=None, diag_n=None, imatrix=None, 
             qw = torch.diagonal(torch.linalg.inv(Ubb.T @ Ubb)).to(torch.float32)[None].expand(B, bs).contiguous()
         else:
             qw = imp[:, c0:c1].contiguous()
-        raw = out[blk_order[k]]
+        raw = out[k]
         gqt.quant(blk, qw, raw)
         if feedback and k + 1 < nblk:
             E = gqt.error(raw, blk, Ud.dtype)
-            Es = torch.linalg.solve_triangular(Ud[c0:c1, c0:c1], E, upper=True, left=False)   # E U_BB^-1
+            Es = E @ Uinv[k]                                                                    # E U_BB^-1
             Wp[:, :, c1:] -= (Es @ Ud[c0:c1, c1:]).to(torch.float32)
-    return out.permute(1, 2, 0, 3).reshape(B, ne1, nblk * tsize)
+    res = torch.empty_like(out).index_copy_(0, perm.view(nblk, bs)[:, 0] // bs, out)   # back to the source order
+    return res.permute(1, 2, 0, 3).reshape(B, ne1, nblk * tsize)
+
+
+def ldlq_experts_torch(Ws, Hs, ns, gqt, imatrices, streams, damp=0.01, order="seq", weights="imatrix", f64=True):
+    """Several experts (each with its own Hessian) one after another, expert e on streams[e % len(streams)]: the
+    factorisation of the next expert runs on the GPU while this one's feedback loop does (the loop's 28 block
+    quantizations are small launches that leave most of the GPU idle). The work and the bytes of every expert are
+    exactly those of prepare_hessian_torch + quantize_matrix_torch on one stream. Ws[e]: f32 [B, ne1, ne0] on the
+    device (updated in place), Hs[e]: [ne0, ne0], imatrices[e]: [B, ne0]. Returns the experts' bytes, ready on the
+    current stream."""
+    import torch
+    cur = torch.cuda.current_stream()
+    outs = []
+    infos, W0 = [], []
+    for e in range(len(Ws)):
+        s = streams[e % len(streams)]
+        s.wait_stream(cur)
+        with torch.cuda.stream(s):
+            W0.append(Ws[e].clone())
+            U, perm, diag_n, _, info = prepare_hessian_torch(Hs[e], ns[e], damp=damp, order=order,
+                                                             device=Ws[e].device, out="torch", check=False)
+            infos.append(info)
+            outs.append(quantize_matrix_torch(Ws[e], gqt, U=U, perm=perm, diag_n=diag_n, imatrix=imatrices[e],
+                                              weights=weights, f64=f64))
+    for s in streams:
+        cur.wait_stream(s)
+    for o in outs:
+        o.record_stream(cur)
+    failed = torch.nonzero(torch.stack([i.reshape(()) for i in infos]) != 0).flatten().tolist()
+    for e in failed:   # (the float32 factorisation failed: the whole ladder, as one expert alone)
+        Ws[e].copy_(W0[e])
+        U, perm, diag_n, _ = prepare_hessian_torch(Hs[e], ns[e], damp=damp, order=order, device=Ws[e].device,
+                                                   out="torch")
+        outs[e] = quantize_matrix_torch(Ws[e], gqt, U=U, perm=perm, diag_n=diag_n, imatrix=imatrices[e],
+                                        weights=weights, f64=f64)
+    return outs
 
 
 def proxy_loss(W, deq, H, n):
