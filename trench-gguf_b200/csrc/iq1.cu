@@ -76,6 +76,19 @@ __device__ int snap_group(const IQ1Warp<T> & st, int sl, int g, int m, float s, 
     return bl == NONE ? -1 : (int) (bl >> 16);
 }
 
+// IQ1_M's running half sums: element v = (w*x, w) goes to half 1's sums when hbit != 0, else to half 0's; the other
+// half's sums stay as they are - which is what ggml's adding +0 to them gives, as these sums start at +0 and a sum
+// of rounded additions that starts at +0 is never -0. Two predicated additions a half, no select.
+__device__ __forceinline__ void half_acc(unsigned hbit, float2 v, float & x0, float & w0, float & x1, float & w1) {
+    asm("{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "@p add.rn.f32 %2, %2, %5;\n\t"
+        "@p add.rn.f32 %3, %3, %6;\n\t"
+        "@!p add.rn.f32 %0, %0, %5;\n\t"
+        "@!p add.rn.f32 %1, %1, %6;\n\t}"
+        : "+f"(x0), "+f"(w0), "+f"(x1), "+f"(w1) : "r"(hbit), "f"(v.x), "f"(v.y));
+}
+
 // group g's levels take the minus shift (IQ1_S: one shift a sub-block; IQ1_M: one a half, bk's two bits)
 template <int T> __device__ __forceinline__ bool minus_of(int bk, int g) {
     return T == IQ1_S ? bk == 1 : (g == 0 ? bk >= 2 : (bk % 2) != 0);
@@ -211,20 +224,19 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
                 // the prefix sums split by half of the sub-block (gpuq.hip:559-571) are not stored: both scan loops
                 // run them forward from the sorted elements' (w*x, w), the same additions in the same order (a
                 // half's sum only moves at its own elements; adding +0 to the other half changes nothing)
-                float ax[2] = {0.f, 0.f}, aw[2] = {0.f, 0.f};
+                float ax0 = 0.f, ax1 = 0.f, aw0 = 0.f, aw1 = 0.f;
                 unsigned hmask = 0;                    // bit j: sorted element j is in the second half
                 for (int j = 0; j < SB; ++j) {
                     const int i = st.idx[j][lane], h = i < SB / 2 ? 0 : 1;
                     const float wi = st.w[i][lane], wx = wi * st.x[i][lane];
                     st.u.sv[j][lane] = make_float2(wx, wi);
                     hmask |= (unsigned) h << j;
-                    ax[h] = ax[h] + wx;
-                    aw[h] = aw[h] + wi;
+                    if (h) { ax1 = ax1 + wx; aw1 = aw1 + wi; } else { ax0 = ax0 + wx; aw0 = aw0 + wi; }
                 }
                 const float p2 = 1 + DELTA, m2 = 1 - DELTA;
                 const float cp1 = (-1 + DELTA) * (-1 + DELTA) - DELTA * DELTA, cp2 = DELTA * DELTA - (1 + DELTA) * (1 + DELTA);
                 const float cm1 = (-1 - DELTA) * (-1 - DELTA) - (-DELTA) * (-DELTA), cm2 = (-DELTA) * (-DELTA) - (1 - DELTA) * (1 - DELTA);
-                const float tx0 = ax[0], tx1 = ax[1], tw0 = aw[0], tw1 = aw[1];
+                const float tx0 = ax0, tx1 = ax1, tw0 = aw0, tw1 = aw1;
                 const float txp0 = tx0 * p2, txp1 = tx1 * p2, txm0 = tx0 * m2, txm1 = tx1 * m2;
                 const float twp0 = tw0 * p2 * p2, twp1 = tw1 * p2 * p2, twm0 = tw0 * m2 * m2, twm1 = tw1 * m2 * m2;
                 float a0 = 0.f, a1 = 0.f, c0 = 0.f, c1 = 0.f;          // px[h][i1], pw[h][i1]
@@ -243,19 +255,9 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
                             if (sq2[c] > 0 && sqx[c] * sqx[c] > best * sq2[c]) {
                                 scale = sqx[c] / sq2[c]; best = scale * sqx[c]; b1 = i1; b2 = i2; bk = c;
                             }
-                        if (i2 < SB) {                             // on to prefix i2 + 1
-                            const float2 v = st.u.sv[i2][lane];
-                            const bool h = (hmask >> i2) & 1u;
-                            r0 += h ? 0.f : v.x; e0 += h ? 0.f : v.y;
-                            r1 += h ? v.x : 0.f; e1 += h ? v.y : 0.f;
-                        }
+                        if (i2 < SB) half_acc(hmask & (1u << i2), st.u.sv[i2][lane], r0, e0, r1, e1);   // prefix i2 + 1
                     }
-                    if (i1 < SB) {                                 // on to prefix i1 + 1
-                        const float2 v = st.u.sv[i1][lane];
-                        const bool h = (hmask >> i1) & 1u;
-                        a0 += h ? 0.f : v.x; c0 += h ? 0.f : v.y;
-                        a1 += h ? v.x : 0.f; c1 += h ? v.y : 0.f;
-                    }
+                    if (i1 < SB) half_acc(hmask & (1u << i1), st.u.sv[i1][lane], a0, c0, a1, c1);       // prefix i1 + 1
                 }
             }
             if (b1 >= 0) {
@@ -413,25 +415,22 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
         } else {
             for (int i = 48; i < 56; ++i) y[i] = 0;
             if (max_scale) {
-                const uint8_t masks[4] = {0x00, 0x80, 0x08, 0x88};
-                uint16_t sc[4] = {0, 0, 0, 0};
+                uint64_t sc = 0;                       // the four 16-bit scale words, word i in bits 16i..16i+15
                 float d = max_scale / 15;
                 const float id = 1 / d;
                 float sqx = 0, sq2 = 0;
                 for (int ib = 0; ib < 16; ++ib) {
                     const int sl = lane * NSUB + ib;
                     const int l = imax(0, imin(7, nearest_int(0.5f * (id * scl[ib] - 1))));
-                    sc[ib / 4] |= (uint16_t) (l << (3 * (ib % 4)));
-                    y[32 + ib] |= masks[st.shifts[sl]];
+                    sc |= (uint64_t) l << (16 * (ib / 4) + 3 * (ib % 4));
+                    const int m = st.shifts[sl];       // shift code: bit 0 -> 0x80, bit 1 -> 0x08
+                    y[32 + ib] |= (uint8_t) ((m & 1) * 0x80 | (m & 2) * 4);
                     for (int e = 0; e < 16; ++e) { const float2 v = st.u.prod[e][sl]; sqx += v.x; sq2 += v.y; }
                 }
                 if (sq2 > 0) d = sqx / sq2;
-                const uint16_t s = half_bits(d * 1.1125f);
-                sc[0] |= (uint16_t) ((s & 0x000f) << 12);
-                sc[1] |= (uint16_t) ((s & 0x00f0) << 8);
-                sc[2] |= (uint16_t) ((s & 0x0f00) << 4);
-                sc[3] |= (uint16_t) (s & 0xf000);
-                for (int i = 0; i < 4; ++i) { y[48 + 2 * i] = sc[i] & 255; y[49 + 2 * i] = sc[i] >> 8; }
+                const uint64_t s = half_bits(d * 1.1125f);
+                sc |= ((s & 0x000f) << 12) | ((s & 0x00f0) << 24) | ((s & 0x0f00) << 36) | ((s & 0xf000) << 48);
+                for (int i = 0; i < 8; ++i) y[48 + i] = (uint8_t) (sc >> (8 * i));
             }
         }
     }
