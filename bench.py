@@ -192,7 +192,8 @@ def run_reference_gpu(args, rank, local):
     im = torch.from_numpy(im_np).to(dev)
     x = torch.empty(nw, dtype=torch.float32, device=dev)
     bpr = COLS // 256
-    outs = {t: torch.empty(nw // 256 * R.gpuq_block_bytes(TYPES[t]), dtype=torch.uint8, device=dev) for t in types}
+    outs = {t: torch.empty(nw // gpuq.BLOCK_LEN[TYPES[t]] * R.gpuq_block_bytes(TYPES[t]), dtype=torch.uint8, device=dev)
+            for t in types}
     stream = torch.cuda.Stream(device=dev)
     sh = c.c_void_p(stream.cuda_stream)
 
@@ -303,7 +304,7 @@ def run_config(args):
         for name, src, host_raw, host_im, (nmat, nrow, npr), key in jobs:
             t = QTYPES[name.split()[0].split("+")[0]]
             nw = nmat * nrow * npr
-            blen = 32 if t == 8 else 256
+            blen = gpuq.BLOCK_LEN[t]
             nbytes = nw // blen * g.block_bytes(t)
             d_raw = torch.from_numpy(np.ascontiguousarray(host_raw).reshape(-1).view(np.uint8)).to(dev)
             d_im = torch.from_numpy(np.ascontiguousarray(host_im)).to(dev) if host_im is not None else None
@@ -484,7 +485,8 @@ def main():
     nw = E * ROWS * COLS
     raw = torch.from_numpy(raw_np.reshape(-1)).to(dev)
     im = torch.from_numpy(im_np).to(dev)
-    outs = {t: torch.empty(nw // 256 * g.block_bytes(TYPES[t]), dtype=torch.uint8, device=dev) for t in types}
+    outs = {t: torch.empty(nw // gpuq.BLOCK_LEN[TYPES[t]] * g.block_bytes(TYPES[t]), dtype=torch.uint8, device=dev)
+            for t in types}
     block_b = {t: g.block_bytes(TYPES[t]) for t in types}
     stream = torch.cuda.Stream(device=dev)
     sh = stream.cuda_stream
@@ -584,7 +586,7 @@ def main():
         roof = {"bound": "fp32", "kernel": top, "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
                 "peak_source": peak_src, "ops_per_weight": opw,
                 "traffic": tb * E * ROWS * COLS if tb else None, "traffic_unit": "bytes a launch (ncu DRAM read+write, "
-                "scaled from a 20-expert capture by the weights a launch)", "algorithmic_bytes": E * ROWS * COLS * (17 / 32 + block_b[top] / 256)}
+                "scaled from a 20-expert capture by the weights a launch)", "algorithmic_bytes": E * ROWS * COLS * (17 / 32 + block_b[top] / gpuq.BLOCK_LEN[TYPES[top]])}
     cb = None
     if not args.no_cpu and world == 1:
         cb = cpu_baseline(types, CPU_SAMPLE_EXPERTS)   # 10-30 s of work on all host cores

@@ -33,7 +33,15 @@ template <> struct KT<IQ4_NL> { static constexpr int BL = 32, SB = 32; };
 
 template <int T> struct alignas(16) KState {
     static constexpr int BL = KT<T>::BL, SB = KT<T>::SB, TILE = 32 * SB, NB = TILE / BL, NSUBB = BL / SB, NSUB = 32;
-    float x[TILE], w[TILE];
+    // x and w hold sub-block s at s * SP. The 32-weight sub-blocks get one float of padding, so that the search
+    // phase - one lane a sub-block, every lane at the same element index - reads 32 different banks (an unpadded
+    // stride of 32 floats puts the whole warp on one bank: Q4_K and Q5_K with an imatrix ran 1.7x slower). The
+    // 16-weight searches keep their sub-block in registers; padding them measured slightly slower.
+    static constexpr int SP = SB == 32 ? SB + 1 : SB;
+    __device__ static int xi(int e) {                                  // tile element e -> its slot
+        if constexpr (SP == SB) return e; else return (e / SB) * SP + e % SB;
+    }
+    float x[32 * SP], w[32 * SP];
     uint8_t L[TILE];
     float scales[NSUB], mins[NSUB], sw[NSUB];
     float sigma2[NB];
@@ -397,8 +405,9 @@ __global__ void __launch_bounds__(128) k_kquant(const uint8_t * __restrict__ src
         float v[8];
         if (e / BL < nb) decode8<SRC>(src, b0 * BL + e, v);
         else for (int j = 0; j < 8; ++j) v[j] = 0.f;
+        const int xe = S::xi(e);                   // (8 elements from e lie in one sub-block)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) st.x[e + j] = v[j];
+        for (int j = 0; j < 8; ++j) st.x[xe + j] = v[j];
         if (IMAT) {
             const int blk = e / BL;
             float q[8];
@@ -407,15 +416,14 @@ __global__ void __launch_bounds__(128) k_kquant(const uint8_t * __restrict__ src
                 load8_f32(qw + ((b / qw_mat) * qw_mod + (b % qw_mod) / qw_div) * BL + (e % BL), q);
             } else for (int j = 0; j < 8; ++j) q[j] = 0.f;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) st.w[e + j] = q[j];   // (raw importances; the search weights below)
+            for (int j = 0; j < 8; ++j) st.w[xe + j] = q[j];   // (raw importances; the search weights below)
         }
     }
     __syncwarp();
     // ---- per block: sumx2 in index order -> sigma2
     if (lane < NB) {
         float s2 = 0;
-        const float * xb = st.x + lane * BL;
-        for (int i = 0; i < BL; ++i) s2 += xb[i] * xb[i];
+        for (int i = 0; i < BL; ++i) { const float v = st.x[S::xi(lane * BL + i)]; s2 += v * v; }
         if constexpr (T == IQ4_NL || T == IQ4_XS) st.sigma2[lane] = s2 * (2.f / BL);
         else if constexpr (T == Q2_K) st.sigma2[lane] = s2 / QK;
         else st.sigma2[lane] = 2 * s2 / QK;
@@ -428,7 +436,7 @@ __global__ void __launch_bounds__(128) k_kquant(const uint8_t * __restrict__ src
             const int e = p * 256 + lane * 8;
             const float sg = st.sigma2[e / BL];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) st.w[e + j] = st.w[e + j] * sqrtf(sg + st.x[e + j] * st.x[e + j]);
+            for (int j = 0; j < 8; ++j) st.w[S::xi(e) + j] = st.w[S::xi(e) + j] * sqrtf(sg + st.x[S::xi(e) + j] * st.x[S::xi(e) + j]);
         }
     }
     if (!IMAT && (T == IQ4_NL || T == IQ4_XS)) {
@@ -436,7 +444,7 @@ __global__ void __launch_bounds__(128) k_kquant(const uint8_t * __restrict__ src
         for (int p = 0; p < TILE / 256; ++p) {
             const int e = p * 256 + lane * 8;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) st.w[e + j] = st.x[e + j] * st.x[e + j];
+            for (int j = 0; j < 8; ++j) st.w[S::xi(e) + j] = st.x[S::xi(e) + j] * st.x[S::xi(e) + j];
         }
     }
     __syncwarp();
@@ -444,8 +452,8 @@ __global__ void __launch_bounds__(128) k_kquant(const uint8_t * __restrict__ src
     {
         const int s = lane;                       // sub-block of the tile
         const bool live = s / NSUBB < nb;
-        const float * xb = st.x + s * SB;
-        float * wb = st.w + s * SB;
+        const float * xb = st.x + s * S::SP;
+        float * wb = st.w + s * S::SP;
         uint8_t * Lb = st.L + s * SB;
         float scale = 0, mn = 0, swv = 0;
         if (live) {
@@ -631,7 +639,7 @@ __global__ void __launch_bounds__(128) k_kquant(const uint8_t * __restrict__ src
 #pragma unroll
         for (int t = 0; t < 8; ++t) {
             const int e = e0 + t;
-            const float xv = st.x[e];
+            const float xv = st.x[S::xi(e)];
             if constexpr (T == Q2_K || T == Q4_K || T == Q5_K) {
                 constexpr int NMAX = T == Q2_K ? 3 : T == Q4_K ? 15 : 31;
                 const float dj = half_to_float(st.d16[k]) * st.sc[k][j];
