@@ -39,12 +39,11 @@ template <int T> struct alignas(16) IQ1Warp {
         uint8_t bkt[NG * 32];                // a (group, lane)'s list-length bucket, 0xFF: no search
         int hist[NBKT];
     };
-    struct PS { float px[SB + 1][32], pw[SB + 1][32]; };
+    using M2 = std::conditional_t<T == IQ1_M, float2[SB][32], char>;
     union {
-        std::conditional_t<T == IQ1_S, PS, char> p;   // IQ1_S: prefix sums
-        float2 sv[SB][32];                   // IQ1_M: (w*x, w) of the sorted elements, for running prefix sums
+        M2 sv;                               // IQ1_M: (w*x, w) of the sorted elements, for running prefix sums
         Snap snap;
-        float2 prod[SB][32];                 // IQ1_M's super-block refit: an element's w*q*x and w*q*q
+        M2 prod;                             // IQ1_M's super-block refit: an element's w*q*x and w*q*q
     } u;
     float msc[NSB];                          // a super-block's max sub-block scale
     uint8_t bk[32];                          // the split scan's shift choice a lane
@@ -191,8 +190,8 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
             int b1 = -1, b2 = -1;
             scale = mx;
             if constexpr (T == IQ1_S) {
-                st.u.p.px[0][lane] = 0.f;
-                st.u.p.pw[0][lane] = 0.f;
+                // the prefix sums (gpuq.hip:429-437) are not stored: the scan runs them forward from the sorted
+                // elements - the same additions in the same order, so every prefix is the stored one bit for bit
                 float sx = 0.f, sw = 0.f;
 #pragma unroll 1
                 for (int j = 0; j < SB; ++j) {
@@ -200,17 +199,17 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
                     const float wi = st.w[i][lane];
                     sx = sx + wi * st.x[i][lane];
                     sw = sw + wi;
-                    st.u.p.px[j + 1][lane] = sx;
-                    st.u.p.pw[j + 1][lane] = sw;
                 }
                 const float tx = sx, tw = sw;
                 const float ap = lvl(0, false), bp = lvl(1, false), cp = lvl(2, false);
                 const float am = lvl(0, true), bm = lvl(1, true), cm = lvl(2, true);
+                float a = 0.f, c = 0.f;                            // sumx[i1], sumw[i1]
                 for (int i1 = 0; i1 <= SB; ++i1) {
-                    const float x1 = st.u.p.px[i1][lane] - 0.f, w1 = st.u.p.pw[i1][lane] - 0.f;   // (sumx[i1] - sumx[0])
-                    const float sx1 = st.u.p.px[i1][lane], sw1 = st.u.p.pw[i1][lane];
+                    const float x1 = a - 0.f, w1 = c - 0.f;       // (sumx[i1] - sumx[0])
+                    const float sx1 = a, sw1 = c;
+                    float r = a, e = c;                            // sumx[i2], sumw[i2]
                     for (int i2 = i1; i2 <= SB; ++i2) {
-                        const float sx2 = st.u.p.px[i2][lane], sw2 = st.u.p.pw[i2][lane];
+                        const float sx2 = r, sw2 = e;
                         const float dx = sx2 - sx1, dw = sw2 - sw1, ex = tx - sx2, ew = tw - sw2;
                         float qx = x1 * ap + dx * bp + ex * cp;
                         float q2 = w1 * ap * ap + dw * bp * bp + ew * cp * cp;
@@ -218,6 +217,18 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
                         qx = x1 * am + dx * bm + ex * cm;
                         q2 = w1 * am * am + dw * bm * bm + ew * cm * cm;
                         if (q2 > 0 && qx * qx > best * q2) { scale = qx / q2; best = scale * qx; b1 = i1; b2 = i2; bk = 1; }
+                        if (i2 < SB) {                             // on to prefix i2 + 1
+                            const int i = st.idx[i2][lane];
+                            const float wi = st.w[i][lane];
+                            r = r + wi * st.x[i][lane];
+                            e = e + wi;
+                        }
+                    }
+                    if (i1 < SB) {                                 // on to prefix i1 + 1
+                        const int i = st.idx[i1][lane];
+                        const float wi = st.w[i][lane];
+                        a = a + wi * st.x[i][lane];
+                        c = c + wi;
                     }
                 }
             } else {
