@@ -9,7 +9,7 @@
 // (IQ1_M also refits the super-block scale over all 256 weights, skipped sub-blocks included).
 //
 // sm_100a mapping: one warp a tile of 32 sub-blocks (4 IQ1_S or 2 IQ1_M super-blocks), ONE LANE A SUB-BLOCK for
-// ggml's sequential work: the stable sort, the prefix sums (IQ1_M: run forward inside the scan), the split scan and
+// ggml's sequential work: the stable sort, the prefix sums (run forward inside the scan, not stored), the split scan and
 // the refit run in ggml's order inside the lane, so the decisions are ggml's by construction, 32 sub-blocks side by
 // side (the reference runs one super-block a thread). The codebook snap is a warp phase: every off-grid group of
 // the tile searched 32 at a time, longest neighbour list first (search.cuh). Per-lane arrays live in shared memory
@@ -39,11 +39,8 @@ template <int T> struct alignas(16) IQ1Warp {
         uint8_t bkt[NG * 32];                // a (group, lane)'s list-length bucket, 0xFF: no search
         int hist[NBKT];
     };
-    using M2 = std::conditional_t<T == IQ1_M, float2[SB][32], char>;
     union {
-        M2 sv;                               // IQ1_M: (w*x, w) of the sorted elements, for running prefix sums
         Snap snap;
-        M2 prod;                             // IQ1_M's super-block refit: an element's w*q*x and w*q*q
     } u;
     float msc[NSB];                          // a super-block's max sub-block scale
     uint8_t bk[32];                          // the split scan's shift choice a lane
@@ -86,6 +83,14 @@ __device__ __forceinline__ void half_acc(unsigned hbit, float2 v, float & x0, fl
         "@!p add.rn.f32 %0, %0, %5;\n\t"
         "@!p add.rn.f32 %1, %1, %6;\n\t}"
         : "+f"(x0), "+f"(w0), "+f"(x1), "+f"(w1) : "r"(hbit), "f"(v.x), "f"(v.y));
+}
+
+// sorted element j of lane's sub-block as (w*x, w), formed as ggml forms the prefix sums' addends
+template <typename W>
+__device__ __forceinline__ float2 sorted_wx(const W & st, int j, int lane) {
+    const int i = st.idx[j][lane];
+    const float wi = st.w[i][lane];
+    return make_float2(wi * st.x[i][lane], wi);
 }
 
 // group g's levels take the minus shift (IQ1_S: one shift a sub-block; IQ1_M: one a half, bk's two bits)
@@ -240,7 +245,6 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
                 for (int j = 0; j < SB; ++j) {
                     const int i = st.idx[j][lane], h = i < SB / 2 ? 0 : 1;
                     const float wi = st.w[i][lane], wx = wi * st.x[i][lane];
-                    st.u.sv[j][lane] = make_float2(wx, wi);
                     hmask |= (unsigned) h << j;
                     if (h) { ax1 = ax1 + wx; aw1 = aw1 + wi; } else { ax0 = ax0 + wx; aw0 = aw0 + wi; }
                 }
@@ -266,9 +270,9 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
                             if (sq2[c] > 0 && sqx[c] * sqx[c] > best * sq2[c]) {
                                 scale = sqx[c] / sq2[c]; best = scale * sqx[c]; b1 = i1; b2 = i2; bk = c;
                             }
-                        if (i2 < SB) half_acc(hmask & (1u << i2), st.u.sv[i2][lane], r0, e0, r1, e1);   // prefix i2 + 1
+                        if (i2 < SB) half_acc(hmask & (1u << i2), sorted_wx(st, i2, lane), r0, e0, r1, e1);   // prefix i2 + 1
                     }
-                    if (i1 < SB) half_acc(hmask & (1u << i1), st.u.sv[i1][lane], a0, c0, a1, c1);       // prefix i1 + 1
+                    if (i1 < SB) half_acc(hmask & (1u << i1), sorted_wx(st, i1, lane), a0, c0, a1, c1);       // prefix i1 + 1
                 }
             }
             if (b1 >= 0) {
@@ -397,9 +401,11 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
                 const bool minus = k == 0 ? sh >= 2 : (sh % 2) != 0;
                 const uint32_t lev = __ldg(tab.glev + (st.dropped[lane] ? 0 : st.gidx[k][lane]));
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
+                for (int j = 0; j < 8; ++j) {   // (x and w are dead after this: the products take their slots)
                     const float ww = st.w[8 * k + j][lane], q = lvl((lev >> (2 * j)) & 3u, minus) * (2 * l + 1);
-                    st.u.prod[8 * k + j][lane] = make_float2(ww * q * st.x[8 * k + j][lane], ww * q * q);
+                    const float px = ww * q * st.x[8 * k + j][lane], pq = ww * q * q;
+                    st.x[8 * k + j][lane] = px;
+                    st.w[8 * k + j][lane] = pq;
                 }
             }
         }
@@ -436,7 +442,7 @@ __global__ void __launch_bounds__(32 * IQ1<T>::WARPS) k_iq1(const uint8_t * __re
                     sc |= (uint64_t) l << (16 * (ib / 4) + 3 * (ib % 4));
                     const int m = st.shifts[sl];       // shift code: bit 0 -> 0x80, bit 1 -> 0x08
                     y[32 + ib] |= (uint8_t) ((m & 1) * 0x80 | (m & 2) * 4);
-                    for (int e = 0; e < 16; ++e) { const float2 v = st.u.prod[e][sl]; sqx += v.x; sq2 += v.y; }
+                    for (int e = 0; e < 16; ++e) { sqx += st.x[e][sl]; sq2 += st.w[e][sl]; }
                 }
                 if (sq2 > 0) d = sqx / sq2;
                 const uint64_t s = half_bits(d * 1.1125f);
