@@ -89,16 +89,24 @@ template <int T> struct alignas(16) WarpState {
         uint8_t bkt[S::RB * 32 * S::NG];              // a (task, group)'s list-length bucket, 0xFF: on the grid
         int hist[NBKT];                               // bucket counts, then cursors
     };
+    struct Sums { float sqx[S::NTASK], sq2[S::NTASK]; };   // every task's index-order sums
+    // With the trials in one batch, the sums are written after the batch's schedule is dead and read before the
+    // re-grid's runs: they share the union (the smaller warp state lets more warps share an SM).
+    static constexpr bool SUMS_IN_U = S::RB >= S::NROUND;
     union {                                           // (phase-disjoint uses of one buffer)
         float x2[QK];                                 // x*x, for sumx2
         QP qp;
         Sched sch;
         Regrid rg;
+        std::conditional_t<SUMS_IN_U, Sums, char> sums;
         uint8_t out[112];                             // the block's bytes (after the trials)
     } u;
     float w[S::NSUB * S::PAD], wa[S::NSUB * S::PAD], xv[S::NSUB * S::PAD];
     float qmax[S::NSUB];                              // make_qp_quants' max (from 0)
-    float t_sqx[S::NTASK], t_sq2[S::NTASK];
+    std::conditional_t<SUMS_IN_U, char, Sums> own_sums;
+    __device__ Sums & sums() {
+        if constexpr (SUMS_IN_U) return u.sums; else return own_sums;
+    }
     uint16_t t_lev[S::NTASK][S::NG];
     uint8_t t_on[S::NTASK];
     float denom[S::NSUB], scale[S::NSUB];
@@ -521,8 +529,8 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
                     }
                 }
             }
-            st.t_sqx[task] = sqx;
-            st.t_sq2[task] = sq2;
+            st.sums().sqx[task] = sqx;
+            st.sums().sq2[task] = sq2;
         }
         __syncwarp();
     }
@@ -536,7 +544,7 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
             int win = -1;
 #pragma unroll 1
             for (int t = 0; t < S::NT; ++t) {
-                const float sqx = st.t_sqx[s * S::NT + t], sq2 = st.t_sq2[s * S::NT + t];
+                const float sqx = st.sums().sqx[s * S::NT + t], sq2 = st.sums().sq2[s * S::NT + t];
                 if (sq2 > 0 && sqx * sqx > best * sq2) { scale = sqx / sq2; best = scale * sqx; win = t; }
             }
             unsigned on = P::INIT_ON ? ALL : 0u;
