@@ -39,6 +39,13 @@ TYPES = {"iq2_xxs": 16, "iq1_m": 29, "iq1_s": 19, "iq2_xs": 17, "iq2_s": 22}
 METRIC = "Gweights/s quantized (IQ2_XXS, IQ1_M) at 1/8 B200, byte-identical to ggml"
 
 
+def metric_name(types):
+    """the headline metric for the default types; other --types name theirs"""
+    if [t.lower() for t in types] == ["iq2_xxs", "iq1_m"]:
+        return METRIC
+    return "Gweights/s quantized (%s) at 1/8 B200, byte-identical to ggml" % ", ".join(t.upper() for t in types)
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -150,7 +157,7 @@ def run_reference(args, rank):
     cb = dict(vals[-1])
     cb["value"] = v
     n = REF_EXPERTS_PER_STEP * ROWS * COLS * len(types)
-    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "Gweights/s", "n_gpus": args.gpus,
+    line = {"impl": "reference", "metric": metric_name(types), "value": v, "unit": "Gweights/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * n / (v * 1e9),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (config 2 distributions, seeded)",
@@ -236,7 +243,7 @@ def run_reference_gpu(args, rank, local):
                                       c.c_void_p(im.data_ptr()), c.c_void_p(torch.cuda.current_stream().cuda_stream))
         torch.cuda.synchronize()
         same[t] = bool(n == mine.numel() and torch.equal(mine, outs[t]))
-    line = {"impl": "reference-gpu", "metric": METRIC, "value": E * ROWS * COLS * len(types) / (ms / 1e3) / 1e9,
+    line = {"impl": "reference-gpu", "metric": metric_name(types), "value": E * ROWS * COLS * len(types) / (ms / 1e3) / 1e9,
             "unit": "Gweights/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "dtype": "f32", "data": "synthetic (config 2 distributions, seeded)",
             "config": {"workload": "config 2 shard: %d experts x %d x %d MXFP4 -> %s" % (E, ROWS, COLS, "+".join(types)),
@@ -590,7 +597,7 @@ def main():
     cb = None
     if not args.no_cpu and world == 1:
         cb = cpu_baseline(types, CPU_SAMPLE_EXPERTS)   # 10-30 s of work on all host cores
-    line = {"metric": METRIC, "value": value, "unit": "Gweights/s", "n_gpus": world, "steps": args.steps,
+    line = {"metric": metric_name(types), "value": value, "unit": "Gweights/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (config 2 distributions, seeded per rank)",
             "config": {"workload": "config 2 shard: %d experts x %d x %d MXFP4 a GPU -> %s" % (E, ROWS, COLS, "+".join(types)),

@@ -381,11 +381,14 @@ __device__ float iq4_sub(const float * xb, const float * w, const IQ4Tab & tb) {
 }
 
 // ------------------------------------------------------------------------------------------------ the kernel
-// CTAs an SM the register allocation is held to (measured: Q6_K runs best at 6, the others at 5)
-template <int T> constexpr int kquant_min_ctas() { return T == Q6_K ? 6 : 5; }
+// CTAs an SM the register allocation is held to (measured: Q6_K runs best at 6, the others at 5, except Q4_K and
+// Q5_K without an imatrix, which spill there and run best unbounded)
+template <int T, bool IMAT> constexpr int kquant_min_ctas() {
+    return T == Q6_K ? 6 : ((T == Q4_K || T == Q5_K) && !IMAT) ? 1 : 5;
+}
 
 template <int T, int SRC, bool IMAT>
-__global__ void __launch_bounds__(128, kquant_min_ctas<T>()) k_kquant(const uint8_t * __restrict__ src, const float * __restrict__ qw,
+__global__ void __launch_bounds__(128, kquant_min_ctas<T, IMAT>()) k_kquant(const uint8_t * __restrict__ src, const float * __restrict__ qw,
                                                int64_t qw_mod, int64_t qw_div, int64_t qw_mat,
                                                uint8_t * __restrict__ out, int64_t nblocks) {
     using S = KState<T>;
