@@ -90,7 +90,9 @@ int gpuq_device_count(void);
 
 /* The device-pointer form of gpuq_requantize_batch: source bytes of type `src` already on the current device ->
  * d_dst, matrix m weighted by d_imatrix row m (nmat x n_per_row floats, device; NULL for the no-imatrix types).
- * Decodes inside the quantize kernel; on `stream`, no synchronisation, no library scratch. */
+ * Decodes inside the quantize kernel; on `stream`, no synchronisation, no library scratch. d_dst must hold
+ * nmat * nrow * n_per_row / block_len * gpuq_block_bytes(type) bytes, block_len being 32 for Q8_0 and IQ4_NL and
+ * 256 for every other type: the kernel writes them all and cannot see the allocation. */
 size_t gpuq_requantize_dev(int src, const void * d_raw, int type, void * d_dst, int64_t nmat, int64_t nrow,
                            int64_t n_per_row, const float * d_imatrix, void * stream);
 
