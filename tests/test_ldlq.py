@@ -160,3 +160,30 @@ def test_gpu_ldlq_batch_and_larger_case(tables, oracle):
         deq = oracle.dequantize(typ, out[b]).reshape(ne1, ne0)
         lw = LO.proxy_loss(Ws[b], deq_w, H, n)
         assert abs(LO.proxy_loss(Ws[b], deq, H, n) - lw) <= LOSS_RTOL * lw
+
+
+@pytest.mark.gpu
+def test_gpu_experts_pipelined_over_streams(tables):
+    """ldlq_experts_torch (experts alternating over CUDA streams, nothing waiting for the device in between) gives
+    every expert the bytes of prepare_hessian_torch + quantize_matrix_torch run alone on one stream"""
+    torch, G, ldlq_gpu, g = _gpu_setup(tables)
+    dev = torch.device("cuda")
+    ne1, ne0, n = 64, 1024, 2048
+    gqt = ldlq_gpu.GpuQuant(g, G.TYPES["IQ2_XXS"])
+    Ws, Hs, ims = [], [], []
+    for e in range(3):
+        H, im = LO.synthetic_hessian(ne0, n, seed=70 + e)
+        rng = np.random.default_rng(80 + e)
+        Ws.append(torch.from_numpy((rng.standard_t(5, (1, ne1, ne0)) * 0.02).astype(np.float32)).to(dev))
+        Hs.append(torch.from_numpy(H).to(dev))
+        ims.append(torch.from_numpy(im[None].astype(np.float32)).to(dev))
+    alone = []
+    for e in range(3):
+        U, perm, diag_n, _ = ldlq_gpu.prepare_hessian_torch(Hs[e], n, device=dev, out="torch")
+        alone.append(ldlq_gpu.quantize_matrix_torch(Ws[e].clone(), gqt, U=U, perm=perm, diag_n=diag_n, imatrix=ims[e]))
+    streams = [torch.cuda.Stream(device=dev) for _ in range(2)]
+    piped = ldlq_gpu.ldlq_experts_torch([w.clone() for w in Ws], Hs, [n] * 3, gqt, ims, streams)
+    torch.cuda.synchronize()
+    for e in range(3):
+        assert torch.equal(piped[e], alone[e]), e
+
