@@ -35,7 +35,8 @@ sys.path.insert(0, PKG)
 
 EXPERTS_PER_GPU, ROWS, COLS = 48, 2048, 7168
 CPU_SAMPLE_EXPERTS = 24
-TYPES = {"iq2_xxs": 16, "iq1_m": 29, "iq1_s": 19, "iq2_xs": 17, "iq2_s": 22}
+TYPES = {"iq2_xxs": 16, "iq1_m": 29, "iq1_s": 19, "iq2_xs": 17, "iq2_s": 22, "iq3_xxs": 18, "iq3_s": 21,
+         "iq4_xs": 23, "iq4_nl": 20, "q2_k": 10, "q3_k": 11, "q4_k": 12, "q5_k": 13, "q6_k": 14, "q8_0": 8}
 METRIC = "Gweights/s quantized (IQ2_XXS, IQ1_M) at 1/8 B200, byte-identical to ggml"
 
 
@@ -586,7 +587,8 @@ def main():
         peak_src = "measured in this run (trench-gguf_b200/peak.cu: FADD/FMUL issue rate)"
     except OSError:
         peak, peak_src = None, "unavailable"
-    opw = ops.get(top.upper(), {}).get("ops_per_weight")
+    okey = top.upper() + "+im" if top.upper() + "+im" in ops else top.upper()   # (this path passes the imatrix)
+    opw = ops.get(okey, {}).get("ops_per_weight")
     if opw and peak:
         ach = opw * E * ROWS * COLS / (per_type_ms[top] / 1e3) / 1e12
         tb = traffic.get(top.upper(), {}).get("dram_bytes_per_weight")
