@@ -67,6 +67,7 @@ template <int T> struct Shape {
     static constexpr int NRG = NSUB * NG;             // re-grid searches a super-block
     // trial rounds scheduled together (their searches sorted by list length): at most 640 searches a batch
     static constexpr int RB = NROUND < 640 / (32 * NG) ? NROUND : (640 / (32 * NG) > 0 ? 640 / (32 * NG) : 1);
+    static constexpr int BT = RB * 32 < NTASK ? RB * 32 : NTASK;   // tasks a batch holds
 };
 
 // per-warp shared state of one super-block
@@ -85,11 +86,11 @@ template <int T> struct alignas(16) WarpState {
         uint32_t be[32];
     };
     struct Sched {                                    // one batch of trial rounds
-        uint16_t perm[(S::RB * 32 < S::NTASK ? S::RB * 32 : S::NTASK) * S::NG];   // the batch's searches, longest first
+        uint16_t perm[S::BT * S::NG];                 // the batch's searches, longest first
         uint8_t bkt[S::RB * 32 * S::NG];              // a (task, group)'s list-length bucket, 0xFF: on the grid
         int hist[NBKT];                               // bucket counts, then cursors
     };
-    struct Sums { float sqx[S::NTASK], sq2[S::NTASK]; };   // every task's index-order sums
+    struct Sums { float sqx[S::BT], sq2[S::BT]; };     // the batch's tasks' index-order sums
     // With the trials in one batch, the sums are written after the batch's schedule is dead and read before the
     // re-grid's runs: they share the union (the smaller warp state lets more warps share an SM).
     static constexpr bool SUMS_IN_U = S::RB >= S::NROUND;
@@ -107,8 +108,10 @@ template <int T> struct alignas(16) WarpState {
     __device__ Sums & sums() {
         if constexpr (SUMS_IN_U) return u.sums; else return own_sums;
     }
-    uint16_t t_lev[S::NTASK][S::NG];
-    uint8_t t_on[S::NTASK];
+    uint16_t t_lev[S::BT][S::NG];                     // the batch's tasks' levels and on-grid groups
+    uint8_t t_on[S::BT];
+    float p6_best[S::NSUB];                           // ggml's trial choice so far: its best (the scale is scale[])
+    uint8_t p6_on[S::NSUB];                           // its on-grid groups
     float denom[S::NSUB], scale[S::NSUB];
     uint16_t lev[S::NSUB][S::NG];
     int32_t gidx[S::NSUB][S::NG];
@@ -441,6 +444,13 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
         }
         __syncwarp();
     }
+    constexpr unsigned ALL = (1u << S::NG) - 1;
+    if (lane < S::NSUB) {                                   // the trial choice's starting state
+        st.p6_best[lane] = 0.f;
+        st.p6_on[lane] = (uint8_t) (P::INIT_ON ? ALL : 0u);
+        for (int g = 0; g < S::NG; ++g) st.lev[lane][g] = 0;
+    }
+    __syncwarp();
     // ---- P5: the trials, (sub-block, trial) tasks 32 a round, in batches of RB rounds:
     //   R  every task's groups rounded at the task's inverse scale (levels and on-grid flags kept); the groups
     //      off the grid counted by the length of their neighbour list;
@@ -464,7 +474,7 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
 #pragma unroll
             for (int g = 0; g < S::NG; ++g) {
                 const uint32_t lev = round_levels<P::GD, P::KMAXQ>(xv + g * P::GD, id, &c3[g]);
-                if (live) st.t_lev[task][g] = (uint16_t) lev;
+                if (live) st.t_lev[r * 32 + lane][g] = (uint16_t) lev;
             }
 #pragma unroll
             for (int g = 0; g < S::NG; ++g) m[g] = live ? __ldg(tab.code3 + c3[g]) : 0;
@@ -482,7 +492,7 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
                 }
                 sch.bkt[(r * 32 + lane) * S::NG + g] = bk;
             }
-            if (task < S::NTASK) st.t_on[task] = (uint8_t) onb;
+            if (task < S::NTASK) st.t_on[r * 32 + lane] = (uint8_t) onb;
         }
         __syncwarp();
         const int nreq = bucket_offsets(sch.hist, lane);                        // S
@@ -501,10 +511,10 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
                 const float ts = 1 / trial_id<T>(task - s * S::NT, st.denom[s]);
                 const float * xv = st.xv + s * S::PAD + g * P::GD;
                 const float * wa = st.wa + s * S::PAD + g * P::GD;
-                const int m = __ldg(tab.code3 + code3_of<P::GD>(st.t_lev[task][g]));
+                const int m = __ldg(tab.code3 + code3_of<P::GD>(st.t_lev[slot][g]));
                 uint32_t lev = P::GD == 8 ? search_lane8(m, xv, wa, ts, tab) : search_lane4(m, xv, wa, ts, tab);
                 if (lev == NONE) { atomicOr(status, ST_NO_NEIGHBOUR); lev = 0; }
-                st.t_lev[task][g] = (uint16_t) lev;
+                st.t_lev[slot][g] = (uint16_t) lev;
             }
         }
         __syncwarp();
@@ -519,7 +529,7 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
                 const float * w = st.w + s * S::PAD;
 #pragma unroll 1
                 for (int g = 0; g < S::NG; ++g) {
-                    const uint32_t lev = st.t_lev[task][g];
+                    const uint32_t lev = st.t_lev[r * 32 + lane][g];
 #pragma unroll
                     for (int i = 0; i < P::GD; ++i) {
                         const float q = odd_level(level_of<P::GD>(lev, i));
@@ -529,31 +539,42 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
                     }
                 }
             }
-            st.sums().sqx[task] = sqx;
-            st.sums().sq2[task] = sq2;
+            st.sums().sqx[r * 32 + lane] = sqx;
+            st.sums().sq2[r * 32 + lane] = sq2;
+        }
+        __syncwarp();
+        // ggml's trial choice (gpuq.hip:305-332) replayed in trial order over this batch's trials of each sub-block,
+        // one lane a sub-block, carrying its state from batch to batch: the same comparisons in the same order as one
+        // pass over all the trials; the winner's levels are copied while the batch still holds them
+        if (lane < S::NSUB && !st.skip[lane]) {
+            const int s = lane, b0 = rb * 32;
+            const int t0 = imax(0, b0 - s * S::NT), t1 = imin(S::NT, imin(S::NTASK, b0 + nr * 32) - s * S::NT);
+            float scale = st.scale[s], best = st.p6_best[s];
+            int take = -1;
+#pragma unroll 1
+            for (int t = t0; t < t1; ++t) {
+                const int slot = s * S::NT + t - b0;
+                const float sqx = st.sums().sqx[slot], sq2 = st.sums().sq2[slot];
+                if (sq2 > 0 && sqx * sqx > best * sq2) { scale = sqx / sq2; best = scale * sqx; take = slot; }
+            }
+            if (take >= 0) {
+#pragma unroll 1
+                for (int g = 0; g < S::NG; ++g) st.lev[s][g] = st.t_lev[take][g];
+                st.p6_on[s] = st.t_on[take];
+            }
+            st.scale[s] = scale;
+            st.p6_best[s] = best;
         }
         __syncwarp();
     }
-    // ---- P6: ggml's trial choice replayed in trial order; which groups to snap again
-    constexpr unsigned ALL = (1u << S::NG) - 1;
+    // ---- P6: which groups to snap again, from ggml's trial choice (replayed batch by batch above)
     if (lane < S::NSUB) {
         const int s = lane;
         uint8_t rg = 0;
         if (!st.skip[s]) {
-            float scale = st.scale[s], best = 0;
-            int win = -1;
-#pragma unroll 1
-            for (int t = 0; t < S::NT; ++t) {
-                const float sqx = st.sums().sqx[s * S::NT + t], sq2 = st.sums().sq2[s * S::NT + t];
-                if (sq2 > 0 && sqx * sqx > best * sq2) { scale = sqx / sq2; best = scale * sqx; win = t; }
-            }
-            unsigned on = P::INIT_ON ? ALL : 0u;
-#pragma unroll 1
-            for (int g = 0; g < S::NG; ++g) st.lev[s][g] = win >= 0 ? st.t_lev[s * S::NT + win][g] : 0;
-            if (win >= 0) on = st.t_on[s * S::NT + win];
+            const unsigned on = st.p6_on[s];
             const int n_off = __popc(~on & ALL);
-            if ((P::REGRID_ANY ? n_off > 0 : true) && scale > 0) rg = (uint8_t) (P::REGRID_ALL ? ALL : (~on & ALL));
-            st.scale[s] = scale;
+            if ((P::REGRID_ANY ? n_off > 0 : true) && st.scale[s] > 0) rg = (uint8_t) (P::REGRID_ALL ? ALL : (~on & ALL));
         }
         st.regrid[s] = rg;
     }
