@@ -92,7 +92,7 @@ template <int T> struct alignas(16) WarpState {
     };
     struct Sums { float sqx[S::BT], sq2[S::BT]; };     // the batch's tasks' index-order sums
     // With the trials in one batch, the sums are written after the batch's schedule is dead and read before the
-    // re-grid's runs: they share the union (the smaller warp state lets more warps share an SM).
+    // next use of the union: they share it (the smaller warp state lets more warps share an SM).
     static constexpr bool SUMS_IN_U = S::RB >= S::NROUND;
     union {                                           // (phase-disjoint uses of one buffer)
         float x2[QK];                                 // x*x, for sumx2
@@ -457,7 +457,8 @@ __global__ void __launch_bounds__(128) k_iq_grid(const uint8_t * __restrict__ sr
     //   S  those searches ordered longest list first (a counting sort over list-length buckets);
     //   Q  the searches 32 at a time in that order, one a lane, so the lanes of a step run lists of about the same
     //      length (the order changes nothing in a result: every search is independent and exact);
-    //   M  each task's sums over its groups in index order.
+    //   M  each task's sums over its groups in index order;
+    //   then ggml's trial choice over the batch's trials, one lane a sub-block (its state carried to the next batch).
     for (int rb = 0; rb < S::NROUND; rb += S::RB) {
         const int nr = S::NROUND - rb < S::RB ? S::NROUND - rb : S::RB;
         auto & sch = st.u.sch;
