@@ -6,15 +6,22 @@ MXFP4 bytes to IQ2_XXS and to IQ1_M, each expert with its own imatrix row; the s
 quantize kernels. Inputs are seeded synthetic data with the config's distributions (workloads.config2); 374 MB of
 MXFP4 a GPU, larger than the 126 MB L2, so every step streams its input from HBM.
 
-  value  device-resident: source and imatrix already in HBM, the kernels timed with CUDA events on their stream
-  e2e    the same step through the host C ABI (gpuq_requantize_batch) from pinned host memory: host->device copies,
-         kernels and device->host copies inside the timed region (timed on the host around the synchronous call)
+  value          device-resident: source and imatrix already in HBM, the kernels timed with CUDA events on their
+                 stream
+  e2e            the same step through the host C ABI (gpuq_requantize_batch) from pinned host memory: host->device
+                 copies, kernels and device->host copies inside the timed region (host clock around the synchronous
+                 calls); e2e.pageable_value the same from plain numpy buffers, as the reference's callers pass them
+  cpu_baseline   the reference's own block functions (oracle/_ref) on all host cores, on the first 24 experts of the
+                 shard; `parity` compares their bytes with the GPU's, block by block
+  reference_gpu  trench-gguf's own GPU library built for sm_100a (oracle/_ref/libgpuq_ref_cuda.so) on the same
+                 device-resident step after this library's timed region (its decode kernel, then its quantize kernels),
+                 with its bytes compared to this library's
 Multi-GPU (torchrun, one rank a GPU): each rank takes its own 48 experts, no collective on the data path
-("scaling": "weak"); rank times are combined by max. `--impl reference` times the reference's own CPU code
-(trench-gguf's block functions compiled for the host, oracle/_ref) on a bounded sample with every host core.
-`--impl reference-gpu` (not part of the bench contract) times trench-gguf's own GPU library built for sm_100a
-(oracle/_ref/libgpuq_ref_cuda.so) on the same device-resident step - its decode kernel, then its quantize kernels -
-and checks its bytes against this library's.
+("scaling": "weak"); rank times are combined by max; the CPU and reference-GPU legs run at N = 1 only.
+`--impl reference` times the reference's own CPU code (oracle/_ref) on a bounded sample with every host core.
+`--impl reference-gpu` (not part of the bench contract) runs the reference_gpu leg alone for --steps steps.
+`--config N` (1, 3, 4, 5) measures the other benchmark configurations on one GPU, each line with its own parity
+sample against the reference's host build.
 """
 import argparse
 import ctypes
@@ -57,6 +64,7 @@ def parse():
     ap.add_argument("--experts", type=int, default=EXPERTS_PER_GPU)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-ref-gpu", action="store_true", help="leave out the reference GPU library's leg")
     ap.add_argument("--ldlq-streams", type=int, default=4,
                     help="config 5: CUDA streams the experts alternate over (the next expert's factorisation runs "
                          "beside this one's loop); 1 = one expert after another on one stream")
@@ -118,16 +126,22 @@ def fp32_peak_tflops(dev):
     return lib.peak_fp32_ops_per_s(dev) / 1e12
 
 
-def cpu_baseline(types, experts, seed=102):
-    """the reference's own block functions on this host's cores (oracle/_ref), else the C restatement, on `experts`
-    whole 2048 x 7168 experts of the config-2 shape (MXFP4 decoded outside the timed region -> each type)"""
+def cpu_checker():
+    """the reference's own block functions compiled for the host (oracle/_ref), else the C restatement pinned to them"""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as orc
-    import workloads
     kind = "reference" if orc.available("reference") else "port"
-    chk = orc.Checker("reference" if kind == "reference" else "oracle", os.path.join(PKG, "gpuq_tables.bin"))
-    raw, im = workloads.config2(experts=experts, rows=ROWS, cols=COLS, seed=seed)
+    return orc.Checker("reference" if kind == "reference" else "oracle", os.path.join(PKG, "gpuq_tables.bin")), kind
+
+
+def cpu_baseline(types, raw, im):
+    """the reference's own block functions on this host's cores on whole 2048 x 7168 MXFP4 experts (raw [E, ...],
+    im [E, 7168]: a slice of the GPU's own workload, decoded outside the timed region) -> each type. Returns the
+    baseline and the bytes it wrote a type, which double as the parity check of the GPU's bytes."""
+    chk, kind = cpu_checker()
     threads = os.cpu_count() or 1
+    experts = raw.shape[0]
+    outs = {t: [] for t in types}
     dt = 0.0
     for e in range(experts):
         x = chk.decode(39, raw[e].reshape(-1), ROWS * COLS).reshape(1, ROWS, COLS)
@@ -136,12 +150,19 @@ def cpu_baseline(types, experts, seed=102):
                 chk.quantize(TYPES[name], x[:, :64], im[e:e + 1], threads=threads)
         t0 = time.perf_counter()
         for name in types:
-            chk.quantize(TYPES[name], x, im[e:e + 1], threads=threads)
+            outs[name].append(chk.quantize(TYPES[name], x, im[e:e + 1], threads=threads))
         dt += time.perf_counter() - t0
     n = len(types) * experts * ROWS * COLS
-    return {"value": n / dt / 1e9, "unit": "Gweights/s", "cores": threads, "kind": kind,
-            "sample": "%d of the shard's experts (%d x %d, MXFP4 -> %s), %.1f s of quantization" % (
-                experts, ROWS, COLS, "+".join(types), dt)}
+    cb = {"value": n / dt / 1e9, "unit": "Gweights/s", "cores": threads, "kind": kind,
+          "sample": "%d of the shard's experts (%d x %d, MXFP4 -> %s), %.1f s of quantization" % (
+              experts, ROWS, COLS, "+".join(types), dt)}
+    return cb, {t: np.concatenate(v) for t, v in outs.items()}
+
+
+def block_parity(got, want, bb):
+    """identical blocks of two byte strings of one type"""
+    g, w = np.asarray(got).reshape(-1, bb), np.asarray(want).reshape(-1, bb)
+    return int((g == w).all(1).sum()), g.shape[0]
 
 
 REF_EXPERTS_PER_STEP = 2
@@ -151,9 +172,11 @@ def run_reference(args, rank):
     types = args.types.split(",")
     if rank != 0:
         return
+    import workloads
     for _ in range(args.warmup):
-        cpu_baseline(types, REF_EXPERTS_PER_STEP)
-    vals = [cpu_baseline(types, REF_EXPERTS_PER_STEP, seed=200 + i) for i in range(args.steps)]
+        cpu_baseline(types, *workloads.config2(experts=REF_EXPERTS_PER_STEP, rows=ROWS, cols=COLS, seed=102))
+    vals = [cpu_baseline(types, *workloads.config2(experts=REF_EXPERTS_PER_STEP, rows=ROWS, cols=COLS, seed=200 + i))[0]
+            for i in range(args.steps)]
     v = statistics.median([r["value"] for r in vals])
     cb = dict(vals[-1])
     cb["value"] = v
@@ -168,19 +191,18 @@ def run_reference(args, rank):
     print(json.dumps(line), flush=True)
 
 
-def run_reference_gpu(args, rank, local):
-    """the reference's own kernels on this GPU: gpuq_dequantize_src_dev (MXFP4 -> f32, once a step) and
-    gpuq_quantize_dev for each type, one launch an expert (its imatrix row addressing: block b reads
-    qw + ((b % qw_mod) / qw_div) * 256, so an expert's 28 blocks a row take qw_mod = 28, qw_div = 1)"""
-    path = os.path.join(ROOT, "oracle", "_ref", "libgpuq_ref_cuda.so")
-    if not os.path.exists(path):
-        if rank == 0:
-            print(json.dumps({"impl": "reference-gpu", "unavailable": "oracle/_ref/libgpuq_ref_cuda.so not built"}))
-        return
+def reference_gpu_leg(types, raw, im, E, local, ours, steps=1, warmup=1):
+    """trench-gguf's own GPU library built for sm_100a (oracle/_ref/libgpuq_ref_cuda.so) on this device-resident step:
+    its decode kernel (gpuq_dequantize_src_dev, MXFP4 -> f32, once a step), then gpuq_quantize_dev for each type, one
+    launch an expert (its imatrix addressing: block b reads qw + ((b % qw_mod) / qw_div) * 256, so an expert's 28
+    blocks a row take qw_mod = 28, qw_div = 1). Timed with CUDA events on its stream; its bytes are compared with
+    `ours` (this library's outputs of the same step, already computed: this library runs first and its status word
+    was clean, so no input here reaches the reference's trap). None when the reference build is absent."""
     import torch
     import gpuq
-    import workloads
-    torch.cuda.set_device(local)
+    path = os.path.join(ROOT, "oracle", "_ref", "libgpuq_ref_cuda.so")
+    if not os.path.exists(path):
+        return None
     dev = torch.device("cuda", local)
     R = ctypes.CDLL(path)
     c = ctypes
@@ -192,12 +214,7 @@ def run_reference_gpu(args, rank, local):
     R.gpuq_dequantize_src_dev.argtypes = [c.c_int, c.c_void_p, c.c_void_p, c.c_int64, c.c_void_p]
     if R.gpuq_init(os.path.join(PKG, "gpuq_tables.bin").encode(), local) != 0:
         raise RuntimeError("reference gpuq_init failed")
-    types = args.types.split(",")
-    E = args.experts
-    raw_np, im_np = workloads.config2(experts=E, rows=ROWS, cols=COLS, seed=102 + rank)
     nw = E * ROWS * COLS
-    raw = torch.from_numpy(raw_np.reshape(-1)).to(dev)
-    im = torch.from_numpy(im_np).to(dev)
     x = torch.empty(nw, dtype=torch.float32, device=dev)
     bpr = COLS // 256
     outs = {t: torch.empty(nw // gpuq.BLOCK_LEN[TYPES[t]] * R.gpuq_block_bytes(TYPES[t]), dtype=torch.uint8, device=dev)
@@ -221,36 +238,64 @@ def run_reference_gpu(args, rank, local):
                 ev[t][1].record(stream)
 
     with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
+        for _ in range(warmup):
             step()
     torch.cuda.synchronize()
     ev = [{t: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for t in types}
-          for _ in range(args.steps)]
+          for _ in range(steps)]
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
         start.record(stream)
-        for k in range(args.steps):
+        for k in range(steps):
             step(ev[k])
         stop.record(stream)
     torch.cuda.synchronize()
-    ms = start.elapsed_time(stop) / args.steps
-    per_type = {t: sum(e[t][0].elapsed_time(e[t][1]) for e in ev) / args.steps for t in types}
-    # the same bytes from this library
+    ms = start.elapsed_time(stop) / steps
+    per_type = {t: sum(e[t][0].elapsed_time(e[t][1]) for e in ev) / steps for t in types}
+    same = {t: bool(torch.equal(ours[t], outs[t])) for t in types}
+    return {"value": nw * len(types) / (ms / 1e3) / 1e9, "unit": "Gweights/s", "ms_per_step": ms,
+            "per_type_ms": per_type, "identical_to_ours": same, "steps": steps, "warmup": warmup,
+            "library": "trench-gguf gpuq.hip, nvcc -O3 -fmad=false -prec-div=true -prec-sqrt=true sm_100a",
+            "path": "gpuq_dequantize_src_dev once a step + gpuq_quantize_dev an expert a launch, after this "
+                    "library's timed region"}
+
+
+def run_reference_gpu(args, rank, local):
+    """--impl reference-gpu: the reference's GPU library alone on the step, for longer than the default bench's leg"""
+    import torch
+    import gpuq
+    import workloads
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    types = args.types.split(",")
+    E = args.experts
+    raw_np, im_np = workloads.config2(experts=E, rows=ROWS, cols=COLS, seed=102 + rank)
+    raw = torch.from_numpy(raw_np.reshape(-1)).to(dev)
+    im = torch.from_numpy(im_np).to(dev)
     g = gpuq.Gpuq(device=local)
-    same = {}
-    for t in types:
-        mine = torch.empty_like(outs[t])
-        n = g.lib.gpuq_requantize_dev(39, c.c_void_p(raw.data_ptr()), TYPES[t], c.c_void_p(mine.data_ptr()), E, ROWS, COLS,
-                                      c.c_void_p(im.data_ptr()), c.c_void_p(torch.cuda.current_stream().cuda_stream))
-        torch.cuda.synchronize()
-        same[t] = bool(n == mine.numel() and torch.equal(mine, outs[t]))
-    line = {"impl": "reference-gpu", "metric": metric_name(types), "value": E * ROWS * COLS * len(types) / (ms / 1e3) / 1e9,
-            "unit": "Gweights/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+    ours = {}
+    for t in types:   # this library first: its status word must be clean before the reference's kernels run
+        ours[t] = torch.empty(E * ROWS * COLS // gpuq.BLOCK_LEN[TYPES[t]] * g.block_bytes(TYPES[t]), dtype=torch.uint8,
+                              device=dev)
+        n = g.lib.gpuq_requantize_dev(39, ctypes.c_void_p(raw.data_ptr()), TYPES[t], ctypes.c_void_p(ours[t].data_ptr()),
+                                      E, ROWS, COLS, ctypes.c_void_p(im.data_ptr()),
+                                      ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        if n != ours[t].numel():
+            raise RuntimeError(g.error())
+    torch.cuda.synchronize()
+    if g.lib.gpuq_status(1) != 0:
+        print(json.dumps({"impl": "reference-gpu", "unavailable": "inputs reach an impossible search state"}))
+        return
+    leg = reference_gpu_leg(types, raw, im, E, local, ours, steps=args.steps, warmup=args.warmup)
+    if leg is None:
+        print(json.dumps({"impl": "reference-gpu", "unavailable": "oracle/_ref/libgpuq_ref_cuda.so not built"}))
+        return
+    line = {"impl": "reference-gpu", "metric": metric_name(types), "value": leg["value"], "unit": "Gweights/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": leg["ms_per_step"],
             "higher_is_better": True, "dtype": "f32", "data": "synthetic (config 2 distributions, seeded)",
             "config": {"workload": "config 2 shard: %d experts x %d x %d MXFP4 -> %s" % (E, ROWS, COLS, "+".join(types)),
-                       "library": "trench-gguf gpuq.hip, nvcc -O3 -fmad=false -prec-div=true -prec-sqrt=true sm_100a",
-                       "path": "gpuq_dequantize_src_dev once a step + gpuq_quantize_dev an expert a launch"},
-            "per_type_ms": per_type, "identical_to_ours": same}
+                       "library": leg["library"], "path": leg["path"]},
+            "per_type_ms": leg["per_type_ms"], "identical_to_ours": leg["identical_to_ours"]}
     print(json.dumps(line), flush=True)
 
 
@@ -281,9 +326,12 @@ def run_config(args):
     cfg = args.config
     if cfg == 5:
         return run_ldlq(args, g, dev, stream, fp32)
+    # the parity sample of each job: the first `sample` matrices (experts) or rows that the CPU reference quantizes
+    # too (config 1: every block; configs 3 and 4: two whole experts / 64 full rows, as the GPU tests)
     if cfg == 1:
         w, im = workloads.config1(seed=101)
         jobs = [("IQ2_XXS", 0, w, im[None], (1, w.shape[0], w.shape[1]), "IQ2_XXS@config1")]
+        sample = {"IQ2_XXS": ("mats", 1)}
         workload = "config 1: IQ2_XXS of a dense f32 4096 x 14336 tensor, t(5) + 0.1 % outliers x10"
     elif cfg == 3:
         E = args.experts
@@ -293,6 +341,7 @@ def run_config(args):
         for t in ("IQ2_XS", "IQ2_S"):
             jobs.append((t, 30, raw, im, (E, ROWS, COLS), t + "@config3"))
             jobs.append((t + " down", 30, rawd, imd, (E, COLS, ROWS), t + "@config3d"))
+        sample = {name: ("mats", 2) for name, *_ in jobs}
         workload = "config 3: %d BF16 experts, 2048 x 7168 (gate/up) and 7168 x 2048 (down) -> IQ2_XS, IQ2_S" % E
     else:
         raw, im = workloads.config4(seed=104)
@@ -302,8 +351,10 @@ def run_config(args):
             jobs.append((t + "+im", 30, raw, im[None], shape, t + "+im"))
             jobs.append((t, 30, raw, None, shape, t))
         jobs.append(("Q8_0", 30, raw, None, shape, "Q8_0"))
+        sample = {name: ("rows", 64) for name, *_ in jobs}
         workload = "config 4: BF16 8192 x 28672 -> Q2_K..Q6_K with and without imatrix, Q8_0"
     results = {}
+    kept = []
     total_w = 0
     total_ms = 0.0
     e2e_s = 0.0
@@ -361,9 +412,35 @@ def run_config(args):
             e2e_s += dt
             h2d += hsrc.numel() + (him.nbytes if him is not None else 0)
             d2h += nbytes
+            kind, k = sample[name]
+            sw = k * (nrow * npr if kind == "mats" else npr)
+            kept.append((name, t, src, host_raw, host_im, (k, nrow, npr) if kind == "mats" else (1, k, npr),
+                         out[:sw // blen * g.block_bytes(t)].cpu().numpy()))
             del d_raw, d_im, out
     if L.gpuq_status(1) != 0:
         raise RuntimeError("device status set during the measurement")
+    # the CPU reference on each job's sample: timed (cpu_baseline) and compared block by block (parity)
+    chk, kind = cpu_checker()
+    threads = os.cpu_count() or 1
+    parity = {"checker": "trench-gguf block functions built for the host (oracle/_ref)" if kind == "reference"
+              else "C restatement (oracle/oracle.c)"}
+    cpu_w, cpu_s = 0, 0.0
+    for name, t, src, host_raw, host_im, (nmat, nrow, npr), got in kept:
+        nv = nmat * nrow * npr
+        flat = np.ascontiguousarray(host_raw).reshape(-1).view(np.uint8)
+        x = chk.decode(src, flat, nv).reshape(nmat, nrow, npr)
+        imx = None if host_im is None else np.ascontiguousarray(host_im)[:nmat]
+        t0 = time.perf_counter()
+        want = chk.quantize(t, x, imx, threads=threads)
+        cpu_s += time.perf_counter() - t0
+        cpu_w += nv
+        same, n = block_parity(got, want, g.block_bytes(t))
+        parity[name] = {"blocks": n, "identical": same, "sample": "%d x %d x %d" % (nmat, nrow, npr)}
+    parity["blocks"] = sum(v["blocks"] for v in parity.values() if isinstance(v, dict))
+    parity["identical"] = sum(v["identical"] for v in parity.values() if isinstance(v, dict))
+    cb = {"value": cpu_w / cpu_s / 1e9, "unit": "Gweights/s", "cores": threads,
+          "kind": "reference" if kind == "reference" else "port",
+          "sample": "each type's parity sample (%.1f M weights, %.1f s)" % (cpu_w / 1e6, cpu_s)}
     line = {"metric": "Gweights/s quantized, config %d" % cfg, "value": total_w / (total_ms / 1e3) / 1e9,
             "unit": "Gweights/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms,
             "higher_is_better": True, "dtype": "f32", "data": "synthetic (config %d distributions, seeded)" % cfg,
@@ -371,7 +448,8 @@ def run_config(args):
             "e2e": {"value": total_w / e2e_s / 1e9, "unit": "Gweights/s", "timing": "host clock, one call a type",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "roofline_peaks": {"fp32_tops": fp32, "hbm_gbs": hbm, "source": "peak.cu measured in this run; "
-                               "MEASURED_PEAKS.json hbm_gbs"}, "clocks": clk.summary()}
+                               "MEASURED_PEAKS.json hbm_gbs"}, "clocks": clk.summary(),
+            "parity": parity, "cpu_baseline": cb}
     print(json.dumps(line), flush=True)
 
 
@@ -571,9 +649,37 @@ def main():
         for t in types:   # the host path wrote the same bytes as the device path
             if not torch.equal(hout[t], outs[t].cpu()):
                 raise RuntimeError("host and device paths differ for %s" % t)
+        # the same calls from plain numpy (pageable) buffers, as the reference's callers pass them
+        # (tools/requant_experts.py:807): the library stages them through pinned slots
+        pout = {t: np.empty(outs[t].numel(), np.uint8) for t in types}
+
+        def host_step_pageable():
+            for t in types:
+                n = L.gpuq_requantize_batch(39, raw_np.ctypes.data, TYPES[t], pout[t].ctypes.data, E, ROWS, COLS,
+                                            him.ctypes.data)
+                if n != pout[t].size:
+                    raise RuntimeError("gpuq_requantize_batch %s: %s" % (t, g.error()))
+        host_step_pageable()
+        barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            host_step_pageable()
+        torch.cuda.synchronize()
+        dtp = time.perf_counter() - t0
+        tm = torch.tensor([dtp], dtype=torch.float64, device=dev)
+        if dist:
+            dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+        dtp = float(tm.item())
+        for t in types:
+            if not np.array_equal(pout[t], hout[t].numpy()):
+                raise RuntimeError("pageable and pinned host paths differ for %s" % t)
         e2e = {"value": total_w / dt / 1e9, "unit": "Gweights/s", "timing": "host clock around the synchronous calls",
                "h2d_bytes_per_step": len(types) * (raw_np.nbytes + im_np.nbytes),
-               "d2h_bytes_per_step": sum(int(o.numel()) for o in outs.values())}
+               "d2h_bytes_per_step": sum(int(o.numel()) for o in outs.values()),
+               "buffers": "pinned (torch pin_memory)",
+               "pageable_value": total_w / dtp / 1e9,
+               "pageable_buffers": "plain numpy arrays, as tools/requant_experts.py passes them"}
     if rank != 0:
         if dist:
             dist.destroy_process_group()
@@ -596,9 +702,21 @@ def main():
                 "peak_source": peak_src, "ops_per_weight": opw,
                 "traffic": tb * E * ROWS * COLS if tb else None, "traffic_unit": "bytes a launch (ncu DRAM read+write, "
                 "scaled from a 20-expert capture by the weights a launch)", "algorithmic_bytes": E * ROWS * COLS * (17 / 32 + block_b[top] / gpuq.BLOCK_LEN[TYPES[top]])}
-    cb = None
+    cb = parity = ref_gpu = None
     if not args.no_cpu and world == 1:
-        cb = cpu_baseline(types, CPU_SAMPLE_EXPERTS)   # 10-30 s of work on all host cores
+        # 10-30 s of work on all host cores, on the first experts of this GPU's own shard; its bytes are the parity
+        # check of the GPU's bytes for those experts
+        cb, ref_bytes = cpu_baseline(types, raw_np[:CPU_SAMPLE_EXPERTS], im_np[:CPU_SAMPLE_EXPERTS])
+        parity = {"checker": "trench-gguf block functions built for the host (oracle/_ref)" if cb["kind"] == "reference"
+                  else "C restatement (oracle/oracle.c)", "sample": "the first %d experts of the shard" % CPU_SAMPLE_EXPERTS}
+        for t in types:
+            nb = ref_bytes[t].size
+            same, n = block_parity(outs[t][:nb].cpu().numpy(), ref_bytes[t], block_b[t])
+            parity[t] = {"blocks": n, "identical": same}
+        parity["blocks"] = sum(parity[t]["blocks"] for t in types)
+        parity["identical"] = sum(parity[t]["identical"] for t in types)
+    if not args.no_ref_gpu and world == 1:
+        ref_gpu = reference_gpu_leg(types, raw, im, E, local, outs)
     line = {"metric": metric_name(types), "value": value, "unit": "Gweights/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (config 2 distributions, seeded per rank)",
@@ -606,7 +724,8 @@ def main():
                        "experts_per_gpu": E, "parallelism": "expert-sharded x%d" % world,
                        "l2": "inputs (%d MB a GPU) larger than L2" % (raw_np.nbytes // 2**20)},
             "per_type": {t: {"ms": per_type_ms[t], "gweights_s": E * ROWS * COLS / (per_type_ms[t] / 1e3) / 1e9} for t in types},
-            "gpu_launches": len(types) * args.steps, "e2e": e2e, "roofline": roof, "cpu_baseline": cb, "clocks": clocks}
+            "gpu_launches": len(types) * args.steps, "e2e": e2e, "roofline": roof, "cpu_baseline": cb, "clocks": clocks,
+            "parity": parity, "reference_gpu": ref_gpu}
     print(json.dumps(line), flush=True)
     if dist:
         dist.destroy_process_group()

@@ -22,7 +22,8 @@ extern "C" {
 
 /* Reads the tables file (trench-gguf gpuq_tables.bin format) and prepares device `device`, which becomes the
  * current device and the one the host API uses. 0 ok; 1 no such device, 2 cannot open, 3 short or corrupt file,
- * 4 allocation failed, 5 no tables. Replaces gpuq_init, gpuq/gpuq.hip:2059-2080. */
+ * 4 allocation failed, 5 no tables. The device state it builds lasts until exit; a device reset (cudaDeviceReset)
+ * invalidates it. Replaces gpuq_init, gpuq/gpuq.hip:2059-2080. */
 int gpuq_init(const char * tables, int device);
 
 /* Bytes of one block of `type`, 0 for a type this library does not produce. Replaces gpuq.hip:2082-2101. */
@@ -102,7 +103,7 @@ size_t gpuq_requantize_dev(int src, const void * d_raw, int type, void * d_dst, 
 size_t gpuq_dequantize_error_dev(int type, const void * d_q, const float * d_blk, void * d_err, int f64, int64_t nblocks,
                                  void * stream);
 
-/* Scratch size of gpuq_requantize_noalloc, held on every GPU that loads the library, from load to exit. */
+/* Scratch size of gpuq_requantize_noalloc, held on every GPU that gpuq_init prepares, from gpuq_init to exit. */
 #define GPUQ_NOALLOC_SCRATCH_BYTES ((size_t) 64 << 20)
 
 /* No counterpart in the reference: gpuq_requantize_batch for callers that must not allocate device memory while
@@ -110,9 +111,12 @@ size_t gpuq_dequantize_error_dev(int type, const void * d_q, const float * d_blk
  * Same arguments, same bytes out, but the imatrix, the source bytes and the output are staged in a static device
  * array of GPUQ_NOALLOC_SCRATCH_BYTES instead of buffers grown with cudaMalloc; it calls no cudaMalloc/cudaFree.
  * A call whose staged bytes exceed the array returns 0 and says how much it needed (gpuq_last_error).
- * gpuq_init must have run for the current device; the first call on each device looks up the array's address
- * (make it before any stream capture). All calls on a device share the array, so calls that overlap on one GPU
- * race; each call clears the status word it uses. Synchronous, on the default stream. */
+ * gpuq_init must have run for the current device: it looks up the array's address there, which loads the array at
+ * set-up (if that lookup failed, the first call retries it: make that call before any stream capture). Under lazy
+ * module loading, the first launch of each quantize kernel loads its code (a driver allocation): warm each type up
+ * once during set-up, or run with CUDA_MODULE_LOADING=EAGER. Sizes are checked before any product is formed.
+ * All calls on a device share the array, so calls that overlap on one GPU race; each call clears the status word it
+ * uses. Calls across a device reset (cudaDeviceReset) are not supported. Synchronous, on the default stream. */
 size_t gpuq_requantize_noalloc(int src, const void * raw, int type, void * dst, int64_t nmat, int64_t nrow,
                                int64_t n_per_row, const float * imatrix);
 

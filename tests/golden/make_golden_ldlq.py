@@ -21,7 +21,8 @@ import ldlq_oracle  # noqa: E402
 
 
 def main():
-    ref_dir = os.environ.get("REF", "/root/reference")
+    # the trench-gguf checkout: $REF, else $TRENCH_GGUF_REF, else the checkout named `reference` beside this repository
+    ref_dir = os.environ.get("REF") or os.environ.get("TRENCH_GGUF_REF") or os.path.join(os.path.dirname(ROOT), "reference")
     spec = importlib.util.spec_from_file_location("ref_ldlq", os.path.join(ref_dir, "tools", "ldlq.py"))
     ref = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(ref)

@@ -40,6 +40,28 @@ def test_noalloc_matches_allocating_entry_point_twice(tables):
     assert np.array_equal(a, b)
 
 
+def test_noalloc_leaves_device_memory_unchanged(tables):
+    """the entry point's promise: once the library is set up and the kernel of the type has run once (its code is
+    loaded on first launch under lazy module loading), a call takes no device memory - the device's free bytes are
+    the same before and after it"""
+    import torch
+    g = G.Gpuq(device=0, tables=tables)
+    raw, im = workloads.config2(experts=1, rows=128, cols=7168, seed=34)
+    out = np.empty(128 * 7168 // 256 * 56, np.uint8)
+
+    def call():
+        n = g.lib.gpuq_requantize_noalloc(G.SOURCES["MXFP4"], raw.ctypes.data, G.TYPES["IQ1_M"], out.ctypes.data,
+                                          1, 128, 7168, im.ctypes.data)
+        assert n == out.size, g.error()
+    call()                                    # warm: the IQ1_M kernel's code is loaded by now
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info(0)[0]
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info(0)[0] == free0
+
+
 def test_noalloc_rejects_oversized_calls(tables):
     g = G.Gpuq(device=0, tables=tables)
     rows, cols = 4096, 7168        # 4 x 4096 x 7168 MXFP4 values: 62 MB in + 26 MB out, over the 64 MiB scratch
@@ -47,5 +69,11 @@ def test_noalloc_rejects_oversized_calls(tables):
     out = np.empty(4 * rows * cols // 256 * 56, np.uint8)
     got = g.lib.gpuq_requantize_noalloc(G.SOURCES["MXFP4"], raw.ctypes.data, G.TYPES["IQ1_M"], out.ctypes.data,
                                         4, rows, cols, im.ctypes.data)
+    assert got == 0
+    assert "limit" in g.error()
+    # shapes whose products would wrap a 64-bit count are refused before anything is multiplied out
+    huge = 1 << 40
+    got = g.lib.gpuq_requantize_noalloc(G.SOURCES["MXFP4"], raw.ctypes.data, G.TYPES["IQ1_M"], out.ctypes.data,
+                                        huge, huge, 7168, im.ctypes.data)
     assert got == 0
     assert "limit" in g.error()

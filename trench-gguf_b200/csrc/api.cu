@@ -143,6 +143,7 @@ struct Device {
     void * d_src[NSLOT] = {}; size_t cap_src[NSLOT] = {};
     void * d_out[NSLOT] = {}; size_t cap_out[NSLOT] = {};
     void * h_out[NSLOT] = {}; size_t cap_hout[NSLOT] = {};   // pinned staging for pageable destinations
+    void * h_src[NSLOT] = {}; size_t cap_hsrc[NSLOT] = {};   // pinned staging for pageable sources
     float * d_qw = nullptr; size_t cap_qw = 0;
 
     const SearchTab * tab(int type) const {
@@ -215,6 +216,7 @@ int init_device(int id) {
         if (cudaEventCreateWithFlags(&d->ev_h2d[i], cudaEventDisableTiming) != cudaSuccess ||
             cudaEventCreateWithFlags(&d->ev_run[i], cudaEventDisableTiming) != cudaSuccess ||
             cudaEventCreateWithFlags(&d->ev_d2h[i], cudaEventDisableTiming) != cudaSuccess) return 4;
+    noalloc_prepare(id);   // gpuq_requantize_noalloc's scratch array: loaded here, at set-up
     d->ready = true;
     return 0;
 }
@@ -260,7 +262,23 @@ struct HostJob {
     int64_t nmat, nrow, n_per_row;
     const float * imatrix;         // host, nmat x n_per_row, or null
     std::vector<Chunk> chunks;
+    std::atomic<bool> cancel{false};   // set by a device worker that failed: the others stop before their next chunk
 };
+
+// host memcpy split over a few threads for large pieces (one thread copies ~10 GB/s, less than a PCIe 5 link)
+void host_copy(void * dst, const void * src, size_t n) {
+    constexpr size_t PIECE = (size_t) 8 << 20;
+    const int nt = (int) std::min<size_t>(4, n / PIECE);
+    if (nt <= 1) { std::memcpy(dst, src, n); return; }
+    std::vector<std::thread> th;
+    const size_t per = (n / nt + 63) & ~(size_t) 63;
+    for (int k = 1; k < nt; ++k) {
+        const size_t a = per * k, b = std::min(n, a + per);
+        if (a < b) th.emplace_back([=] { std::memcpy((uint8_t *) dst + a, (const uint8_t *) src + a, b - a); });
+    }
+    std::memcpy(dst, src, std::min(n, per));
+    for (auto & t : th) t.join();
+}
 
 std::vector<Chunk> make_chunks(int64_t nmat, int64_t nrow, int64_t n_per_row, int64_t target_values) {
     std::vector<Chunk> c;
@@ -282,8 +300,11 @@ int64_t chunk_values() {
     return mw * 1000000;
 }
 
-// runs the chunks [c0, c1) of a job on one device through the 3-stream pipeline; false on error
-bool run_chunks(Device & d, const HostJob & j, size_t c0, size_t c1) {
+// runs the chunks [c0, c1) of a job on one device through the 3-stream pipeline; false on error. Pinned caller
+// buffers are copied directly; a pageable source chunk is first copied on the host into the slot's pinned staging
+// buffer (while the other slot's kernel runs), a pageable destination is filled from the slot's pinned staging
+// buffer once its device-to-host copy is done - so the copies overlap the kernels for numpy callers too.
+bool run_chunks(Device & d, HostJob & j, size_t c0, size_t c1) {
     std::lock_guard<std::mutex> lk(d.mu);
     if (const char * f = std::getenv("GPUQ_FAIL_DEVICE")) {   // host-side fault injection: this device's worker fails
         if (std::atoi(f) == d.id) { set_err("device worker failure injected by GPUQ_FAIL_DEVICE"); return false; }
@@ -314,6 +335,7 @@ bool run_chunks(Device & d, const HostJob & j, size_t c0, size_t c1) {
     cudaEventRecord(ev_qw, d.s_h2d);
     cudaStreamWaitEvent(d.s_run, ev_qw, 0);
     for (size_t ci = c0; ci < c1 && ok; ++ci) {
+        if (j.cancel.load(std::memory_order_relaxed)) { set_err("cancelled: another device of this call failed"); ok = false; break; }
         const Chunk & c = j.chunks[ci];
         const int slot = (int) ((ci - c0) % NSLOT);
         const int64_t rows = c.r1 - c.r0, mats = c.m1 - c.m0;
@@ -323,13 +345,18 @@ bool run_chunks(Device & d, const HostJob & j, size_t c0, size_t c1) {
         const size_t in_bytes = raw_bytes(j.src, nv), out_bytes = (size_t) nblocks * bb;
         finish(slot);   // the slot's previous chunk: its bytes are out, its buffers free
         if (!grow(&d.d_src[slot], &d.cap_src[slot], in_bytes) || !grow(&d.d_out[slot], &d.cap_out[slot], out_bytes) ||
-            (!dst_pinned && !grow(&d.h_out[slot], &d.cap_hout[slot], out_bytes, true))) { ok = false; break; }
+            (!dst_pinned && !grow(&d.h_out[slot], &d.cap_hout[slot], out_bytes, true)) ||
+            (!src_pinned && !grow(&d.h_src[slot], &d.cap_hsrc[slot], in_bytes, true))) { ok = false; break; }
+        const uint8_t * hsrc = j.raw + raw_bytes(j.src, v0);
+        if (!src_pinned) {   // (the slot's previous H2D is done: finish() waited for its D2H, which followed it)
+            host_copy(d.h_src[slot], hsrc, in_bytes);
+            hsrc = (const uint8_t *) d.h_src[slot];
+        }
         // H2D once the kernel that last read this slot's source buffer is done
         cudaStreamWaitEvent(d.s_h2d, d.ev_run[slot], 0);
-        if (cudaMemcpyAsync(d.d_src[slot], j.raw + raw_bytes(j.src, v0), in_bytes, cudaMemcpyHostToDevice, d.s_h2d) != cudaSuccess) {
+        if (cudaMemcpyAsync(d.d_src[slot], hsrc, in_bytes, cudaMemcpyHostToDevice, d.s_h2d) != cudaSuccess) {
             set_err("host-to-device copy failed"); ok = false; break;
         }
-        (void) src_pinned;
         cudaEventRecord(d.ev_h2d[slot], d.s_h2d);
         cudaStreamWaitEvent(d.s_run, d.ev_h2d[slot], 0);
         cudaStreamWaitEvent(d.s_run, d.ev_d2h[slot], 0);   // the output buffer's previous D2H is done
@@ -391,10 +418,15 @@ size_t run_host_job(HostJob & j) {
         for (int k = 0; k < nd; ++k) {
             const size_t a = nc * k / nd, b = nc * (k + 1) / nd;
             if (a >= b) continue;
-            th.emplace_back([&, k, a, b] { res[k] = run_chunks(*devs[k], j, a, b); if (!res[k]) errs[k] = t_err; });
+            th.emplace_back([&, k, a, b] {
+                res[k] = run_chunks(*devs[k], j, a, b);
+                if (!res[k]) { errs[k] = t_err; j.cancel.store(true, std::memory_order_relaxed); }
+            });
         }
         for (auto & t : th) t.join();
-        for (int k = 0; k < nd; ++k) if (!res[k]) { ok = false; t_err = "device " + std::to_string(devs[k]->id) + ": " + errs[k]; }
+        // the first failure that was not a cancellation names the cause
+        for (int k = nd - 1; k >= 0; --k)
+            if (!res[k] && (ok || errs[k].rfind("cancelled", 0) != 0)) { ok = false; t_err = "device " + std::to_string(devs[k]->id) + ": " + errs[k]; }
     }
     cudaSetDevice(cur);
     return ok ? total : 0;

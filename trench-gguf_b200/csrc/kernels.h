@@ -40,6 +40,9 @@ cudaError_t launch_decode(int src, const void * raw, float * out, int64_t n, cud
 const SearchTab * current_search_tab(int type, bool * device_ready);
 // Records the reason of a failed call for gpuq_last_error(). Implemented in api.cu.
 void set_last_error(const char * msg);
+// Looks up gpuq_requantize_noalloc's static scratch array on device `dev` (current), loading its module at set-up.
+// Implemented in noalloc.cu; gpuq_init calls it for every device it prepares.
+void noalloc_prepare(int dev);
 
 inline bool is_iq_grid(int t) { return t == IQ2_XXS || t == IQ2_XS || t == IQ2_S || t == IQ3_XXS || t == IQ3_S; }
 inline bool is_iq1(int t) { return t == IQ1_S || t == IQ1_M; }

@@ -11,9 +11,17 @@
 //     the output, each 256-byte aligned; a call that does not fit returns 0 with the needed size in
 //     gpuq_last_error() - split the tensor (whole rows) into smaller calls;
 //   * gpuq_init must have run for the current device (it uploads the search tables: that allocation happens once,
-//     at set-up);
-//   * the first call on each device looks up the scratch array's device address (cudaGetSymbolAddress) with that
-//     device current; make that first call before any stream capture;
+//     at set-up). gpuq_init also looks up the scratch array's device address (cudaGetSymbolAddress, with that device
+//     current), which loads this file's device module - and so the 64 MiB array - at set-up even under CUDA's lazy
+//     module loading; should that lookup fail there, the first call on the device retries it, so make that first
+//     call before any stream capture;
+//   * under lazy module loading (CUDA_MODULE_LOADING=LAZY, the default) the first launch of a quantize kernel loads
+//     that kernel's code into device memory (the driver's allocation, once a kernel and device): callers that must
+//     see no change in device memory after set-up make one warm-up call of each type they use during set-up, or run
+//     with CUDA_MODULE_LOADING=EAGER;
+//   * the cached address is the array's address in the device's primary context: resetting the device
+//     (cudaDeviceReset) invalidates it, as it invalidates every other piece of the library's device state (the
+//     tables, the staging buffers) - the library does not support calls across a device reset;
 //   * every call on a device shares the one array, which keeps the last call's bytes: the status word is cleared
 //     at the start of each call, and calls that overlap on the same GPU (other host threads) race on it.
 // Nothing here calls cudaMalloc, cudaFree or an allocating library routine: copies are cudaMemcpy, the kernel is the
@@ -44,6 +52,7 @@ unsigned char * scratch_address(int dev) {
         void * p = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess) {
+            cudaGetLastError();   // (not left behind for the caller's next CUDA call)
             char msg[256];
             snprintf(msg, sizeof(msg), "gpuq_requantize_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
                      cudaGetErrorString(e));
@@ -56,6 +65,12 @@ unsigned char * scratch_address(int dev) {
 }
 
 }  // namespace
+
+// called by gpuq_init for each device it prepares (that device current): loads the array at set-up
+void noalloc_prepare(int dev) {
+    if (!scratch_address(dev)) set_last_error("");   // (a failure here is retried, and reported, by the first call)
+}
+
 }  // namespace gq
 
 using namespace gq;
@@ -72,7 +87,17 @@ extern "C" size_t gpuq_requantize_noalloc(int src, const void * raw, int type, v
         set_last_error("gpuq_requantize_noalloc: this type needs an importance matrix");
         return 0;
     }
-    const int64_t n = nmat * nrow * n_per_row;
+    // every size below is bounded by the scratch before it is multiplied out, so no product can wrap: each of the
+    // imatrix, the source and the output must fit the array on its own
+    const int64_t lim = (int64_t) SCRATCH;
+    if (n_per_row > lim / 4 || nmat > lim / 4 / n_per_row || nrow > lim / 4 / n_per_row ||
+        nmat > lim / nrow / n_per_row) {
+        snprintf(msg, sizeof(msg), "gpuq_requantize_noalloc: %lld x %lld x %lld values exceed the %zu-byte scratch "
+                 "limit: quantize fewer rows a call", (long long) nmat, (long long) nrow, (long long) n_per_row, SCRATCH);
+        set_last_error(msg);
+        return 0;
+    }
+    const int64_t n = nmat * nrow * n_per_row;   // < 64 Mi: no overflow in the byte counts below
     if (n % 32) { set_last_error("gpuq_requantize_noalloc: the value count must be a multiple of 32"); return 0; }
     const bool want_qw = imatrix && type != Q8_0;   // (Q8_0 ignores the imatrix, as ggml_quantize_chunk)
     const size_t qw_bytes = want_qw ? (size_t) nmat * n_per_row * 4 : 0;
