@@ -325,7 +325,7 @@ def run_config(args):
     sh = stream.cuda_stream
     cfg = args.config
     if cfg == 5:
-        return run_ldlq(args, g, dev, stream, fp32)
+        return run_ldlq(args, g, dev, stream, fp32)   # (single process; under torchrun main() calls it per rank)
     # the parity sample of each job: the first `sample` matrices (experts) or rows that the CPU reference quantizes
     # too (config 1: every block; configs 3 and 4: two whole experts / 64 full rows, as the GPU tests)
     if cfg == 1:
@@ -453,90 +453,169 @@ def run_config(args):
     print(json.dumps(line), flush=True)
 
 
-def run_ldlq(args, g, dev, stream, fp32):
-    """config 5: LDLQ re-quantization of experts 2048 x 7168 to IQ2_XXS with their own Hessians
-    H = X^T X / n + 0.01 mean(diag) I (X = (Z + A B) diag(g), n = 4096, rank-32 structure, built on the GPU before the
-    timing), from the Hessian's factorisation through the 28-block feedback loop (ldlq_gpu.py). Timed twice: one expert
-    at a time on one stream (the latency of an expert), and the experts alternating over --ldlq-streams CUDA streams
-    from one host thread (ldlq_gpu.ldlq_experts_torch; the reference overlaps experts with --gpu-threads): the next
-    expert's factorisation runs while this one's loop of small quantize launches leaves most of the GPU idle. The
-    pipelined bytes must equal the sequential ones."""
+def fp64_peak_tflops(dev):
+    """float64 FMA rate (2 flop each) measured by trench-gguf_b200/peak.cu"""
+    lib = ctypes.CDLL(os.path.join(PKG, "libgpuq_peak.so"))
+    lib.peak_fp64_flop_per_s.restype = ctypes.c_double
+    lib.peak_fp64_flop_per_s.argtypes = [ctypes.c_int]
+    return lib.peak_fp64_flop_per_s(dev) / 1e12
+
+
+def ldlq_flops(ne1, ne0, bs=256):
+    """float64 flop of one expert's LDLQ as this library runs it: the Cholesky (n^3/3), the triangular inverse
+    (n^3/3), and per block k the scale E U_kk^-1 (2 ne1 256^2) and the update (2 ne1 256 (ne0 - 256 (k+1)))"""
+    nblk = ne0 // bs
+    loop = sum(2 * ne1 * bs * bs + 2 * ne1 * bs * (ne0 - bs * (k + 1)) for k in range(nblk - 1))
+    return {"cholesky": ne0 ** 3 / 3, "triangular_inverse": ne0 ** 3 / 3, "loop": float(loop)}
+
+
+def run_ldlq(args, g, dev, stream, fp32, rank=0, world=1, dist=None):
+    """config 5: LDLQ re-quantization of experts 2048 x 7168 to IQ2_XXS, each with its own Hessian built from n = 4096
+    activation rows X = (Z + A B) diag(g) (rank-32 structure, lognormal gains) by tools/hessian_from_dump.py:73-79's
+    recipe - a float32 GEMM of X^T X, accumulated in float64, timed on its own as input preparation - then
+    H / n + 0.01 mean(diag) I (the preparation's damping). The timed step is ldlq_gpu.ldlq_experts over this GPU's
+    experts: every Hessian's float64 factor, then the 28-block loop of all experts in lockstep. Under torchrun each
+    rank takes its own experts (the tensor's experts sharded, no collective; the max over ranks is reported). One
+    expert's bytes are compared with the reference's loop (the float64 restatement on the CPU with the reference's
+    block quantizer) on rank 0."""
     import torch
     import ldlq_gpu
     E = args.experts if args.experts != EXPERTS_PER_GPU else 8
-    K = max(1, args.ldlq_streams)
-    n, rank, ne1, ne0 = 4096, 32, ROWS, COLS
-    gen = torch.Generator(device=dev).manual_seed(105)
-    torch.manual_seed(105)
+    n, rk, ne1, ne0 = 4096, 32, ROWS, COLS
+    gen = torch.Generator(device=dev).manual_seed(105 + 1000 * rank)
+    torch.backends.cuda.matmul.allow_tf32 = False       # (the reference's float32 GEMM is a full float32 one)
     gqt = ldlq_gpu.GpuQuant(g.lib, 16)
     Hs, ims, Ws = [], [], []
+    hess_ms = 0.0
     for e in range(E):
         Z = torch.randn(n, ne0, device=dev, generator=gen)
-        A = torch.randn(n, rank, device=dev, generator=gen)
-        B = torch.randn(rank, ne0, device=dev, generator=gen) / rank ** 0.5
+        A = torch.randn(n, rk, device=dev, generator=gen)
+        B = torch.randn(rk, ne0, device=dev, generator=gen) / rk ** 0.5
         gain = torch.exp(torch.randn(ne0, device=dev, generator=gen))
         X = (Z + A @ B) * gain[None]
-        H = X.double().T @ X.double()
+        del Z, A, B
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        H = torch.zeros(ne0, ne0, dtype=torch.float64, device=dev)
+        for c0 in range(0, n, 1024):                     # row chunks: float32 X^T X, float64 accumulation
+            xc = X[c0:c0 + 1024]
+            H += (xc.T @ xc).double()
+        b.record()
+        torch.cuda.synchronize()
+        hess_ms += a.elapsed_time(b)
         Hs.append(H)
         ims.append((torch.diagonal(H) / n).float()[None].contiguous())
         Ws.append((torch.distributions.StudentT(5.0).sample((1, ne1, ne0)).to(dev) * 0.02 / (5.0 / 3.0) ** 0.5).float())
-        del Z, A, B, X
+        del X
     torch.cuda.synchronize()
 
-    def one(e):
-        U, perm, diag_n, dead = ldlq_gpu.prepare_hessian_torch(Hs[e], n, device=dev, out="torch")
-        return ldlq_gpu.quantize_matrix_torch(Ws[e].clone(), gqt, U=U, perm=perm, diag_n=diag_n, imatrix=ims[e])
-
-    seq, times = [], []
-    for e in range(E):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(stream):
-            a.record(stream)
-            seq.append(one(e))
-            b.record(stream)
-        torch.cuda.synchronize()
-        if e >= min(1, E - 1):               # the first expert warms the library and cuSOLVER up
+    def step():
+        return ldlq_gpu.ldlq_experts([w.clone() for w in Ws], Hs, [n] * E, gqt, ims)
+    step()                                               # warm-up: cuSOLVER / cuBLAS handles, the kernels' code
+    torch.cuda.synchronize()
+    times = []
+    with Clocks(int(os.environ.get("LOCAL_RANK", "0"))) as clk:
+        for _ in range(max(1, args.steps)):
+            if dist:
+                dist.barrier()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            outs = step()
+            b.record()
+            torch.cuda.synchronize()
             times.append(a.elapsed_time(b))
-    losses = []
-    for e in range(E):
-        deq = gqt.dequant(seq[e].reshape(1, -1, gqt.tsize)).reshape(ne1, ne0)
-        D = (Ws[e][0] - deq).double()
-        losses.append(float(((D @ Hs[e]) * D).sum()) / n)          # ldlq.py:110-113's proxy loss, on the GPU
-    streams = [torch.cuda.Stream(device=dev) for _ in range(K)]
-    for rep in range(2):                     # (the first pass warms the streams' allocations and library handles up)
-        Wc = [w.clone() for w in Ws]
-        torch.cuda.synchronize()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        par = ldlq_gpu.ldlq_experts_torch(Wc, Hs, [n] * E, gqt, ims, streams)
-        b.record()
-        torch.cuda.synchronize()
-        wall = a.elapsed_time(b) / 1e3
-        del Wc
-    if not all(torch.equal(par[e], seq[e]) for e in range(E)):
-        raise RuntimeError("LDLQ bytes differ between the sequential and the pipelined runs")
-    ms = statistics.mean(times)
-    # one stream: the experts' device time (CUDA events, the first expert left out as warm-up); several: the whole
-    # pipelined pass (CUDA events around it, every stream joined)
-    rate = ne1 * ne0 / (ms / 1e3) / 1e9 if K == 1 else E * ne1 * ne0 / wall / 1e9
-    line = {"metric": "Gweights/s LDLQ-requantized to IQ2_XXS, config 5", "value": rate,
-            "unit": "Gweights/s", "n_gpus": 1, "steps": E, "warmup": 1, "ms_per_step": ne1 * ne0 / rate / 1e6,
-            "higher_is_better": True, "dtype": "f32 weights, f64 feedback", "data": "synthetic (config 5, seeded)",
-            "config": {"workload": "config 5: %d experts 2048 x 7168 -> IQ2_XXS, own Hessian each (7168^2), "
-                       "act order seq, imatrix weights, f64 update; %s" % (
-                           E, "one stream" if K == 1 else "experts alternating over %d CUDA streams" % K)},
-            "expert_latency_ms": ms, "sequential_gweights_s": ne1 * ne0 / (ms / 1e3) / 1e9,
-            "proxy_loss_mean": statistics.mean(losses)}
+    ms = statistics.median(times)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    if g.lib.gpuq_status(1) != 0:
+        raise RuntimeError("device status set during the LDLQ measurement")
+    if rank != 0:
+        return
+    # parity of expert 0 against the reference loop (float64 on the CPU)
+    parity = None
+    if not args.no_cpu:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import ldlq_oracle as LO
+        chk, kind = cpu_checker()
+        H0 = Hs[0].cpu().numpy()
+        W0 = Ws[0][0].cpu().numpy()
+        im0 = ims[0][0].cpu().numpy()
+        t0 = time.perf_counter()
+        quant, dequant, tsize = LO.checker_quant(chk, 16, threads=os.cpu_count() or 1)
+        U, perm, _, _ = LO.prepare_hessian(H0, n, damp=0.01)
+        want, deq_w = LO.quantize_matrix(W0, quant, dequant, tsize, U=U, perm=perm, imatrix=im0, feedback=True)
+        cpu_s = time.perf_counter() - t0
+        got = outs[0].cpu().numpy()[0]
+        same, nb = block_parity(got, want, tsize)
+        deq = chk.dequantize(16, got).reshape(ne1, ne0)
+        lw, lg = LO.proxy_loss(W0, deq_w, H0, n), LO.proxy_loss(W0, deq, H0, n)
+        parity = {"blocks": nb, "identical": same, "share": same / nb, "proxy_loss_rel_diff": abs(lg - lw) / lw,
+                  "checker": "the reference loop restated (oracle/ldlq_oracle.py, float64) with %s" % (
+                      "the reference's host block quantizer" if kind == "reference" else "the C restatement"),
+                  "cpu_s": cpu_s}
+    fl = ldlq_flops(ne1, ne0)
+    total_fl = E * sum(fl.values())
+    peak64 = fp64_peak_tflops(int(os.environ.get("LOCAL_RANK", "0")))
+    rate = world * E * ne1 * ne0 / (ms / 1e3) / 1e9
+    line = {"metric": "Gweights/s LDLQ-requantized to IQ2_XXS, config 5", "value": rate, "unit": "Gweights/s",
+            "n_gpus": world, "steps": len(times), "warmup": 1, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "dtype": "f32 weights, f64 factor and feedback", "data": "synthetic (config 5, seeded)",
+            "config": {"workload": "config 5: %d experts a GPU, 2048 x 7168 -> IQ2_XXS, own Hessian each (7168^2 from "
+                                   "4096 rows), act order seq, imatrix weights; factor + lockstep loop" % E,
+                       "parallelism": "expert-sharded x%d" % world},
+            "per_expert_ms": ms / E, "hessian_build_ms_per_expert": hess_ms / E,
+            "roofline": {"bound": "fp64", "achieved": total_fl / (ms / 1e3) / 1e12, "peak": peak64, "unit": "TFLOP/s",
+                         "frac": total_fl / (ms / 1e3) / 1e12 / peak64, "flop_per_expert": fl,
+                         "peak_source": "trench-gguf_b200/peak.cu float64 FMA rate, measured in this run"},
+            "parity": parity, "clocks": clk.summary()}
     print(json.dumps(line), flush=True)
+
+
+def init_dist(local):
+    """the process group of a torchrun launch (NCCL, bound to this rank's device); anything NCCL prints while it is
+    set up goes to stderr, so rank 0's stdout carries the JSON line alone"""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    sys.stdout.flush()
+    saved = os.dup(1)
+    os.dup2(2, 1)
+    try:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+        dist.barrier()
+    finally:
+        sys.stdout.flush()
+        os.dup2(saved, 1)
+        os.close(saved)
+    return dist
+
+
+def run_ldlq_sharded(args, rank, world, local):
+    """config 5 under torchrun: each rank its own experts (the tensor's experts sharded by expert, no collective)"""
+    import torch
+    import gpuq
+    dist = init_dist(local)
+    dev = torch.device("cuda", local)
+    g = gpuq.Gpuq(device=local)
+    try:
+        run_ldlq(args, g, dev, torch.cuda.Stream(device=dev), None, rank=rank, world=world, dist=dist)
+    finally:
+        dist.destroy_process_group()
 
 
 def main():
     args = parse()
-    if args.config != 2:
-        return run_config(args)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.config == 5 and world > 1:
+        return run_ldlq_sharded(args, rank, world, local)
+    if args.config != 2:
+        return run_config(args)
     if args.impl == "reference":
         return run_reference(args, rank)
     if args.impl == "reference-gpu":
@@ -546,21 +625,7 @@ def main():
     import workloads
     dist = None
     if world > 1:
-        import datetime
-        import torch.distributed as dist
-        torch.cuda.set_device(local)
-        # the communicator is set up here (eager, bound to the device); anything NCCL prints meanwhile goes to stderr,
-        # so rank 0's stdout carries the JSON line alone
-        sys.stdout.flush()
-        saved = os.dup(1)
-        os.dup2(2, 1)
-        try:
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
-            dist.barrier()
-        finally:
-            sys.stdout.flush()
-            os.dup2(saved, 1)
-            os.close(saved)
+        dist = init_dist(local)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     types = args.types.split(",")

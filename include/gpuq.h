@@ -56,13 +56,16 @@ size_t gpuq_requantize_batch(int src, const void * raw, int type, void * dst, in
                              int64_t n_per_row, const float * imatrix);
 
 /* Device API: nblocks contiguous 256-weight super-blocks of d_x (float32, device) -> d_dst (device); block b takes
- * the 256 importance weights d_qw + ((b % qw_mod) / qw_div) * 256. The 256-block i-quants only (not IQ4_NL, not the
- * k-quants), as the reference. On `stream` (a cudaStream_t), no synchronisation. Returns nblocks * block bytes, 0
- * on a bad argument or launch error. Replaces gpuq_quantize_dev, gpuq.hip:2279-2289. */
+ * the 256 importance weights d_qw + ((b % qw_mod) / qw_div) * 256. The 256-block i-quants, as the reference, and
+ * the k-quants Q2_K..Q6_K (an extension: d_qw may then be NULL for ggml's no-imatrix path); not IQ4_NL or Q8_0.
+ * On `stream` (a cudaStream_t), no synchronisation. Returns nblocks * block bytes, 0 on a bad argument or launch
+ * error. Replaces gpuq_quantize_dev, gpuq.hip:2279-2289. */
 size_t gpuq_quantize_dev(int type, const float * d_x, void * d_dst, int64_t nblocks, const float * d_qw,
                          int64_t qw_mod, int64_t qw_div, void * stream);
 
-/* 1 when gpuq_dequantize_dev decodes `type` (the seven grid i-quants and IQ4_XS). Replaces gpuq.hip:2291-2299. */
+/* 1 when gpuq_dequantize_dev decodes `type`: the seven grid i-quants and IQ4_XS (as the reference), and the k-quants
+ * Q2_K..Q6_K (an extension: the reference's LDLQ callers then keep those types on the GPU too, GpuQuant.supported,
+ * tools/ldlq.py:352-354). Replaces gpuq.hip:2291-2299. */
 int gpuq_can_dequantize_type(int type);
 
 /* ggml's to_float on the device: nblocks super-blocks -> nblocks * 256 floats, bit for bit.
@@ -102,6 +105,21 @@ size_t gpuq_requantize_dev(int src, const void * d_raw, int type, void * d_dst, 
  * gpuq_dequantize_dev. d_blk: nblocks x 256 floats. Returns the bytes written to d_err, 0 on error. */
 size_t gpuq_dequantize_error_dev(int type, const void * d_q, const float * d_blk, void * d_err, int f64, int64_t nblocks,
                                  void * stream);
+
+/* LDLQ's error feedback of column block k on the device, in two calls (no counterpart as calls in the reference: they
+ * are tools/ldlq.py:428-429, `Es = E U_kk^-1; Wp[:, :, c1:] -= (Es @ U[c0:c1, c1:]).to(float32)`, as this library's
+ * own float64 tensor-core kernels, every group in one launch). A group is the matrices that share one Hessian factor
+ * (an expert's gate and up, or one matrix), `rows` their rows together.
+ * gpuq_ldlq_scale_dev:  Es = E Rd[k], float64 (Rd: the inverses U_kk^-1 of U's 256 x 256 diagonal blocks)
+ *   d_err, d_es: float64 [ngroups][rows][256]; d_rd: float64 [ngroups][nblk][256][256]. Returns the bytes of d_es.
+ * gpuq_ldlq_update_dev: for every column c >= (k+1)*256: W[c] = f32(W[c] - f32(sum_i Es[i] * U[k*256 + i][c]))
+ *   (float64 sum, float32 cast and subtraction); d_w: float32 [ne0/256][ngroups][rows][256] (column-block major),
+ *   d_u: float64 [ngroups][ne0][ne0]. Returns the bytes of d_w updated.
+ * Float64 arrays 16-byte aligned; on `stream`, no synchronisation; 0 on a bad argument. */
+size_t gpuq_ldlq_scale_dev(const double * d_err, const double * d_rd, double * d_es, int64_t ngroups, int64_t rows,
+                           int64_t nblk, int64_t k, void * stream);
+size_t gpuq_ldlq_update_dev(const double * d_es, const double * d_u, float * d_w, int64_t ngroups, int64_t rows,
+                            int64_t ne0, int64_t k, void * stream);
 
 /* Scratch size of gpuq_requantize_noalloc, held on every GPU that gpuq_init prepares, from gpuq_init to exit. */
 #define GPUQ_NOALLOC_SCRATCH_BYTES ((size_t) 64 << 20)

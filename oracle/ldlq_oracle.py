@@ -76,12 +76,12 @@ def proxy_loss(W, deq, H, n):
     return float(np.einsum("ij,jk,ik->", D, np.asarray(H, dtype=np.float64), D) / max(float(n), 1.0))
 
 
-def checker_quant(checker, typ):
+def checker_quant(checker, typ, threads=1):
     """quant / dequant callables of an oracle.Checker for quantize_matrix"""
     tsize = checker.block_bytes(typ)
 
     def quant(blk, qw):
-        return checker.quantize(typ, blk[None], qw[None]).reshape(blk.shape[0], tsize)
+        return checker.quantize(typ, blk[None], qw[None], threads=threads).reshape(blk.shape[0], tsize)
 
     def dequant(raw):
         return checker.dequantize(typ, raw).reshape(raw.shape[0], QK)

@@ -1390,7 +1390,91 @@ size_t orc_quantize_blocks(int type, const float * x, void * y, int64_t nblocks,
     return o_blocks(type, x, qw, y, nblocks, qw_mod, qw_div, INT64_MAX, nthreads);
 }
 
+/* ggml's dequantize_row_q2_K .. q6_K (ggml-quants.c; the reference leaves them to ggml on the CPU): one super-block,
+ * in ggml's output order and operand order. */
+static void o_scale_min_k4(int j, const uint8_t * q, int * sc, int * m) {
+    if (j < 4) { *sc = q[j] & 63; *m = q[j + 4] & 63; }
+    else { *sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4); *m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4); }
+}
+
+static int o_dequant_kquant(int type, const uint8_t * x, float * y) {
+    uint16_t h0, h1;
+    if (type == O_Q2_K) {                       /* scales[16] qs[64] d dmin */
+        memcpy(&h0, x + 80, 2); memcpy(&h1, x + 82, 2);
+        const float d = o_unhalf(h0), dmin = o_unhalf(h1);
+        for (int half = 0; half < 2; ++half) {
+            const uint8_t * qs = x + 16 + 32 * half;
+            for (int j = 0; j < 4; ++j)
+                for (int part = 0; part < 2; ++part) {
+                    const uint8_t sc = x[8 * half + 2 * j + part];
+                    const float dl = d * (sc & 0xF), ml = dmin * (sc >> 4);
+                    for (int l = 0; l < 16; ++l) *y++ = dl * ((int8_t) ((qs[16 * part + l] >> (2 * j)) & 3)) - ml;
+                }
+        }
+        return 0;
+    }
+    if (type == O_Q3_K) {                       /* hmask[32] qs[64] scales[12] d */
+        memcpy(&h0, x + 108, 2);
+        const float d_all = o_unhalf(h0);
+        int8_t scales[16];
+        for (int i = 0; i < 16; ++i) {
+            const uint8_t lo = x[96 + (i & 7)];
+            scales[i] = (int8_t) ((i < 8 ? lo & 0xF : lo >> 4) | (((x[104 + (i & 3)] >> (2 * (i >> 2))) & 3) << 4));
+        }
+        for (int half = 0; half < 2; ++half) {
+            const uint8_t * qs = x + 32 + 32 * half;
+            for (int j = 0; j < 4; ++j) {
+                const uint8_t m = (uint8_t) (1u << (4 * half + j));
+                for (int part = 0; part < 2; ++part) {
+                    const float dl = d_all * (scales[8 * half + 2 * j + part] - 32);
+                    for (int l = 0; l < 16; ++l)
+                        *y++ = dl * ((int8_t) ((qs[16 * part + l] >> (2 * j)) & 3) - ((x[16 * part + l] & m) ? 0 : 4));
+                }
+            }
+        }
+        return 0;
+    }
+    if (type == O_Q4_K || type == O_Q5_K) {     /* d dmin scales[12] (qh[32]) qs[128] */
+        memcpy(&h0, x, 2); memcpy(&h1, x + 2, 2);
+        const float d = o_unhalf(h0), dmin = o_unhalf(h1);
+        const uint8_t * qs = x + (type == O_Q4_K ? 16 : 48);
+        for (int c = 0; c < 4; ++c)
+            for (int hi = 0; hi < 2; ++hi) {
+                int sc, m;
+                o_scale_min_k4(2 * c + hi, x + 4, &sc, &m);
+                const float d1 = d * sc, m1 = dmin * m;
+                for (int l = 0; l < 32; ++l) {
+                    const int v = hi ? qs[32 * c + l] >> 4 : qs[32 * c + l] & 0xF;
+                    *y++ = type == O_Q4_K ? d1 * v - m1 : d1 * (v + ((x[16 + l] >> (2 * c + hi)) & 1 ? 16 : 0)) - m1;
+                }
+            }
+        return 0;
+    }
+    if (type == O_Q6_K) {                       /* ql[128] qh[64] scales[16] d */
+        memcpy(&h0, x + 208, 2);
+        const float d = o_unhalf(h0);
+        for (int half = 0; half < 2; ++half)
+            for (int qq = 0; qq < 4; ++qq)
+                for (int l = 0; l < 32; ++l) {
+                    const uint8_t ql = x[64 * half + 32 * (qq & 1) + l], qh = x[128 + 32 * half + l];
+                    const int v = ((qq < 2 ? ql & 0xF : ql >> 4) | (((qh >> (2 * qq)) & 3) << 4)) - 32;
+                    const int8_t sc = (int8_t) x[192 + 8 * half + l / 16 + 2 * qq];
+                    *y++ = d * sc * (int8_t) v;
+                }
+        return 0;
+    }
+    return 1;
+}
+
+static int o_is_kquant256(int t) { return t == O_Q2_K || t == O_Q3_K || t == O_Q4_K || t == O_Q5_K || t == O_Q6_K; }
+
 size_t orc_dequantize(int type, const void * q, float * out, int64_t nblocks) {
+    if (o_is_kquant256(type)) {
+        const size_t bb = o_bytes(type);
+        for (int64_t b = 0; b < nblocks; ++b)
+            if (o_dequant_kquant(type, (const uint8_t *) q + b * bb, out + b * QK)) return 0;
+        return (size_t) nblocks * QK * 4;
+    }
     const otab_t * T = dequant_tab(type);
     if (type != O_IQ4_XS && !T) return 0;
     const size_t bb = o_bytes(type);

@@ -138,6 +138,40 @@ def test_device_api_quantize_dequantize(gpuq, oracle):
     assert gpuq.lib.gpuq_status(1) == 0
 
 
+@pytest.mark.parametrize("name", ["Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K"])
+def test_device_api_kquants(gpuq, oracle, name):
+    """the k-quants through the device API (an extension of the reference's, which has none): gpuq_quantize_dev with
+    and without importance rows (block b weighted by row (b % qw_mod) / qw_div) == ggml's quantizer, and
+    gpuq_dequantize_dev == ggml's dequantize_row_q*_K, bit for bit"""
+    import torch
+    rng = np.random.default_rng(13)
+    B, rows = 2, 6
+    x = (rng.standard_t(4, (B * rows, 256)) * 0.02).astype(np.float32)
+    qw = rng.gamma(1.0, 1.0, (B, 256)).astype(np.float32)
+    t = TYPES[name]
+    bb = gpuq.block_bytes(t)
+    assert gpuq.lib.gpuq_can_dequantize_type(t) == 1
+    st = torch.cuda.current_stream().cuda_stream
+    dx = torch.from_numpy(x).cuda()
+    dq = torch.from_numpy(qw).cuda()
+    for with_qw in (True, False):
+        out = torch.zeros(B * rows * bb, dtype=torch.uint8, device="cuda")
+        n = gpuq.lib.gpuq_quantize_dev(t, dev_ptr(dx), dev_ptr(out), B * rows, dev_ptr(dq) if with_qw else None,
+                                       B * rows, rows, st)
+        assert n == B * rows * bb, gpuq.error()
+        torch.cuda.synchronize()
+        if with_qw:
+            want = oracle.quantize_blocks(t, x, qw, B * rows, rows)
+        else:
+            want = oracle.quantize(t, x, None)
+        assert np.array_equal(out.cpu().numpy(), want), (name, with_qw)
+        f = torch.empty(B * rows * 256, dtype=torch.float32, device="cuda")
+        assert gpuq.lib.gpuq_dequantize_dev(t, dev_ptr(out), dev_ptr(f), B * rows, st) == f.numel() * 4
+        torch.cuda.synchronize()
+        assert np.array_equal(f.cpu().numpy().view(np.uint32), oracle.dequantize(t, want).view(np.uint32)), name
+    assert gpuq.lib.gpuq_status(1) == 0
+
+
 @pytest.mark.parametrize("src", ["F16", "BF16", "Q8_0", "MXFP4"])
 def test_device_api_decode(gpuq, golden, src):
     import torch

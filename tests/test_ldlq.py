@@ -163,9 +163,72 @@ def test_gpu_ldlq_batch_and_larger_case(tables, oracle):
 
 
 @pytest.mark.gpu
-def test_gpu_experts_pipelined_over_streams(tables):
-    """ldlq_experts_torch (experts alternating over CUDA streams, nothing waiting for the device in between) gives
-    every expert the bytes of prepare_hessian_torch + quantize_matrix_torch run alone on one stream"""
+def test_gpu_feedback_kernels_against_torch(tables):
+    """gpuq_ldlq_scale_dev (Es = E U_kk^-1 as E R_kk) and gpuq_ldlq_update_dev (W -= f32(Es U_k,rest)) on random data
+    of two groups: Es equals torch's float64 product to rounding, and W equals torch's float32 subtraction of the
+    float32-cast product except where the float64 sums of the two differ in their last bits right at a float32
+    rounding boundary (at most 1 ulp, on a tiny share of the weights)"""
+    torch, G, ldlq_gpu, g = _gpu_setup(tables)
+    dev = torch.device("cuda")
+    gen = torch.Generator(device=dev).manual_seed(3)
+    P, M, ne0, nblk = 2, 192, 1024, 4                      # (192 rows: a partial 128-row tile)
+    E = torch.randn(P, M, 256, dtype=torch.float64, device=dev, generator=gen) * 1e-3
+    U = torch.triu(torch.randn(P, ne0, ne0, dtype=torch.float64, device=dev, generator=gen))
+    Rd = torch.randn(P, nblk, 256, 256, dtype=torch.float64, device=dev, generator=gen)
+    W = torch.randn(nblk, P, M, 256, dtype=torch.float32, device=dev, generator=gen)
+    Es = torch.empty_like(E)
+    st = torch.cuda.current_stream().cuda_stream
+    for k in range(nblk - 1):
+        assert g.lib.gpuq_ldlq_scale_dev(E.data_ptr(), Rd.data_ptr(), Es.data_ptr(), P, M, nblk, k, st) == E.numel() * 8
+        want_es = torch.bmm(E, Rd[:, k])
+        torch.cuda.synchronize()
+        assert torch.allclose(Es, want_es, rtol=1e-12, atol=1e-15)
+        Wrows = W.permute(1, 2, 0, 3).reshape(P, M, ne0)                   # row view of the column-block-major W
+        upd = torch.bmm(Es, U[:, k * 256:(k + 1) * 256, (k + 1) * 256:]).to(torch.float32)
+        want = Wrows.clone()
+        want[:, :, (k + 1) * 256:] -= upd
+        n = g.lib.gpuq_ldlq_update_dev(Es.data_ptr(), U.data_ptr(), W.data_ptr(), P, M, ne0, k, st)
+        assert n == P * M * (ne0 - (k + 1) * 256) * 4, g.error()
+        torch.cuda.synchronize()
+        got = W.permute(1, 2, 0, 3).reshape(P, M, ne0)
+        ulps = (got.view(torch.int32).long() - want.view(torch.int32).long()).abs()
+        assert int(ulps.max()) <= 1
+        assert float((ulps != 0).double().mean()) < 1e-4
+        assert torch.equal(got[:, :, :(k + 1) * 256], want[:, :, :(k + 1) * 256])   # columns before c1 untouched
+    # argument checks
+    assert g.lib.gpuq_ldlq_update_dev(Es.data_ptr(), U.data_ptr(), W.data_ptr(), P, M, ne0, nblk - 1, st) == 0
+    assert g.lib.gpuq_ldlq_scale_dev(E.data_ptr() + 8, Rd.data_ptr(), Es.data_ptr(), P, M, nblk, 0, st) == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", ["Q4_K", "Q6_K", "IQ4_XS"])
+def test_gpu_ldlq_other_types_against_reference_loop(tables, oracle, name):
+    """LDLQ of the other types the reference's LDLQ takes (tools/requant_experts.py:195-196: the k-quants of dense
+    tensors, IQ4_XS): the GPU loop against the restatement's loop on the same U, 64 x 1024 (4 blocks)"""
+    torch, G, ldlq_gpu, g = _gpu_setup(tables)
+    ne1, ne0, n = 64, 1024, 4096
+    H, im = LO.synthetic_hessian(ne0, n, seed=57)
+    W = (np.random.default_rng(58).standard_t(5, (ne1, ne0)) * 0.02).astype(np.float32)
+    U, perm, diag_n, _ = LO.prepare_hessian(H, n, damp=0.01)
+    typ = G.TYPES[name]
+    gqt = ldlq_gpu.GpuQuant(g, typ)
+    assert ldlq_gpu.GpuQuant.supported(g, typ)
+    dev = torch.device("cuda")
+    out = ldlq_gpu.quantize_matrix_torch(torch.from_numpy(W[None].copy()).to(dev), gqt, U=torch.from_numpy(U).to(dev),
+                                         perm=torch.from_numpy(perm).to(dev), diag_n=torch.from_numpy(diag_n).to(dev),
+                                         imatrix=torch.from_numpy(im[None].copy()).to(dev)).cpu().numpy()[0]
+    quant, dequant, tsize = LO.checker_quant(oracle, typ)
+    want, deq_w = LO.quantize_matrix(W, quant, dequant, tsize, U=U, perm=perm, imatrix=im, feedback=True)
+    same = (out.reshape(ne1, -1, tsize) == want.reshape(ne1, -1, tsize)).all(-1).mean()
+    assert same >= IDENTICAL_MIN, same
+    lw = LO.proxy_loss(W, deq_w, H, n)
+    assert abs(LO.proxy_loss(W, oracle.dequantize(typ, out).reshape(ne1, ne0), H, n) - lw) <= LOSS_RTOL * lw
+
+
+@pytest.mark.gpu
+def test_gpu_experts_in_lockstep(tables):
+    """ldlq_experts (every expert's factor, then one loop over all experts, one launch of each kernel a block) gives
+    every expert the bytes of prepare_hessian_torch + quantize_matrix_torch run for it alone"""
     torch, G, ldlq_gpu, g = _gpu_setup(tables)
     dev = torch.device("cuda")
     ne1, ne0, n = 64, 1024, 2048
@@ -181,9 +244,35 @@ def test_gpu_experts_pipelined_over_streams(tables):
     for e in range(3):
         U, perm, diag_n, _ = ldlq_gpu.prepare_hessian_torch(Hs[e], n, device=dev, out="torch")
         alone.append(ldlq_gpu.quantize_matrix_torch(Ws[e].clone(), gqt, U=U, perm=perm, diag_n=diag_n, imatrix=ims[e]))
-    streams = [torch.cuda.Stream(device=dev) for _ in range(2)]
-    piped = ldlq_gpu.ldlq_experts_torch([w.clone() for w in Ws], Hs, [n] * 3, gqt, ims, streams)
+    together = ldlq_gpu.ldlq_experts([w.clone() for w in Ws], Hs, [n] * 3, gqt, ims)
     torch.cuda.synchronize()
     for e in range(3):
-        assert torch.equal(piped[e], alone[e]), e
+        assert torch.equal(together[e], alone[e]), e
 
+
+@pytest.mark.gpu
+def test_gpu_ldlq_full_config5_shape_against_reference_loop(tables, oracle):
+    """one 2048 x 7168 expert with its own 7168^2 Hessian (config 5's recipe: X = (Z + A B) diag(g), n = 4096) through
+    the whole GPU path - the float64 factor, then the lockstep loop - against the reference's loop (the restatement,
+    float64 on the CPU, with the reference's own block quantizer where it is built): at least 99.9 % identical
+    super-blocks and the proxy loss within 1e-5, at the full 28-block depth of the feedback chain"""
+    torch, G, ldlq_gpu, g = _gpu_setup(tables)
+    import oracle as orc_mod
+    chk = orc_mod.Checker("reference", tables) if orc_mod.available("reference") else oracle
+    ne1, ne0, n = 2048, 7168, 4096
+    H, im = LO.synthetic_hessian(ne0, n, seed=105)
+    rng = np.random.default_rng(205)
+    W = (rng.standard_t(5, (ne1, ne0)) * 0.02 / np.sqrt(5.0 / 3.0)).astype(np.float32)
+    typ = G.TYPES["IQ2_XXS"]
+    quant, dequant, tsize = LO.checker_quant(chk, typ, threads=os.cpu_count() or 1)
+    U, perm, _, _ = LO.prepare_hessian(H, n, damp=0.01)
+    want, deq_w = LO.quantize_matrix(W, quant, dequant, tsize, U=U, perm=perm, imatrix=im, feedback=True)
+    dev = torch.device("cuda")
+    gqt = ldlq_gpu.GpuQuant(g, typ)
+    got = ldlq_gpu.ldlq_experts([torch.from_numpy(W[None].copy()).to(dev)], [torch.from_numpy(H).to(dev)], [n], gqt,
+                                [torch.from_numpy(im[None].copy()).to(dev)])[0].cpu().numpy()[0]
+    same = (got.reshape(ne1, -1, tsize) == want.reshape(ne1, -1, tsize)).all(-1).mean()
+    assert same >= IDENTICAL_MIN, same
+    deq = oracle.dequantize(typ, got).reshape(ne1, ne0)
+    loss, lw = LO.proxy_loss(W, deq, H, n), LO.proxy_loss(W, deq_w, H, n)
+    assert abs(loss - lw) <= LOSS_RTOL * lw, (loss, lw)

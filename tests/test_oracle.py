@@ -67,6 +67,18 @@ def test_oracle_dequant_golden_and_gguf(oracle, golden, name):
     assert np.array_equal(got, ref.reshape(-1).astype(np.float32))
 
 
+@pytest.mark.parametrize("name", ["Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K"])
+def test_oracle_kquant_dequant_matches_gguf(oracle, golden, name):
+    """ggml's dequantize_row_q*_K (the reference leaves it to ggml on the CPU): the restatement against gguf-py's
+    dequantizers, bit for bit, on the reference's own k-quant bytes of both modes"""
+    from gguf import quants as gq, GGMLQuantizationType as G
+    for mode in (0, 1):
+        q = golden["selftest_%s_%d" % (name, mode)]
+        got = oracle.dequantize(TYPES[name], q)
+        ref = gq.dequantize(q.reshape(-1, oracle.block_bytes(TYPES[name])), G[name]).reshape(-1)
+        assert np.array_equal(got.view(np.uint32), ref.astype(np.float32).view(np.uint32)), (name, mode)
+
+
 def test_oracle_q8_0_matches_gguf(oracle):
     from gguf import quants as gq, GGMLQuantizationType as G
     rng = np.random.default_rng(7)

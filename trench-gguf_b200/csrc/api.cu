@@ -561,15 +561,16 @@ size_t gpuq_requantize(int src, const void * raw, int type, void * dst, int64_t 
 
 size_t gpuq_quantize_dev(int type, const float * d_x, void * d_dst, int64_t nblocks, const float * d_qw, int64_t qw_mod,
                          int64_t qw_div, void * stream) {
-    // the types of the reference's device API: the 256-block i-quants (not IQ4_NL, not the k-quants)
-    if (!block_bytes(type) || type == IQ4_NL || is_kquant(type) || nblocks <= 0 || qw_mod <= 0 || qw_div <= 0 || !d_x || !d_dst) {
+    // the reference's device API takes the 256-block i-quants; this library also takes the k-quants (Q2_K..Q6_K, which
+    // its gpuq_can_dequantize_type reports, so LDLQ callers run them on the GPU); not the 32-block IQ4_NL and Q8_0
+    if (!block_bytes(type) || block_len(type) != QK || nblocks <= 0 || qw_mod <= 0 || qw_div <= 0 || !d_x || !d_dst) {
         set_err("gpuq_quantize_dev: unsupported type %d or bad arguments", type);
         return 0;
     }
     Device * d = current_device();
     if (!d) { set_err("gpuq_quantize_dev: current device not initialized"); return 0; }
     if (needs_search_tab(type) && !d->tab(type)) { set_err("gpuq_quantize_dev: no tables for type %d", type); return 0; }
-    if (!d_qw && type != IQ4_XS) { set_err("gpuq_quantize_dev: type %d needs importance weights", type); return 0; }
+    if (!d_qw && !takes_no_imatrix(type)) { set_err("gpuq_quantize_dev: type %d needs importance weights", type); return 0; }
     LaunchArgs a{};
     a.src_type = SRC_F32; a.src = d_x; a.qw = d_qw; a.qw_mod = qw_mod; a.qw_div = qw_div; a.qw_mat = INT64_MAX;
     a.out = d_dst; a.nblocks = nblocks;
@@ -612,7 +613,7 @@ int gpuq_can_dequantize_type(int type) {
             std::lock_guard<std::mutex> lk(g_mu);
             return !g_active.empty() && g_active[0]->dq_grid(type) ? 1 : 0;
         }
-        case IQ4_XS: return 1;
+        case IQ4_XS: case Q2_K: case Q3_K: case Q4_K: case Q5_K: case Q6_K: return 1;
         default: return 0;
     }
 }
@@ -641,6 +642,35 @@ size_t gpuq_dequantize_error_dev(int type, const void * d_q, const float * d_blk
         return 0;
     }
     return (size_t) nblocks * QK * (f64 ? 8 : 4);
+}
+
+namespace {
+bool misaligned(const void * p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) != 0; }
+}  // namespace
+
+size_t gpuq_ldlq_scale_dev(const double * d_err, const double * d_rd, double * d_es, int64_t ngroups, int64_t rows,
+                           int64_t nblk, int64_t k, void * stream) {
+    if (!d_err || !d_rd || !d_es || ngroups <= 0 || rows <= 0 || nblk <= 0 || k < 0 || k >= nblk ||
+        misaligned(d_err, 16) || misaligned(d_rd, 16) || misaligned(d_es, 16)) {
+        set_err("gpuq_ldlq_scale_dev: bad arguments (0 <= k < nblk; every pointer 16-byte aligned)");
+        return 0;
+    }
+    const cudaError_t e = launch_ldlq_scale(d_err, d_rd, d_es, ngroups, rows, nblk, (int) k, (cudaStream_t) stream);
+    if (e != cudaSuccess) { set_err("gpuq_ldlq_scale_dev: launch failed: %s", cudaGetErrorString(e)); return 0; }
+    return (size_t) ngroups * rows * QK * 8;
+}
+
+size_t gpuq_ldlq_update_dev(const double * d_es, const double * d_u, float * d_w, int64_t ngroups, int64_t rows,
+                            int64_t ne0, int64_t k, void * stream) {
+    if (!d_es || !d_u || !d_w || ngroups <= 0 || rows <= 0 || ne0 <= 0 || ne0 % QK || k < 0 || (k + 1) * QK >= ne0 ||
+        misaligned(d_es, 16) || misaligned(d_u, 16) || misaligned(d_w, 8)) {
+        set_err("gpuq_ldlq_update_dev: bad arguments (k must leave columns to update; ne0 %% 256 == 0; Es and U 16-byte "
+                "aligned, W 8-byte aligned)");
+        return 0;
+    }
+    const cudaError_t e = launch_ldlq_update(d_es, d_u, d_w, ngroups, rows, ne0, (int) k, (cudaStream_t) stream);
+    if (e != cudaSuccess) { set_err("gpuq_ldlq_update_dev: launch failed: %s", cudaGetErrorString(e)); return 0; }
+    return (size_t) ngroups * rows * (ne0 - (k + 1) * QK) * 4;
 }
 
 size_t gpuq_dequantize_src_dev(int src, const void * d_raw, float * d_out, int64_t n, void * stream) {

@@ -1,5 +1,6 @@
-// dequant.cu - ggml's to_float of the i-quant types (dequantize_row_iq*, trench-gguf gpuq.hip:1850-2028) and the
-// source decoder (kdq, gpuq.hip:2123-2141), HBM-bound.
+// dequant.cu - ggml's to_float of the i-quant types (dequantize_row_iq*, trench-gguf gpuq.hip:1850-2028), of the
+// k-quants (ggml's dequantize_row_q2_K .. q6_K, which the reference leaves to ggml on the CPU) and the source decoder
+// (kdq, gpuq.hip:2123-2141), HBM-bound.
 //
 // Layout: one warp a 256-weight super-block, lane l producing weights 8l..8l+7 (its 32-weight sub-block l/4 and
 // 8-weight group l%4), stored as two 16-byte writes: a warp writes its 1 KiB of floats fully coalesced. Every
@@ -24,10 +25,70 @@ __device__ __forceinline__ uint8_t gbyte(const uint64_t * grid, int gi, int j) {
 
 __constant__ int8_t c_iq4nl[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
 
+// ggml's 6-bit k-quant scale and min j (get_scale_min_k4): 12 bytes hold 8 pairs
+__device__ __forceinline__ void scale_min_k4(int j, const uint8_t * q, int & sc, int & m) {
+    if (j < 4) { sc = q[j] & 63; m = q[j + 4] & 63; }
+    else { sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4); m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4); }
+}
+
+// ggml's dequantize_row_q2_K .. q6_K (ggml-quants.c), weights v0 .. v0+7 of one super-block (v0 = 8 * lane: all
+// eight share one sub-block scale). Every expression keeps ggml's operand order: the products that can round
+// (q4_K/q5_K's d1 * q - m1, q6_K's (d * sc) * q) round exactly as ggml's C does.
+template <int T>
+__device__ __forceinline__ void dq8_kquant(const uint8_t * q, int v0, float * y) {
+    if constexpr (T == Q2_K) {            // scales[16] qs[64] d dmin
+        const float d = half_to_float((uint16_t) ld_u16(q + 80)), dmin = half_to_float((uint16_t) ld_u16(q + 82));
+        const int h = v0 >> 7, j = (v0 >> 5) & 3, part = (v0 >> 4) & 1, l0 = v0 & 15;
+        const uint8_t sc = q[8 * h + 2 * j + part];
+        const float dl = d * (sc & 0xF), ml = dmin * (sc >> 4);
+        const uint8_t * qs = q + 16 + 32 * h + 16 * part + l0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = dl * ((int8_t) ((qs[i] >> (2 * j)) & 3)) - ml;
+    } else if constexpr (T == Q3_K) {     // hmask[32] qs[64] scales[12] d
+        const float d_all = half_to_float((uint16_t) ld_u16(q + 108));
+        const int h = v0 >> 7, j = (v0 >> 5) & 3, part = (v0 >> 4) & 1, l0 = v0 & 15;
+        const int si = 8 * h + 2 * j + part;
+        const uint8_t lo = q[96 + (si & 7)];
+        const int sc6 = (si < 8 ? lo & 0xF : lo >> 4) | (((q[104 + (si & 3)] >> (2 * (si >> 2))) & 3) << 4);
+        const float dl = d_all * ((int8_t) sc6 - 32);
+        const uint8_t * qs = q + 32 + 32 * h + 16 * part + l0;
+        const uint8_t * hm = q + 16 * part + l0;
+        const uint8_t m = (uint8_t) (1u << (4 * h + j));
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = dl * ((int8_t) ((qs[i] >> (2 * j)) & 3) - ((hm[i] & m) ? 0 : 4));
+    } else if constexpr (T == Q4_K || T == Q5_K) {   // d dmin scales[12] (qh[32]) qs[128]
+        const float d = half_to_float((uint16_t) ld_u16(q)), dmin = half_to_float((uint16_t) ld_u16(q + 2));
+        const int c = v0 >> 6, hi = (v0 >> 5) & 1, l0 = v0 & 31;
+        int sc, m;
+        scale_min_k4(2 * c + hi, q + 4, sc, m);
+        const float d1 = d * sc, m1 = dmin * m;
+        const uint8_t * qs = q + (T == Q4_K ? 16 : 48) + 32 * c + l0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int v = hi ? qs[i] >> 4 : qs[i] & 0xF;
+            if constexpr (T == Q4_K) y[i] = d1 * v - m1;
+            else y[i] = d1 * (v + ((q[16 + l0 + i] >> (2 * c + hi)) & 1 ? 16 : 0)) - m1;
+        }
+    } else {                              // Q6_K: ql[128] qh[64] scales[16] d
+        const float d = half_to_float((uint16_t) ld_u16(q + 208));
+        const int h = v0 >> 7, qq = (v0 >> 5) & 3, l0 = v0 & 31;
+        const uint8_t * ql = q + 64 * h + 32 * (qq & 1) + l0;
+        const uint8_t * qh = q + 128 + 32 * h + l0;
+        const int8_t sc = (int8_t) q[192 + 8 * h + (l0 >> 4) + 2 * qq];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int v = ((qq < 2 ? ql[i] & 0xF : ql[i] >> 4) | (((qh[i] >> (2 * qq)) & 3) << 4)) - 32;
+            y[i] = d * sc * (int8_t) v;
+        }
+    }
+}
+
 template <int T>
 __device__ __forceinline__ void dq8(const uint8_t * q, int lane, const uint64_t * G, float * y) {
     const int ib = lane >> 2, l = lane & 3;
-    if constexpr (T == IQ4_XS) {
+    if constexpr (T == Q2_K || T == Q3_K || T == Q4_K || T == Q5_K || T == Q6_K) {
+        dq8_kquant<T>(q, 8 * lane, y);
+    } else if constexpr (T == IQ4_XS) {
         const float d = half_to_float((uint16_t) ld_u16(q));
         const uint32_t sh = ld_u16(q + 2);
         const int ls = ((q[4 + ib / 2] >> (4 * (ib % 2))) & 0xf) | (((sh >> (2 * ib)) & 3) << 4);
@@ -191,6 +252,11 @@ cudaError_t launch_dequant(int type, const void * q, float * out, int64_t nblock
         case IQ1_S:   k_dequant<IQ1_S><<<g, 256, 0, st>>>(qb, out, nblocks, tab.grid); break;
         case IQ1_M:   k_dequant<IQ1_M><<<g, 256, 0, st>>>(qb, out, nblocks, tab.grid); break;
         case IQ4_XS:  k_dequant<IQ4_XS><<<g, 256, 0, st>>>(qb, out, nblocks, tab.grid); break;
+        case Q2_K:    k_dequant<Q2_K><<<g, 256, 0, st>>>(qb, out, nblocks, nullptr); break;
+        case Q3_K:    k_dequant<Q3_K><<<g, 256, 0, st>>>(qb, out, nblocks, nullptr); break;
+        case Q4_K:    k_dequant<Q4_K><<<g, 256, 0, st>>>(qb, out, nblocks, nullptr); break;
+        case Q5_K:    k_dequant<Q5_K><<<g, 256, 0, st>>>(qb, out, nblocks, nullptr); break;
+        case Q6_K:    k_dequant<Q6_K><<<g, 256, 0, st>>>(qb, out, nblocks, nullptr); break;
         default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
@@ -211,6 +277,11 @@ cudaError_t launch_dequant_error(int type, const void * q, const float * blk, vo
         case IQ1_S:   DE(IQ1_S); break;
         case IQ1_M:   DE(IQ1_M); break;
         case IQ4_XS:  DE(IQ4_XS); break;
+        case Q2_K:    DE(Q2_K); break;
+        case Q3_K:    DE(Q3_K); break;
+        case Q4_K:    DE(Q4_K); break;
+        case Q5_K:    DE(Q5_K); break;
+        case Q6_K:    DE(Q6_K); break;
         default: return cudaErrorInvalidValue;
     }
 #undef DE

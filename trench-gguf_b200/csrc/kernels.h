@@ -32,6 +32,14 @@ cudaError_t launch_dequant(int type, const void * q, float * out, int64_t nblock
 // LDLQ block error E = blk - to_float(q), float32 maths, stored as float64 (f64) or float32
 cudaError_t launch_dequant_error(int type, const void * q, const float * blk, void * err, bool f64, int64_t nblocks,
                                  DequantTab tab, cudaStream_t st);
+// LDLQ's error-feedback steps of block k (ldlq.cu), every group (matrices sharing one factor) in one launch:
+// scale Es = E Rd[k] (Rd [ngroups][nblk][256][256] f64: U_kk^-1), E and Es [ngroups][rows][256] f64;
+// update W~[:, c] = f32(W~[:, c] - f32(Es U[k*256.., c])) for c >= (k+1)*256, W~ column-block major
+// [nblk][ngroups][rows][256] f32, U [ngroups][ne0][ne0] f64
+cudaError_t launch_ldlq_scale(const double * E, const double * Rd, double * Es, int64_t ngroups, int64_t rows,
+                              int64_t nblk, int k, cudaStream_t st);
+cudaError_t launch_ldlq_update(const double * Es, const double * U, float * W, int64_t ngroups, int64_t rows, int64_t ne0,
+                               int k, cudaStream_t st);
 // source bytes (F32 / F16 / BF16 / Q8_0 / MXFP4) -> n floats
 cudaError_t launch_decode(int src, const void * raw, float * out, int64_t n, cudaStream_t st);
 

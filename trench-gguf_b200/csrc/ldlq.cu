@@ -1,0 +1,174 @@
+// ldlq.cu - the error-feedback steps of LDLQ / GPTQ re-quantization (trench-gguf tools/ldlq.py:391-431) on sm_100a.
+//
+// What is computed, for step k of the 256-column block loop and every group g (the matrices that share one Hessian
+// factor: an expert's gate and up, or one matrix), in the reference's arithmetic (tools/ldlq.py:427-429):
+//     Es = E U_kk^-1                                                        (float64; "scale")
+//     W~[:, c] = f32( W~[:, c] - f32( sum_i Es[:, i] * U[k*256 + i, c] ) )   for every column c >= (k+1)*256 ("update")
+// where E = f32(W~_k - to_float(Q_k)) widened to float64 is the block's rounding error and U the upper Cholesky factor
+// of the damped Hessian's inverse. U_kk^-1 is the diagonal block R_kk of the Hessian's own factor R (Hp = R R^T, U =
+// R^-1), so the first product is a plain multiplication, as the second. Sums in float64, the cast and the subtraction
+// in float32, as the reference's `Wp[:, :, c1:] -= (Es @ U[c0:c1, c1:]).to(float32)`.
+//
+// How: one float64 GEMM kernel on the tensor cores (mma.sync m8n8k4 f64: sm_100a's FP64 matrix path - tcgen05 has no
+// float64 kind) with two epilogues: float64 stores (scale), or the float32 read-modify-write of W~ (update). CTA tile
+// 128 rows x 64 columns, 8 warps of 32 x 32, K = 256 in chunks of 32 staged by cp.async into a two-stage ring; row
+// strides padded by 4 doubles so the fragment loads of a half-warp hit 16 distinct bank pairs. One launch covers every
+// group (grid z).
+//
+// Layouts (all device memory, row-major):
+//   W~  float32 [nblk][ngroups][rows][256]  (column block major: block k of every group is one contiguous
+//       [ngroups * rows, 256] slab, the quantize kernel's input)
+//   E, Es  float64 [ngroups][rows][256]
+//   U   float64 [ngroups][ne0][ne0] (update: the rows of block k and the columns after it are read)
+//   Rd  float64 [ngroups][nblk][256][256] (scale: the diagonal blocks U_kk^-1)
+#include <cstdint>
+#include "common.cuh"
+#include "kernels.h"
+
+namespace gq {
+namespace {
+
+constexpr int UBM = 128, UBN = 64, UBK = 32, UTHREADS = 256, USTAGES = 2;
+constexpr int APAD = UBK + 4;   // doubles a row of the A (E) tile
+constexpr int BPAD = UBN + 4;   // doubles a row of the B (G) tile
+
+struct UpdSmem {
+    double a[USTAGES][UBM * APAD];
+    double b[USTAGES][UBK * BPAD];
+};
+
+__device__ __forceinline__ void cp_async16(void * smem, const void * gmem) {
+    const unsigned s = (unsigned) __cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
+// D = A (8x4) * B (4x8) + D, float64; lane l holds A[l/4][l%4], B[l%4][l/4], D[l/4][2*(l%4) + {0, 1}]
+__device__ __forceinline__ void dmma_8x8x4(double (&d)[2], double a, double b) {
+    asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};\n"
+                 : "+d"(d[0]), "+d"(d[1])
+                 : "d"(a), "d"(b));
+}
+
+// One tile of A [rows][256] (group g) times B [256][ldb] (columns n0 .. n0+63), float64. SUB: W~ -= f32(product) at
+// columns n0.. of the column-block-major W~; else the product is stored to Out [ngroups][rows][256] at columns n0..
+template <bool SUB>
+__global__ void __launch_bounds__(UTHREADS, 2) k_ldlq_gemm(const double * __restrict__ A, const double * __restrict__ B,
+                                                           int64_t b_group_stride, int64_t ldb, int64_t n_first,
+                                                           void * __restrict__ out, int64_t ngroups, int64_t rows) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    UpdSmem & sm = *reinterpret_cast<UpdSmem *>(smem_raw);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int wm = warp >> 1, wn = warp & 1;             // 4 x 2 warps
+    const int64_t g = blockIdx.z;
+    const int64_t m0 = (int64_t) blockIdx.y * UBM;
+    const int64_t n0 = n_first + (int64_t) blockIdx.x * UBN;   // first column of the tile (in B's columns)
+    const double * Eg = A + g * rows * QK;
+    const double * Gk = B + g * b_group_stride;
+    const int64_t ne0 = ldb;
+
+    auto load = [&](int stage, int kk) {
+        // A: 128 rows x 32 doubles = 2,048 16-byte pieces; B: 32 rows x 64 doubles = 1,024 pieces
+#pragma unroll
+        for (int i = tid; i < UBM * (UBK / 2); i += UTHREADS) {
+            const int r = i / (UBK / 2), ch = i % (UBK / 2);
+            double * dst = &sm.a[stage][r * APAD + ch * 2];
+            if (m0 + r < rows) cp_async16(dst, Eg + (m0 + r) * QK + kk + ch * 2);
+            else { dst[0] = 0.0; dst[1] = 0.0; }
+        }
+#pragma unroll
+        for (int i = tid; i < UBK * (UBN / 2); i += UTHREADS) {
+            const int r = i / (UBN / 2), ch = i % (UBN / 2);
+            cp_async16(&sm.b[stage][r * BPAD + ch * 2], Gk + (int64_t) (kk + r) * ne0 + n0 + ch * 2);
+        }
+    };
+
+    double acc[4][4][2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j][0] = acc[i][j][1] = 0.0;
+
+    constexpr int NKT = QK / UBK;
+    load(0, 0);
+    cp_commit();
+#pragma unroll 1
+    for (int kt = 0; kt < NKT; ++kt) {
+        if (kt + 1 < NKT) {
+            load((kt + 1) & 1, (kt + 1) * UBK);
+            cp_commit();
+            cp_wait<1>();
+        } else {
+            cp_wait<0>();
+        }
+        __syncthreads();
+        const double * As = sm.a[kt & 1] + (wm * 32 + (lane >> 2)) * APAD + (lane & 3);
+        const double * Bs = sm.b[kt & 1] + (lane & 3) * BPAD + wn * 32 + (lane >> 2);
+#pragma unroll
+        for (int kq = 0; kq < UBK / 4; ++kq) {
+            double a[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) a[i] = As[i * 8 * APAD + kq * 4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) b[j] = Bs[kq * 4 * BPAD + j * 8];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) dmma_8x8x4(acc[i][j], a[i], b[j]);
+        }
+        __syncthreads();
+    }
+    // epilogue, two adjacent columns a lane: W~ = f32(W~ - f32(acc)) (one 8-byte access), or the float64 product
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int64_t row = m0 + wm * 32 + i * 8 + (lane >> 2);
+        if (row >= rows) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int64_t col = n0 + wn * 32 + j * 8 + (lane & 3) * 2;
+            if constexpr (SUB) {
+                const int64_t blk = col / QK, cc = col % QK;
+                float2 * p = reinterpret_cast<float2 *>(static_cast<float *>(out) + ((blk * ngroups + g) * rows + row) * QK + cc);
+                float2 w = *p;
+                w.x = w.x - (float) acc[i][j][0];
+                w.y = w.y - (float) acc[i][j][1];
+                *p = w;
+            } else {
+                *reinterpret_cast<double2 *>(static_cast<double *>(out) + (g * rows + row) * QK + col) =
+                    make_double2(acc[i][j][0], acc[i][j][1]);
+            }
+        }
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_ldlq_scale(const double * E, const double * Rd, double * Es, int64_t ngroups, int64_t rows,
+                              int64_t nblk, int k, cudaStream_t st) {
+    if (ngroups <= 0 || rows <= 0 || k < 0 || k >= nblk || ngroups > 65535) return cudaErrorInvalidValue;
+    const size_t smem = sizeof(UpdSmem);
+    const cudaError_t e = cudaFuncSetAttribute(k_ldlq_gemm<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    if (e != cudaSuccess) return e;
+    const dim3 grid(QK / UBN, (unsigned) ((rows + UBM - 1) / UBM), (unsigned) ngroups);
+    if (grid.y > 65535) return cudaErrorInvalidValue;
+    k_ldlq_gemm<false><<<grid, UTHREADS, smem, st>>>(E, Rd + (int64_t) k * QK * QK, nblk * QK * QK, QK, 0, Es, ngroups,
+                                                     rows);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ldlq_update(const double * Es, const double * U, float * W, int64_t ngroups, int64_t rows, int64_t ne0,
+                               int k, cudaStream_t st) {
+    if (ngroups <= 0 || rows <= 0 || ne0 % QK || k < 0 || (int64_t) (k + 1) * QK >= ne0 || ngroups > 65535)
+        return cudaErrorInvalidValue;
+    const size_t smem = sizeof(UpdSmem);
+    const cudaError_t e = cudaFuncSetAttribute(k_ldlq_gemm<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    if (e != cudaSuccess) return e;
+    const int64_t c1 = (int64_t) (k + 1) * QK, rest = ne0 - c1;
+    const dim3 grid((unsigned) (rest / UBN), (unsigned) ((rows + UBM - 1) / UBM), (unsigned) ngroups);
+    if (grid.y > 65535) return cudaErrorInvalidValue;
+    k_ldlq_gemm<true><<<grid, UTHREADS, smem, st>>>(Es, U + (int64_t) k * QK * ne0, ne0 * ne0, ne0, c1, W, ngroups, rows);
+    return cudaGetLastError();
+}
+
+}  // namespace gq

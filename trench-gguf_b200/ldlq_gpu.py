@@ -1,20 +1,27 @@
-"""LDLQ / GPTQ error-feedback re-quantization on the B200 (config 5), over this library's device API.
+"""LDLQ / GPTQ error-feedback re-quantization on the B200 (benchmark config 5), on this library's own kernels.
 
-Mirrors trench-gguf's GPU loop in tools/ldlq.py - `GpuQuant` (ldlq.py:334-388), `prepare_hessian_torch`
-(ldlq.py:275-323), `quantize_matrix_torch` (ldlq.py:391-431), `proxy_loss` (ldlq.py:110-113) - with the same
-names, arguments and results, so ldlq.py's callers can switch modules. The maths is the reference's: for each
-256-column block (a super-block of the type) in order, quantize the block (this library's byte-identical
-kernels, gpuq_quantize_dev), dequantize it (gpuq_dequantize_dev, ggml's to_float bit for bit), form E = W_B - Q_B
-in float32 cast to float64, solve E U_BB^-1 (float64 triangular solve) and subtract (E U_BB^-1) U_B,rest cast to
-float32 from the remaining columns. The triangular solve and the float64 update are plain library calls (cuBLAS
-through torch); the quantizer, the dequantizer and the error are this library's kernels, fused where ggml's order
-allows (gpuq_dequantize_error_dev forms E from the bytes in one pass).
+What is computed is trench-gguf's GPU loop (tools/ldlq.py: prepare_hessian_torch :275-323, quantize_matrix_torch
+:391-431): the columns of the weights are taken 256 at a time (one super-block of the target type), optionally in
+act order; each block is quantized with ggml's quantizer, its rounding error E = W~_k - to_float(Q_k) (float32,
+widened to float64) is pushed into the columns after it,
+    W~_rest = f32( W~_rest - f32( (E U_kk^-1) U_k,rest ) ),
+with U the upper Cholesky factor of the inverse of the normalised, damped Hessian (H^-1 = U^T U), and the bytes of
+each block go back to the block's own position in the row.
 
-Several matrices that share U (gate and up of one expert) run as one batch: one quantize launch a block for all
-their rows (block b of the batch takes imatrix row b // rows).
+How it is organised here:
+  * the factor, float64, once a Hessian (`factor_hessian`): one Cholesky of the order-reversed Hessian (cuSOLVER
+    through torch) gives Hp = R R^T with R upper; U = R^-1 comes from a triangular inverse made of GEMMs, and
+    U_kk^-1 = R_kk is read off R. Float64 because a float32 factor changes the bytes: on the config-5 shape (28
+    blocks) a float32 factor - the reference's GPU default - leaves about 96 % of the super-blocks identical to the
+    reference's float64 loop, against 100 % for float64;
+  * the loop, in lockstep over every group (the matrices that share one factor: an expert's gate and up, or a single
+    matrix) of every expert given (`ldlq_groups`): per block k ONE quantize launch over all groups' rows, ONE fused
+    dequantize-error launch, then the two float64 tensor-core GEMMs of this library (gpuq_ldlq_scale_dev for
+    E U_kk^-1, gpuq_ldlq_update_dev for the update with its float32 cast and subtraction fused). The weights are held
+    column-block major, [block][group][row][256], so each step's input is one contiguous slab of every group.
+The reference's public names and arguments are kept (GpuQuant, prepare_hessian_torch, quantize_matrix_torch,
+proxy_loss) so its callers can switch modules; `ldlq_experts` is the batched driver the benchmark uses.
 """
-import ctypes
-
 import numpy as np
 
 import gpuq as G
@@ -22,221 +29,302 @@ import gpuq as G
 QK = 256
 
 
+def _torch():
+    import torch
+    return torch
+
+
+def _stream():
+    return _torch().cuda.current_stream().cuda_stream
+
+
 class GpuQuant:
-    """device-pointer quantizer / dequantizer of one type for torch tensors (the reference's GpuQuant contract)"""
+    """The device kernels of one target type on torch tensors: the interface trench-gguf's LDLQ loop binds
+    (tools/ldlq.py:334-388), over this library's C ABI."""
 
     def __init__(self, gq, typ, tsize=None, bs=QK):
-        self.gq = gq if hasattr(gq, "gpuq_quantize_dev") else gq.lib
-        G.declare(self.gq)
-        self.typ, self.bs = int(typ), bs
-        self.tsize = int(tsize or self.gq.gpuq_block_bytes(self.typ))
+        lib = gq if hasattr(gq, "gpuq_quantize_dev") else gq.lib
+        self.gq = G.declare(lib)
+        self.typ, self.bs = int(typ), int(bs)
+        self.tsize = int(tsize) if tsize else int(lib.gpuq_block_bytes(self.typ))
 
     @staticmethod
     def supported(gq, typ):
-        lib = gq if hasattr(gq, "gpuq_quantize_dev") else gq.lib
-        G.declare(lib)
-        return lib.gpuq_block_bytes(int(typ)) > 0 and int(typ) != 20 and lib.gpuq_can_dequantize_type(int(typ)) == 1
+        """types with both a device quantizer and a device to_float (IQ4_NL's 32-weight blocks excluded)"""
+        lib = G.declare(gq if hasattr(gq, "gpuq_quantize_dev") else gq.lib)
+        t = int(typ)
+        return t != 20 and lib.gpuq_block_bytes(t) > 0 and lib.gpuq_can_dequantize_type(t) == 1
 
-    @staticmethod
-    def _stream():
-        import torch
-        return torch.cuda.current_stream().cuda_stream
+    def _ok(self, got, want, call):
+        if got != want:
+            msg = self.gq.gpuq_last_error().decode()
+            raise RuntimeError("%s (type %d) returned %d, want %d: %s" % (call, self.typ, got, want, msg))
 
-    def _err(self, what):
-        return RuntimeError("%s failed (type %d): %s" % (what, self.typ, self.gq.gpuq_last_error().decode()))
+    def quant_slab(self, x, qw, raw, rows):
+        """x: f32 [n, bs] contiguous (device) -> raw [n, tsize]; block b weighted by importance row b // rows of qw"""
+        n = x.shape[0]
+        got = self.gq.gpuq_quantize_dev(self.typ, x.data_ptr(), raw.data_ptr(), n, qw.data_ptr(), n, rows, _stream())
+        self._ok(got, n * self.tsize, "gpuq_quantize_dev")
 
     def quant(self, blk, qw, raw):
-        """blk [B, rows, bs] f32 contiguous (device), qw [B, bs] f32 contiguous -> raw [B, rows, tsize] uint8"""
-        B, rows = blk.shape[0], blk.shape[1]
-        got = self.gq.gpuq_quantize_dev(self.typ, blk.data_ptr(), raw.data_ptr(), B * rows, qw.data_ptr(), B * rows,
-                                        rows, self._stream())
-        if got != B * rows * self.tsize:
-            raise self._err("gpuq_quantize_dev")
+        """blk [B, rows, bs] f32, qw [B, bs] f32 -> raw [B, rows, tsize] uint8, matrix b weighted by qw[b]"""
+        self.quant_slab(blk.reshape(-1, self.bs), qw, raw.reshape(-1, self.tsize), blk.shape[1])
 
     def dequant(self, raw):
-        """raw [B, rows, tsize] uint8 contiguous -> f32 [B, rows, bs]"""
-        import torch
+        """raw [B, rows, tsize] uint8 -> f32 [B, rows, bs] (ggml's to_float)"""
+        torch = _torch()
         B, rows = raw.shape[0], raw.shape[1]
         f = torch.empty((B, rows, self.bs), dtype=torch.float32, device=raw.device)
-        if self.gq.gpuq_dequantize_dev(self.typ, raw.data_ptr(), f.data_ptr(), B * rows, self._stream()) == 0:
-            raise self._err("gpuq_dequantize_dev")
+        got = self.gq.gpuq_dequantize_dev(self.typ, raw.data_ptr(), f.data_ptr(), B * rows, _stream())
+        self._ok(got, f.numel() * 4, "gpuq_dequantize_dev")
         return f
 
-    def error(self, raw, blk, out_dtype):
-        """E = (blk - to_float(raw)) in float32, cast to out_dtype (float64 or float32): one kernel"""
-        import torch
-        B, rows = raw.shape[0], raw.shape[1]
-        E = torch.empty((B, rows, self.bs), dtype=out_dtype, device=raw.device)
-        f64 = 1 if out_dtype == torch.float64 else 0
-        if self.gq.gpuq_dequantize_error_dev(self.typ, raw.data_ptr(), blk.data_ptr(), E.data_ptr(), f64, B * rows,
-                                             self._stream()) == 0:
-            raise self._err("gpuq_dequantize_error_dev")
-        return E
+    def error(self, raw, blk, out_dtype, out=None):
+        """(blk - to_float(raw)) in float32, stored as out_dtype (float64 / float32): one kernel"""
+        torch = _torch()
+        n = blk.numel() // self.bs
+        if out is None:
+            out = torch.empty(blk.shape, dtype=out_dtype, device=blk.device)
+        wide = 1 if out.dtype == torch.float64 else 0
+        got = self.gq.gpuq_dequantize_error_dev(self.typ, raw.data_ptr(), blk.data_ptr(), out.data_ptr(), wide, n,
+                                                _stream())
+        self._ok(got, out.numel() * out.element_size(), "gpuq_dequantize_error_dev")
+        return out
 
     def dequant_src(self, src, raw_host, n, device):
-        """source tensor bytes (ggml type src, numpy uint8) -> f32 [n] on the device, None if not decodable here"""
-        import torch
+        """a source tensor's bytes (ggml type src, host) -> f32 [n] on the device; None for a source the GPU cannot
+        read"""
+        torch = _torch()
         if self.gq.gpuq_can_dequantize(int(src)) != 1:
             return None
-        rb = torch.from_numpy(np.ascontiguousarray(raw_host).reshape(-1)).to(device)
+        dev_bytes = torch.from_numpy(np.ascontiguousarray(raw_host).reshape(-1).view(np.uint8)).to(device)
         f = torch.empty(n, dtype=torch.float32, device=device)
-        if self.gq.gpuq_dequantize_src_dev(int(src), rb.data_ptr(), f.data_ptr(), n, self._stream()) == 0:
-            raise self._err("gpuq_dequantize_src_dev")
+        got = self.gq.gpuq_dequantize_src_dev(int(src), dev_bytes.data_ptr(), f.data_ptr(), n, _stream())
+        self._ok(got, n * 4, "gpuq_dequantize_src_dev")
         return f
 
 
-def tri_inv_lower(L, leaf=1024):
-    """Inverse of a lower-triangular matrix by halves: [[A, 0], [B, C]]^-1 = [[A^-1, 0], [-C^-1 B A^-1, C^-1]], the
-    off-diagonal block two GEMMs, the leaves (<= leaf rows) triangular solves against the identity."""
-    import torch
+# ------------------------------------------------------------------------------------------------ the factor
+def _trmm_right_lower(B, T, leaf):
+    """B @ T for a lower-triangular T, by halving T: [B1 B2] [[T11, 0], [T21, T22]] = [B1 T11 + B2 T21, B2 T22]
+    (half the multiplications of a full GEMM)"""
+    m = T.shape[0]
+    if m <= leaf:
+        return B @ T
+    h = (m // 2 + QK - 1) // QK * QK
+    left = _trmm_right_lower(B[:, :h], T[:h, :h], leaf)
+    left.addmm_(B[:, h:], T[h:, :h])
+    return _torch().cat([left, _trmm_right_lower(B[:, h:], T[h:, h:], leaf)], 1)
+
+
+def _trmm_left_lower(T, B, leaf):
+    """T @ B for a lower-triangular T: [[T11, 0], [T21, T22]] [B1; B2] = [T11 B1; T21 B1 + T22 B2]"""
+    m = T.shape[0]
+    if m <= leaf:
+        return T @ B
+    h = (m // 2 + QK - 1) // QK * QK
+    top = _trmm_left_lower(T[:h, :h], B[:h], leaf)
+    bot = _trmm_left_lower(T[h:, h:], B[h:], leaf)
+    bot.addmm_(T[h:, :h], B[:h])
+    return _torch().cat([top, bot], 0)
+
+
+def _lower_inverse(L, out, leaf=512):
+    """out = L^-1 for a lower-triangular L, by halves: [[A, 0], [B, C]]^-1 = [[A^-1, 0], [-C^-1 B A^-1, C^-1]]; the
+    off-diagonal block two triangular-times-full products (n^3/3 multiply-adds in all, as a triangular inverse), the
+    leaves triangular solves against the identity"""
+    torch = _torch()
     m = L.shape[0]
     if m <= leaf:
-        return torch.linalg.solve_triangular(L, torch.eye(m, dtype=L.dtype, device=L.device), upper=False)
+        out.copy_(torch.linalg.solve_triangular(L, torch.eye(m, dtype=L.dtype, device=L.device), upper=False))
+        return
     h = (m // 2 + QK - 1) // QK * QK
-    Ai = tri_inv_lower(L[:h, :h], leaf)
-    Ci = tri_inv_lower(L[h:, h:], leaf)
-    out = torch.zeros_like(L)
-    out[:h, :h] = Ai
-    out[h:, h:] = Ci
-    out[h:, :h] = -(Ci @ L[h:, :h]) @ Ai
-    return out
+    _lower_inverse(L[:h, :h], out[:h, :h], leaf)
+    _lower_inverse(L[h:, h:], out[h:, h:], leaf)
+    out[:h, h:].zero_()
+    x = _trmm_left_lower(out[h:, h:], _trmm_right_lower(L[h:, :h], out[:h, :h], leaf), leaf)
+    out[h:, :h].copy_(x.neg_())
 
 
-def prepare_hessian_torch(H, n, damp=0.01, order="seq", bs=QK, device="cuda", out="numpy", check=True):
-    """ldlq.py:275-323: normalised, dead columns zeroed, optional act-order block permutation, damped; U the upper
-    Cholesky factor of the inverse (float32 on the GPU first; float64 and more ridge when it does not factor).
-    Returns (U float64, perm, diag_n, dead) as numpy arrays, or with out="torch" as tensors on `device`.
-    Nothing here waits for the device except the factorisation's success check; check=False leaves that out too
-    (only the first rung of the ladder runs) and returns the factorisation's status tensor last (0: factored)."""
-    import torch
-    dt = torch.float64 if device == "cpu" else torch.float32
-    ne0 = H.shape[0]
-    if isinstance(H, torch.Tensor):
-        Hn = H.to(device=device, dtype=torch.float64) / max(float(n), 1.0)
-    else:
-        Hn = torch.as_tensor(np.asarray(H), dtype=torch.float64).to(device) / max(float(n), 1.0)
+class Factor:
+    """One Hessian's feedback data on the device (float64): U [ne0, ne0] upper with Hp^-1 = U^T U, Rd [nblk, 256, 256]
+    the inverses of U's diagonal blocks, perm the column order, diag_n = diag(H)/n in that order, dead columns."""
+    __slots__ = ("U", "Rd", "perm", "diag_n", "dead")
+
+    def __init__(self, U, Rd, perm, diag_n, dead):
+        self.U, self.Rd, self.perm, self.diag_n, self.dead = U, Rd, perm, diag_n, dead
+
+
+def factor_hessian(H, n, damp=0.01, order="seq", bs=QK, device="cuda", U_out=None):
+    """The reference's preparation (tools/ldlq.py:275-323, its CPU twin :34-68): H / n; a column no input reached
+    (diag <= 0) gets its row and column zeroed and a unit diagonal; the column order (blocks in sequence, or 'act':
+    by falling block energy); damping by damp * mean(diag), raised to 10x and 100x more when the matrix does not
+    factor. Everything in float64. U_out: an optional preallocated [ne0, ne0] float64 tensor for U."""
+    torch = _torch()
+    Hn = torch.as_tensor(H).to(device=device, dtype=torch.float64)
+    Hn = Hn / max(float(n), 1.0)
+    ne0 = Hn.shape[0]
+    nblk = ne0 // bs
     dead = torch.diagonal(Hn) <= 0
-    keep = ~dead
-    Hn = torch.where(keep[:, None] & keep[None, :], Hn, 0.0)   # dead rows and columns zeroed, their diagonal 1
+    live = ~dead
+    Hn = torch.where(live[:, None] & live[None, :], Hn, torch.zeros((), dtype=Hn.dtype, device=Hn.device))
     Hn.diagonal().add_(dead.to(Hn.dtype))
     d = torch.diagonal(Hn).clone()
-    nblk = ne0 // bs
     if order == "act":
-        blk_order = torch.argsort(-d.reshape(nblk, bs).sum(1), stable=True)
+        blocks = torch.argsort(-d.view(nblk, bs).sum(1), stable=True)
+    elif order == "seq":
+        blocks = torch.arange(nblk, device=Hn.device)
     else:
-        blk_order = torch.arange(nblk, device=device)
-    perm = (blk_order[:, None] * bs + torch.arange(bs, device=device)[None]).reshape(-1)
-    Hp64 = Hn[perm][:, perm] if order == "act" else Hn   # (the sequential order's permutation is the identity)
-    mean_d = torch.diagonal(Hp64).mean()
-
-    def factor(dtype, extra):
-        # U is the upper factor of Hp^-1 = U^T U. With J the order reversal, J Hp J = Lr Lr^T (lower Cholesky), so
-        # Hp = R R^T with R = J Lr J upper and Hp^-1 = R^-T R^-1: U = R^-1 = J Lr^-1 J (upper, positive diagonal,
-        # hence the same factor as ldlq.py's cholesky(cholesky_inverse(cholesky(Hp)), upper) up to rounding), for
-        # one factorisation and one triangular inverse instead of three factor/inverse passes.
-        Hp = Hp64.to(dtype).clone()
-        Hp.diagonal().add_((damp + extra) * mean_d)
-        Lr, info = torch.linalg.cholesky_ex(Hp.flip(0, 1))
-        return tri_inv_lower(Lr).flip(0, 1), info
-
-    if not check:
-        U, info = factor(dt, 0.0)
-        res = (U.double(), perm, d[perm], dead)
-        return (res if out == "torch" else tuple(t.cpu().numpy() for t in res)) + (info,)
-    U = None
-    for dtype, extra in ((dt, 0.0), (torch.float64, 0.0), (torch.float64, 10 * damp), (torch.float64, 100 * damp)):
-        Uc, info = factor(dtype, extra)
-        if int(info) == 0 and bool(torch.isfinite(torch.diagonal(Uc)).all()):
-            U = Uc
+        raise ValueError("order must be 'seq' or 'act', not %r" % (order,))
+    perm = (blocks[:, None] * bs + torch.arange(bs, device=Hn.device)[None]).reshape(-1)
+    if order == "act":
+        Hn = Hn.index_select(0, perm).index_select(1, perm)
+    mean_diag = torch.diagonal(Hn).mean()
+    rev = Hn.flip(0, 1)                      # J Hp J: its lower factor Lr gives Hp = R R^T with R = J Lr J upper
+    del Hn
+    Lr = None
+    for extra in (0.0, 10 * damp, 100 * damp):
+        M = rev.clone()
+        M.diagonal().add_((damp + extra) * mean_diag)
+        Lr, info = torch.linalg.cholesky_ex(M)
+        del M
+        if int(info) == 0:
             break
-    if U is None:
-        raise RuntimeError("Hessian could not be factored even with %.0f%% ridge" % (100 * (damp + 100 * damp)))
-    if out == "torch":
-        return U.double(), perm, d[perm], dead
-    return U.double().cpu().numpy(), perm.cpu().numpy(), d[perm].cpu().numpy(), dead.cpu().numpy()
+        Lr = None
+    del rev
+    if Lr is None:
+        raise RuntimeError("the Hessian does not factor even with %g x mean(diag) damping" % (damp + 100 * damp))
+    # U = R^-1 = J Lr^-1 J; U's diagonal blocks are the inverses of R's, so U_kk^-1 = R_kk = J (Lr block) J
+    Li = torch.empty_like(Lr)
+    _lower_inverse(Lr, Li)
+    U = U_out if U_out is not None else torch.empty_like(Li)
+    U.copy_(Li.flip(0, 1))
+    del Li
+    lr_blocks = torch.stack([Lr[i * bs:(i + 1) * bs, i * bs:(i + 1) * bs] for i in range(nblk)])
+    Rd = lr_blocks.flip(0).flip(1, 2).contiguous()     # R_kk for k = 0..nblk-1
+    return Factor(U, Rd, perm, d[perm], dead)
+
+
+def factor_from_U(U, perm=None, diag_n=None, bs=QK):
+    """a Factor for a U given by the caller (the reference's quantize_matrix_torch arguments)"""
+    torch = _torch()
+    U = U.to(torch.float64).contiguous()
+    ne0 = U.shape[0]
+    nblk = ne0 // bs
+    Ubb = torch.stack([U[i * bs:(i + 1) * bs, i * bs:(i + 1) * bs] for i in range(nblk)])
+    eye = torch.eye(bs, dtype=torch.float64, device=U.device).expand(nblk, bs, bs)
+    Rd = torch.linalg.solve_triangular(Ubb, eye, upper=True).contiguous()
+    if perm is None:
+        perm = torch.arange(ne0, device=U.device)
+    return Factor(U, Rd, perm, diag_n, None)
+
+
+def prepare_hessian_torch(H, n, damp=0.01, order="seq", bs=QK, device="cuda", out="numpy"):
+    """tools/ldlq.py:275-323's contract: (U float64, perm, diag_n, dead) as numpy arrays, or with out="torch" as
+    tensors on `device` (the factor is always float64 here: see the module docstring)"""
+    f = factor_hessian(H, n, damp=damp, order=order, bs=bs, device=device)
+    res = (f.U, f.perm, f.diag_n, f.dead)
+    return res if out == "torch" else tuple(t.cpu().numpy() for t in res)
+
+
+# ------------------------------------------------------------------------------------------------ the loop
+def _importance(f, imatrix, weights, B, bs):
+    """[B, ne0] float32 importance rows in the factor's column order: the imatrix ('imatrix'), diag(H)/n ('diag'),
+    or diag((U_kk^T U_kk)^-1) of each block ('schur', tools/ldlq.py:414-417)"""
+    torch = _torch()
+    if weights == "imatrix":
+        return imatrix.to(torch.float32).index_select(1, f.perm)
+    if weights == "diag":
+        return f.diag_n.to(torch.float32)[None].expand(B, -1)
+    if weights == "schur":
+        nblk = f.Rd.shape[0]
+        Ubb = torch.stack([f.U[i * bs:(i + 1) * bs, i * bs:(i + 1) * bs] for i in range(nblk)])
+        s = torch.diagonal(torch.linalg.inv(Ubb.transpose(1, 2) @ Ubb), dim1=1, dim2=2).reshape(-1)
+        return s.to(torch.float32)[None].expand(B, -1)
+    raise ValueError("weights must be 'imatrix', 'diag' or 'schur', not %r" % (weights,))
+
+
+def ldlq_groups(Ws, factors, gqt, imatrices, weights="imatrix", feedback=True, bs=QK, U_stack=None):
+    """The loop over every group at once. Ws[g]: f32 [B, ne1, ne0] on the device (all groups one shape); factors[g]:
+    Factor (None with feedback=False: identity order); imatrices[g]: [B, ne0] (for weights='imatrix'). U_stack: the
+    groups' U already stacked [P, ne0, ne0] (else stacked here). Returns [g] uint8 [B, ne1, nblk*tsize], ggml's row
+    layout, ready on the current stream."""
+    torch = _torch()
+    lib = gqt.gq
+    P = len(Ws)
+    B, ne1, ne0 = Ws[0].shape
+    nblk, M, tsize = ne0 // bs, B * ne1, gqt.tsize
+    dev = Ws[0].device
+    perms = [f.perm if f is not None else torch.arange(ne0, device=dev) for f in factors]
+    # column-block-major weights and importance rows: step k reads Wb[k] ([P*M, 256]) and qw[k] ([P*B, 256])
+    Wb = torch.empty((nblk, P, M, bs), dtype=torch.float32, device=dev)
+    qw = torch.empty((nblk, P * B, bs), dtype=torch.float32, device=dev)
+    for g in range(P):
+        Wb[:, g] = Ws[g].index_select(2, perms[g]).reshape(M, nblk, bs).transpose(0, 1)
+        if factors[g] is None:
+            imp = imatrices[g].to(torch.float32)
+        else:
+            imp = _importance(factors[g], imatrices[g] if imatrices is not None else None, weights, B, bs)
+        qw[:, g * B:(g + 1) * B] = imp.reshape(B, nblk, bs).transpose(0, 1)
+    raw = torch.empty((nblk, P * M, tsize), dtype=torch.uint8, device=dev)
+    if feedback:
+        U = U_stack if U_stack is not None else torch.stack([f.U for f in factors])
+        Rd = torch.stack([f.Rd for f in factors])
+        E = torch.empty((P, M, bs), dtype=torch.float64, device=dev)
+        Es = torch.empty_like(E)
+    st = _stream()
+    for k in range(nblk):
+        gqt.quant_slab(Wb[k].view(P * M, bs), qw[k], raw[k], ne1)
+        if not feedback or k + 1 == nblk:
+            continue
+        gqt.error(raw[k], Wb[k], torch.float64, out=E)
+        if lib.gpuq_ldlq_scale_dev(E.data_ptr(), Rd.data_ptr(), Es.data_ptr(), P, M, nblk, k, st) != E.numel() * 8:
+            raise RuntimeError("gpuq_ldlq_scale_dev: " + lib.gpuq_last_error().decode())
+        want = P * M * (ne0 - (k + 1) * bs) * 4
+        if lib.gpuq_ldlq_update_dev(Es.data_ptr(), U.data_ptr(), Wb.data_ptr(), P, M, ne0, k, st) != want:
+            raise RuntimeError("gpuq_ldlq_update_dev: " + lib.gpuq_last_error().decode())
+    # bytes back to ggml's row layout, each block at its own column position
+    raw = raw.view(nblk, P, B, ne1, tsize)
+    outs = []
+    for g in range(P):
+        pos = perms[g].view(nblk, bs)[:, 0] // bs
+        rows = torch.empty((nblk, B, ne1, tsize), dtype=torch.uint8, device=dev)
+        rows.index_copy_(0, pos, raw[:, g])
+        outs.append(rows.permute(1, 2, 0, 3).reshape(B, ne1, nblk * tsize))
+    return outs
 
 
 def quantize_matrix_torch(W, gqt, U=None, perm=None, diag_n=None, imatrix=None, weights="imatrix", feedback=True,
                           bs=QK, f64=True):
-    """ldlq.py:391-431. W: f32 [B, ne1, ne0] on the device (B matrices sharing U and perm); gqt: GpuQuant; U:
-    [ne0, ne0] on the device; perm: [ne0] long; diag_n: [ne0] (permuted order); imatrix: [B, ne0] f32.
-    Returns uint8 [B, ne1, nblk*tsize] on the device in GGUF row layout."""
-    import torch
-    B, ne1, ne0 = W.shape
-    nblk = ne0 // bs
-    tsize = gqt.tsize
-    dev = W.device
-    if perm is None:
-        perm = torch.arange(ne0, device=dev)
-    Wp = W.index_select(2, perm).contiguous()
-    Ud = Uinv = None
-    if feedback:
-        Ud = U.to(torch.float64 if f64 else torch.float32)
-        # the diagonal blocks' inverses, all in one batched solve (E U_BB^-1 is then one small GEMM a block)
-        Ubb = torch.stack([Ud[k * bs:(k + 1) * bs, k * bs:(k + 1) * bs] for k in range(nblk - 1)]) if nblk > 1 else None
-        if Ubb is not None:
-            Uinv = torch.linalg.solve_triangular(Ubb, torch.eye(bs, dtype=Ud.dtype, device=dev).expand_as(Ubb), upper=True)
-    if weights == "imatrix":
-        imp = imatrix.index_select(1, perm).contiguous()
-    elif weights == "diag":
-        imp = diag_n.to(torch.float32)[None].expand(B, ne0).contiguous()
-    elif weights != "schur":
-        raise ValueError(weights)
-    out = torch.empty((nblk, B, ne1, tsize), dtype=torch.uint8, device=dev)   # in the permuted block order
-    for k in range(nblk):
-        c0, c1 = k * bs, (k + 1) * bs
-        blk = Wp[:, :, c0:c1].contiguous()
-        if weights == "schur":
-            Ubb = U[c0:c1, c0:c1].double()
-            qw = torch.diagonal(torch.linalg.inv(Ubb.T @ Ubb)).to(torch.float32)[None].expand(B, bs).contiguous()
-        else:
-            qw = imp[:, c0:c1].contiguous()
-        raw = out[k]
-        gqt.quant(blk, qw, raw)
-        if feedback and k + 1 < nblk:
-            E = gqt.error(raw, blk, Ud.dtype)
-            Es = E @ Uinv[k]                                                                    # E U_BB^-1
-            Wp[:, :, c1:] -= (Es @ Ud[c0:c1, c1:]).to(torch.float32)
-    res = torch.empty_like(out).index_copy_(0, perm.view(nblk, bs)[:, 0] // bs, out)   # back to the source order
-    return res.permute(1, 2, 0, 3).reshape(B, ne1, nblk * tsize)
+    """tools/ldlq.py:391-431's contract: W f32 [B, ne1, ne0] on the device (B matrices sharing U, perm); U [ne0, ne0];
+    perm [ne0]; diag_n [ne0] (permuted order); imatrix [B, ne0] -> uint8 [B, ne1, nblk*tsize] on the device. The
+    update is always float64 here (f64=False, the reference's reduced-precision option, is refused)."""
+    if not f64:
+        raise ValueError("the float32 feedback update is not provided: the float64 one is exact to the reference's "
+                         "default and runs on the tensor cores")
+    if not feedback:
+        f = None
+        if perm is not None or weights != "imatrix":
+            f = Factor(None, None, perm if perm is not None else _torch().arange(W.shape[2], device=W.device),
+                       diag_n, None)
+        return ldlq_groups([W], [f], gqt, [imatrix], weights=weights, feedback=False, bs=bs)[0]
+    return ldlq_groups([W], [factor_from_U(U, perm, diag_n, bs)], gqt, [imatrix], weights=weights, bs=bs)[0]
 
 
-def ldlq_experts_torch(Ws, Hs, ns, gqt, imatrices, streams, damp=0.01, order="seq", weights="imatrix", f64=True):
-    """Several experts (each with its own Hessian) one after another, expert e on streams[e % len(streams)]: the
-    factorisation of the next expert runs on the GPU while this one's feedback loop does (the loop's 28 block
-    quantizations are small launches that leave most of the GPU idle). The work and the bytes of every expert are
-    exactly those of prepare_hessian_torch + quantize_matrix_torch on one stream. Ws[e]: f32 [B, ne1, ne0] on the
-    device (updated in place), Hs[e]: [ne0, ne0], imatrices[e]: [B, ne0]. Returns the experts' bytes, ready on the
-    current stream."""
-    import torch
-    cur = torch.cuda.current_stream()
-    outs = []
-    infos, W0 = [], []
-    for e in range(len(Ws)):
-        s = streams[e % len(streams)]
-        s.wait_stream(cur)
-        with torch.cuda.stream(s):
-            W0.append(Ws[e].clone())
-            U, perm, diag_n, _, info = prepare_hessian_torch(Hs[e], ns[e], damp=damp, order=order,
-                                                             device=Ws[e].device, out="torch", check=False)
-            infos.append(info)
-            outs.append(quantize_matrix_torch(Ws[e], gqt, U=U, perm=perm, diag_n=diag_n, imatrix=imatrices[e],
-                                              weights=weights, f64=f64))
-    for s in streams:
-        cur.wait_stream(s)
-    for o in outs:
-        o.record_stream(cur)
-    failed = torch.nonzero(torch.stack([i.reshape(()) for i in infos]) != 0).flatten().tolist()
-    for e in failed:   # (the float32 factorisation failed: the whole ladder, as one expert alone)
-        Ws[e].copy_(W0[e])
-        U, perm, diag_n, _ = prepare_hessian_torch(Hs[e], ns[e], damp=damp, order=order, device=Ws[e].device,
-                                                   out="torch")
-        outs[e] = quantize_matrix_torch(Ws[e], gqt, U=U, perm=perm, diag_n=diag_n, imatrix=imatrices[e],
-                                        weights=weights, f64=f64)
-    return outs
+def ldlq_experts(Ws, Hs, ns, gqt, imatrices, damp=0.01, order="seq", weights="imatrix", bs=QK):
+    """Every expert of a tensor on this GPU: each Hessian factored (float64) into one stacked U, then the loop of all
+    experts in lockstep (one launch of each kernel a block for all of them). Ws[e]: f32 [B, ne1, ne0] (device),
+    Hs[e]: [ne0, ne0], ns[e]: rows H was summed over, imatrices[e]: [B, ne0]. Returns the experts' bytes."""
+    torch = _torch()
+    ne0 = Ws[0].shape[2]
+    U = torch.empty((len(Ws), ne0, ne0), dtype=torch.float64, device=Ws[0].device)
+    factors = [factor_hessian(Hs[e], ns[e], damp=damp, order=order, bs=bs, device=Ws[e].device, U_out=U[e])
+               for e in range(len(Ws))]
+    return ldlq_groups(Ws, factors, gqt, imatrices, weights=weights, bs=bs, U_stack=U)
 
 
 def proxy_loss(W, deq, H, n):
-    """tr((W - Q) H (W - Q)^T) / n (ldlq.py:110-113), numpy inputs"""
-    D = (np.asarray(W) - np.asarray(deq)).astype(np.float64)
-    return float(np.einsum("ij,jk,ik->", D, np.asarray(H, dtype=np.float64), D) / max(float(n), 1.0))
+    """tools/ldlq.py:110-113's measure tr((W - Q) H (W - Q)^T) / n: the difference taken in float32, the rest in
+    float64 (numpy inputs)"""
+    D = (np.asarray(W, dtype=np.float32) - np.asarray(deq, dtype=np.float32)).astype(np.float64)
+    return float(((D @ np.asarray(H, dtype=np.float64)) * D).sum() / max(float(n), 1.0))
