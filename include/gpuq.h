@@ -42,7 +42,11 @@ size_t gpuq_quantize(int type, const float * src, void * dst, int64_t nrow, int6
 size_t gpuq_quantize_batch(int type, const float * src, void * dst, int64_t nmat, int64_t nrow, int64_t n_per_row,
                            const float * imatrix);
 
-/* 1 when the source type can be decoded on the GPU (F32, F16, BF16, Q8_0, MXFP4). Replaces gpuq.hip:2235. */
+/* 1 when the source type can be decoded on the GPU. Replaces gpuq.hip:2235, which reads F32, F16, BF16, Q8_0 and
+ * MXFP4; this library also reads NVFP4 (40), the MXFP8 row layout of unsloth's type 43 (33-byte blocks: an E8M0
+ * scale byte and 32 E4M3 values, tools/requant_table.py:8-9), and the k-quant and i-quant types that
+ * gpuq_can_dequantize_type reports (the reference's callers then leave their "(gpu quant, cpu dequant)" path).
+ * The first five are decoded inside the quantize kernels; the others by a decode pass of their own. */
 int gpuq_can_dequantize(int src);
 
 /* Source tensor bytes of ggml type `src` (host) -> quantized `type` (host), decoded on the GPU.
@@ -50,10 +54,17 @@ int gpuq_can_dequantize(int src);
 size_t gpuq_requantize(int src, const void * raw, int type, void * dst, int64_t nrow, int64_t n_per_row,
                        const float * imatrix);
 
-/* The batched form: nmat matrices, matrix m weighted by imatrix row m; nmat*nrow*n_per_row % 32 == 0.
- * Replaces gpuq.hip:2237-2250. */
+/* The batched form: nmat matrices, matrix m weighted by imatrix row m; n_per_row a multiple of the source's block
+ * (32 values; NVFP4 64; k-/i-quant sources 256). Replaces gpuq.hip:2237-2250. */
 size_t gpuq_requantize_batch(int src, const void * raw, int type, void * dst, int64_t nmat, int64_t nrow,
                              int64_t n_per_row, const float * imatrix);
+
+/* gpuq_requantize_batch with a second scale a matrix: matrix m's decoded values are multiplied by mat_scale[m] in
+ * float32 before quantizing (no counterpart in the reference's library: its callers fold NVFP4 experts' per-expert
+ * scale into CPU-decoded floats, `f32 *= esc[e]`, tools/requant_experts.py:240-248, 704-706; this is the same product
+ * after the GPU's decode). mat_scale: nmat floats (host). */
+size_t gpuq_requantize_scaled_batch(int src, const void * raw, int type, void * dst, int64_t nmat, int64_t nrow,
+                                    int64_t n_per_row, const float * imatrix, const float * mat_scale);
 
 /* Device API: nblocks contiguous 256-weight super-blocks of d_x (float32, device) -> d_dst (device); block b takes
  * the 256 importance weights d_qw + ((b % qw_mod) / qw_div) * 256. The 256-block i-quants, as the reference, and
@@ -72,7 +83,8 @@ int gpuq_can_dequantize_type(int type);
  * Replaces gpuq.hip:2301-2320. */
 size_t gpuq_dequantize_dev(int type, const void * d_q, float * d_out, int64_t nblocks, void * stream);
 
-/* n values of source type `src` (device bytes) -> n floats (device); n % 32 == 0. Replaces gpuq.hip:2322-2328. */
+/* n values of source type `src` (device bytes) -> n floats (device); n a multiple of 32 and of the source's block
+ * (every source gpuq_can_dequantize reports). Replaces gpuq.hip:2322-2328. */
 size_t gpuq_dequantize_src_dev(int src, const void * d_raw, float * d_out, int64_t n, void * stream);
 
 /* ---- extensions (no counterpart in the reference; callers find them with hasattr) ---- */
@@ -94,7 +106,8 @@ int gpuq_device_count(void);
 
 /* The device-pointer form of gpuq_requantize_batch: source bytes of type `src` already on the current device ->
  * d_dst, matrix m weighted by d_imatrix row m (nmat x n_per_row floats, device; NULL for the no-imatrix types).
- * Decodes inside the quantize kernel; on `stream`, no synchronisation, no library scratch. d_dst must hold
+ * Decodes inside the quantize kernel, so the sources are the five it reads (F32, F16, BF16, Q8_0, MXFP4; others:
+ * gpuq_dequantize_src_dev first); on `stream`, no synchronisation, no library scratch. d_dst must hold
  * nmat * nrow * n_per_row / block_len * gpuq_block_bytes(type) bytes, block_len being 32 for Q8_0 and IQ4_NL and
  * 256 for every other type: the kernel writes them all and cannot see the allocation. */
 size_t gpuq_requantize_dev(int src, const void * d_raw, int type, void * d_dst, int64_t nmat, int64_t nrow,

@@ -1484,10 +1484,57 @@ size_t orc_dequantize(int type, const void * q, float * out, int64_t nblocks) {
 }
 
 /* source bytes -> floats (kdq, gpuq.hip:2123-2141) */
+/* NVFP4's scale byte (unsigned E4M3, times 0.5 - gguf-py's ue4m3_to_fp32) and an E4M3 value (the FN variant, NaN
+ * read as 0 - tools/requant_table.py's e4m3_lut), from their definitions, in double then float (exact) */
+static float o_ue4m3_half(uint8_t x) {
+    if (x == 0 || x == 0x7F) return 0.0f;
+    const int e = (x >> 3) & 0xF, m = x & 7;
+    return (float) (0.5 * (e == 0 ? m * ldexp(1.0, -9) : (1.0 + m / 8.0) * ldexp(1.0, e - 7)));
+}
+static float o_e4m3(uint8_t x) {
+    const int e = (x >> 3) & 0xF, m = x & 7;
+    const double s = x & 0x80 ? -1.0 : 1.0;
+    if (e == 15 && m == 7) return 0.0f;
+    return (float) (e == 0 ? s * (m / 8.0) * ldexp(1.0, -6) : s * (1.0 + m / 8.0) * ldexp(1.0, e - 7));
+}
+
+static int o_is_block_src(int s) {
+    return s == O_IQ2_XXS || s == O_IQ2_XS || s == O_IQ2_S || s == O_IQ3_XXS || s == O_IQ3_S || s == O_IQ1_S ||
+           s == O_IQ1_M || s == O_IQ4_XS || o_is_kquant256(s);
+}
+
+size_t orc_dequantize(int type, const void * q, float * out, int64_t nblocks);
+
 size_t orc_decode(int src, const void * raw, float * out, int64_t n) {
     static const int8_t kv[16] = {0, 1, 2, 3, 4, 6, 8, 12, 0, -1, -2, -3, -4, -6, -8, -12};
     if (n <= 0 || n % 32) return 0;
     const uint8_t * r = (const uint8_t *) raw;
+    if (o_is_block_src(src)) {   /* the k-quants and i-quants as sources: ggml's to_float */
+        if (n % QK) return 0;
+        return orc_dequantize(src, raw, out, n / QK);
+    }
+    if (src == 40) {             /* NVFP4: 64 values, 4 scales then 4 x 8 bytes (group j: low nibbles, then high) */
+        if (n % 64) return 0;
+        for (int64_t b = 0; b < n / 64; ++b) {
+            const uint8_t * q = r + 36 * b;
+            for (int j = 0; j < 4; ++j) {
+                const float d = o_ue4m3_half(q[j]);
+                for (int i = 0; i < 8; ++i) {
+                    out[64 * b + 16 * j + i] = d * kv[q[4 + 8 * j + i] & 15];
+                    out[64 * b + 16 * j + 8 + i] = d * kv[q[4 + 8 * j + i] >> 4];
+                }
+            }
+        }
+        return (size_t) n * 4;
+    }
+    if (src == 43) {             /* unsloth's MXFP8 rows: E8M0 scale 2^(e-127) (255: 0), 32 E4M3 values */
+        for (int64_t b = 0; b < n / 32; ++b) {
+            const uint8_t * q = r + 33 * b;
+            const float sc = q[0] == 255 ? 0.0f : (float) ldexp(1.0, q[0] - 127);
+            for (int j = 0; j < 32; ++j) out[32 * b + j] = o_e4m3(q[1 + j]) * sc;
+        }
+        return (size_t) n * 4;
+    }
     for (int64_t b = 0; b < n / 32; ++b) {
         float * y = out + 32 * b;
         switch (src) {

@@ -81,6 +81,62 @@ def test_requantize_sources(gpuq, oracle, golden, src, name):
     assert np.array_equal(got, want)
 
 
+def staged_source(oracle, src, nmat, nrow, npr, seed):
+    """source bytes of a staged type: NVFP4 / MXFP8 random blocks, or k-/i-quant bytes written by the oracle"""
+    from test_oracle import mxfp8_bytes, nvfp4_bytes
+    n = nmat * nrow * npr
+    if src == 40:
+        return nvfp4_bytes(n // 64, seed)
+    if src == 43:   # (scales 2^-27 .. 2^-1: the full E8M0 range overflows float32 - 448 x 2^127 - into inf)
+        raw = mxfp8_bytes(n // 32, seed)
+        raw[:, 0] = 100 + raw[:, 0] % 27
+        return raw
+    rng = np.random.default_rng(seed)
+    x = (rng.standard_t(5, (nmat, nrow, npr)) * 0.02).astype(np.float32)
+    im = rng.gamma(1.0, 1.0, (nmat, npr)).astype(np.float32)
+    return oracle.quantize(src, x, im)
+
+
+@pytest.mark.parametrize("src", ["NVFP4", "MXFP8", "Q4_K", "Q6_K", "Q2_K", "IQ2_XXS", "IQ1_M", "IQ4_XS"])
+@pytest.mark.parametrize("name", ["IQ2_XXS", "Q4_K", "Q8_0"])
+def test_requantize_staged_sources(gpuq, oracle, monkeypatch, src, name):
+    """sources decoded by their own pass (NVFP4, unsloth's MXFP8 rows, k-quants and i-quants: the reference leaves
+    those to ggml on the CPU) == their to_float then ggml's quantizer; with per-matrix scales as well (NVFP4's
+    per-expert scale, `f32 *= esc[e]`)"""
+    nmat, nrow, npr = 3, 8, 1024
+    s = G.SOURCES[src] if src in G.SOURCES else TYPES[src]
+    raw = staged_source(oracle, s, nmat, nrow, npr, 31 + s)
+    x = oracle.decode(s, raw, nmat * nrow * npr).reshape(nmat, nrow, npr)
+    t = TYPES[name]
+    im = np.random.default_rng(32).gamma(1.0, 1.0, (nmat, npr)).astype(np.float32)
+    imx = None if name == "Q8_0" else im
+    assert np.array_equal(gpuq.requantize(s, raw, t, (nmat, nrow, npr), imx), oracle.quantize(t, x, imx))
+    scale = np.array([0.37, 1.0, 2.5e-3], np.float32)
+    want = oracle.quantize(t, (x * scale[:, None, None]).astype(np.float32), imx)
+    monkeypatch.setenv("GPUQ_CHUNK_MW", "1")
+    assert np.array_equal(gpuq.requantize(s, raw, t, (nmat, nrow, npr), imx, mat_scale=scale), want)
+
+
+@pytest.mark.parametrize("src", ["NVFP4", "MXFP8", "Q5_K", "IQ3_S", "IQ2_S"])
+def test_device_api_decode_staged(gpuq, oracle, src):
+    """gpuq_dequantize_src_dev on the staged sources == the oracle's decode, bit for bit"""
+    import torch
+    s = G.SOURCES[src] if src in G.SOURCES else TYPES[src]
+    raw = staged_source(oracle, s, 1, 4, 1024, 40 + s)
+    n = 4 * 1024
+    want = oracle.decode(s, raw, n)
+    d_raw = torch.from_numpy(np.ascontiguousarray(raw).reshape(-1).view(np.uint8).copy()).cuda()
+    f = torch.empty(n, dtype=torch.float32, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    assert gpuq.lib.gpuq_dequantize_src_dev(s, dev_ptr(d_raw), dev_ptr(f), n, st) == n * 4, gpuq.error()
+    torch.cuda.synchronize()
+    assert np.array_equal(f.cpu().numpy().view(np.uint32), want.view(np.uint32))
+    # the device-pointer requantize takes only the inline sources, and says what to do instead
+    out = torch.empty(16 * 66, dtype=torch.uint8, device="cuda")
+    assert gpuq.lib.gpuq_requantize_dev(s, dev_ptr(d_raw), 16, dev_ptr(out), 1, 4, 1024, None, st) == 0
+    assert "gpuq_dequantize_src_dev" in gpuq.error()
+
+
 def test_chunked_pipeline_matches_one_chunk(gpuq, oracle, monkeypatch):
     """many pipeline chunks (whole matrices and row ranges of one matrix) == the oracle"""
     raw, im = workloads.config3(experts=3, rows=16, cols=7168, seed=5)
@@ -228,7 +284,7 @@ def test_argument_errors(gpuq):
     assert b"multiple" in L.gpuq_last_error()
     assert L.gpuq_quantize(16, x.ctypes.data, y.ctypes.data, 2, 256, None) == 0               # IQ needs imatrix
     assert L.gpuq_quantize(99, x.ctypes.data, y.ctypes.data, 2, 256, None) == 0
-    assert L.gpuq_requantize(16, x.ctypes.data, 8, y.ctypes.data, 2, 256, None) == 0          # F16? no: src 16
+    assert L.gpuq_requantize(20, x.ctypes.data, 8, y.ctypes.data, 2, 256, None) == 0          # IQ4_NL: no source
     assert L.gpuq_can_quantize(16, 0) == 0 and L.gpuq_can_quantize(16, 1) == 1 and L.gpuq_can_quantize(12, 0) == 1
 
 

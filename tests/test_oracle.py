@@ -102,6 +102,57 @@ def test_oracle_decode_matches_gguf(oracle):
         assert np.array_equal(got, np.asarray(ref, dtype=np.float32).reshape(-1)), src
 
 
+def nvfp4_bytes(nblocks, seed):
+    """random NVFP4 blocks: 4 scale bytes (UE4M3 < 0x7F, 0x7F included: read as 0) and 32 bytes of nibbles"""
+    rng = np.random.default_rng(seed)
+    b = rng.integers(0, 256, (nblocks, 36), dtype=np.uint8)
+    b[:, :4] = rng.integers(0, 0x80, (nblocks, 4), dtype=np.uint8)
+    return b
+
+
+def mxfp8_bytes(nblocks, seed):
+    """random 33-byte MXFP8 row blocks: an E8M0 scale byte (all 256 values, 255 read as 0) and 32 E4M3 bytes"""
+    rng = np.random.default_rng(seed)
+    return rng.integers(0, 256, (nblocks, 33), dtype=np.uint8)
+
+
+def test_oracle_decode_nvfp4_matches_gguf(oracle):
+    from gguf import quants as gq, GGMLQuantizationType as G
+    raw = nvfp4_bytes(256, 21)
+    got = oracle.decode(40, raw, raw.shape[0] * 64)
+    ref = gq.dequantize(raw, G.NVFP4).reshape(-1).astype(np.float32)
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+def _reference_module(rel):
+    """a module of the trench-gguf checkout ($REF, $TRENCH_GGUF_REF, or the checkout named `reference` beside this
+    repository), or None where it is absent"""
+    import importlib.util
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    ref = os.environ.get("REF") or os.environ.get("TRENCH_GGUF_REF") or os.path.join(os.path.dirname(root), "reference")
+    path = os.path.join(ref, rel)
+    if not os.path.exists(path):
+        return None
+    spec = importlib.util.spec_from_file_location("ref_" + os.path.basename(path)[:-3], path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def test_oracle_decode_mxfp8_matches_reference(oracle):
+    """unsloth's type-43 rows as the reference reads them (tools/requant_table.py:109-119: its E4M3 table times
+    2^(e-127), 0 for e = 255)"""
+    rt = _reference_module(os.path.join("tools", "requant_table.py"))
+    if rt is None:
+        pytest.skip("the reference checkout is absent")
+    raw = mxfp8_bytes(512, 22)
+    lut = rt.e4m3_lut()
+    exp2 = np.array([2.0 ** (i - 127) if i < 255 else 0.0 for i in range(256)], np.float64).astype(np.float32)
+    ref = (lut[raw[:, 1:]] * exp2[raw[:, 0]][:, None]).reshape(-1)
+    got = oracle.decode(43, raw, raw.shape[0] * 32)
+    assert np.array_equal(got.view(np.uint32), ref.astype(np.float32).view(np.uint32))
+
+
 @pytest.mark.parametrize("name,mode", MODES)
 def test_oracle_matches_reference_build(oracle, reference, name, mode):
     """fresh inputs (all four self-test matrices at 32 x 2304) against the reference's own code"""

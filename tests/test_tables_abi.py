@@ -85,7 +85,10 @@ def test_block_bytes_and_source_types():
         assert lib.gpuq_block_bytes(t) == b
     for t in (0, 1, 2, 3, 15, 24, 30, 39):
         assert lib.gpuq_block_bytes(t) == 0
-    assert [lib.gpuq_can_dequantize(s) for s in (0, 1, 8, 30, 39, 2, 16)] == [1, 1, 1, 1, 1, 0, 0]
+    # the reference's five sources, NVFP4 and unsloth's MXFP8 rows, the k-/i-quants with a device to_float; not
+    # Q4_0 (2) or IQ4_NL (20), whose to_float this library does not have
+    srcs = (0, 1, 8, 30, 39, 40, 43, 16, 29, 23, 10, 14, 2, 20)
+    assert [lib.gpuq_can_dequantize(s) for s in srcs] == [1] * 12 + [0, 0]
     assert lib.gpuq_can_dequantize_type(23) == 1 and lib.gpuq_can_dequantize_type(20) == 0
 
 

@@ -145,6 +145,8 @@ struct Device {
     void * h_out[NSLOT] = {}; size_t cap_hout[NSLOT] = {};   // pinned staging for pageable destinations
     void * h_src[NSLOT] = {}; size_t cap_hsrc[NSLOT] = {};   // pinned staging for pageable sources
     float * d_qw = nullptr; size_t cap_qw = 0;
+    void * d_f32[NSLOT] = {}; size_t cap_f32[NSLOT] = {};   // staged sources: the chunk decoded to float32
+    float * d_scale = nullptr; size_t cap_scale = 0;         // per-matrix second scales
 
     const SearchTab * tab(int type) const {
         const int want = type == IQ1_M ? IQ1_S : type;
@@ -231,8 +233,8 @@ Device * current_device() {
 }
 
 size_t raw_bytes(int src, int64_t n) {
-    const int b = src_bytes32(src);
-    return b && n >= 0 ? (size_t) (n / 32) * b : 0;
+    const int bl = src_block_len(src);
+    return bl && n >= 0 ? (size_t) (n / bl) * src_block_bytes(src) : 0;
 }
 
 bool type_ok(int type, int64_t n_per_row, const void * imatrix) {
@@ -261,6 +263,7 @@ struct HostJob {
     uint8_t * dst;                 // host output bytes
     int64_t nmat, nrow, n_per_row;
     const float * imatrix;         // host, nmat x n_per_row, or null
+    const float * mat_scale;       // host, nmat per-matrix scales applied after decoding, or null
     std::vector<Chunk> chunks;
     std::atomic<bool> cancel{false};   // set by a device worker that failed: the others stop before their next chunk
 };
@@ -318,6 +321,15 @@ bool run_chunks(Device & d, HostJob & j, size_t c0, size_t c1) {
         if (!grow((void **) &d.d_qw, &d.cap_qw, qb)) return false;
         if (cudaMemcpyAsync(d.d_qw, j.imatrix, qb, cudaMemcpyHostToDevice, d.s_h2d) != cudaSuccess) { set_err("imatrix copy failed"); return false; }
     }
+    // staged sources (and any source with per-matrix scales) are decoded to float32 by their own pass first
+    const bool staged = !src_bytes32(j.src) || j.mat_scale;
+    if (j.mat_scale) {
+        if (!grow((void **) &d.d_scale, &d.cap_scale, (size_t) j.nmat * 4)) return false;
+        if (cudaMemcpyAsync(d.d_scale, j.mat_scale, (size_t) j.nmat * 4, cudaMemcpyHostToDevice, d.s_h2d) != cudaSuccess) {
+            set_err("scale copy failed"); return false;
+        }
+    }
+    const DequantTab src_tab{d.dq_grid(j.src)};
     const bool src_pinned = is_pinned(j.raw), dst_pinned = is_pinned(j.dst);
     cudaMemsetAsync(d.status, 0, sizeof(unsigned), d.s_run);
     struct Pending { bool on = false; uint8_t * dst = nullptr; size_t bytes = 0; };
@@ -329,7 +341,7 @@ bool run_chunks(Device & d, HostJob & j, size_t c0, size_t c1) {
         else if (!dst_pinned) std::memcpy(pend[slot].dst, d.h_out[slot], pend[slot].bytes);
         pend[slot].on = false;
     };
-    // the imatrix copy must land before the first kernel
+    // the imatrix and scale copies must land before the first kernel
     cudaEvent_t ev_qw = nullptr;
     cudaEventCreateWithFlags(&ev_qw, cudaEventDisableTiming);
     cudaEventRecord(ev_qw, d.s_h2d);
@@ -346,7 +358,8 @@ bool run_chunks(Device & d, HostJob & j, size_t c0, size_t c1) {
         finish(slot);   // the slot's previous chunk: its bytes are out, its buffers free
         if (!grow(&d.d_src[slot], &d.cap_src[slot], in_bytes) || !grow(&d.d_out[slot], &d.cap_out[slot], out_bytes) ||
             (!dst_pinned && !grow(&d.h_out[slot], &d.cap_hout[slot], out_bytes, true)) ||
-            (!src_pinned && !grow(&d.h_src[slot], &d.cap_hsrc[slot], in_bytes, true))) { ok = false; break; }
+            (!src_pinned && !grow(&d.h_src[slot], &d.cap_hsrc[slot], in_bytes, true)) ||
+            (staged && !grow(&d.d_f32[slot], &d.cap_f32[slot], (size_t) nv * 4))) { ok = false; break; }
         const uint8_t * hsrc = j.raw + raw_bytes(j.src, v0);
         if (!src_pinned) {   // (the slot's previous H2D is done: finish() waited for its D2H, which followed it)
             host_copy(d.h_src[slot], hsrc, in_bytes);
@@ -360,9 +373,13 @@ bool run_chunks(Device & d, HostJob & j, size_t c0, size_t c1) {
         cudaEventRecord(d.ev_h2d[slot], d.s_h2d);
         cudaStreamWaitEvent(d.s_run, d.ev_h2d[slot], 0);
         cudaStreamWaitEvent(d.s_run, d.ev_d2h[slot], 0);   // the output buffer's previous D2H is done
+        if (staged && launch_stage(j.src, d.d_src[slot], (float *) d.d_f32[slot], nv, src_tab, j.mat_scale ? d.d_scale : nullptr,
+                                   j.nrow * j.n_per_row, v0, d.s_run) != cudaSuccess) {
+            set_err("source decode launch failed: %s", cudaGetErrorString(cudaGetLastError())); ok = false; break;
+        }
         LaunchArgs a{};
-        a.src_type = j.src;
-        a.src = d.d_src[slot];
+        a.src_type = staged ? (int) SRC_F32 : j.src;
+        a.src = staged ? d.d_f32[slot] : d.d_src[slot];
         a.qw = want_qw ? d.d_qw + c.m0 * j.n_per_row : nullptr;
         a.qw_mod = nb_row; a.qw_div = 1; a.qw_mat = rows * nb_row;
         a.out = d.d_out[slot];
@@ -529,7 +546,7 @@ size_t gpuq_quantize_batch(int type, const float * src, void * dst, int64_t nmat
             return 0;
         }
     }
-    HostJob j{type, SRC_F32, (const uint8_t *) src, (uint8_t *) dst, nmat, nrow, n_per_row, imatrix, {}};
+    HostJob j{type, SRC_F32, (const uint8_t *) src, (uint8_t *) dst, nmat, nrow, n_per_row, imatrix, nullptr, {}};
     return run_host_job(j);
 }
 
@@ -537,20 +554,43 @@ size_t gpuq_quantize(int type, const float * src, void * dst, int64_t nrow, int6
     return gpuq_quantize_batch(type, src, dst, 1, nrow, n_per_row, imatrix);
 }
 
-int gpuq_can_dequantize(int src) { return raw_bytes(src, 32) > 0 ? 1 : 0; }
+int gpuq_can_dequantize(int src) { return src_block_len(src) > 0 ? 1 : 0; }
+
+}  // extern "C"
+
+namespace {
+// checks of a requantize call from host bytes (the callers hold no lock)
+bool requantize_args_ok(int src, const void * raw, int type, const void * dst, int64_t nmat, int64_t nrow,
+                        int64_t n_per_row, const float * imatrix) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    const int sl = src_block_len(src);
+    if (!sl) { set_err("source type %d cannot be read on the GPU", src); return false; }
+    if (g_active.empty()) { set_err("gpuq_init has not been called"); return false; }
+    if (nmat <= 0 || nrow <= 0) { set_err("empty batch"); return false; }
+    if (!raw || !dst) { set_err("null source or destination"); return false; }
+    if (!type_ok(type, n_per_row, imatrix)) return false;
+    if (n_per_row % sl) { set_err("row length %lld is not a multiple of source type %d's %d-value blocks", (long long) n_per_row, src, sl); return false; }
+    if (is_block_src(src) && src != IQ4_XS && !is_kquant(src) && !g_active[0]->dq_grid(src)) {
+        set_err("source type %d: no dequant grid (gpuq_init first)", src); return false;
+    }
+    return true;
+}
+}  // namespace
+
+extern "C" {
 
 size_t gpuq_requantize_batch(int src, const void * raw, int type, void * dst, int64_t nmat, int64_t nrow,
                              int64_t n_per_row, const float * imatrix) {
-    {
-        std::lock_guard<std::mutex> lk(g_mu);
-        const int64_t n = nmat * nrow * n_per_row;
-        if (nmat <= 0 || nrow <= 0 || !raw || !dst || !raw_bytes(src, 32) || n % 32 || !type_ok(type, n_per_row, imatrix)) {
-            if (!raw_bytes(src, 32)) set_err("source type %d cannot be read on the GPU", src);
-            else if (nmat <= 0 || nrow <= 0) set_err("empty batch");
-            return 0;
-        }
-    }
-    HostJob j{type, src, (const uint8_t *) raw, (uint8_t *) dst, nmat, nrow, n_per_row, imatrix, {}};
+    if (!requantize_args_ok(src, raw, type, dst, nmat, nrow, n_per_row, imatrix)) return 0;
+    HostJob j{type, src, (const uint8_t *) raw, (uint8_t *) dst, nmat, nrow, n_per_row, imatrix, nullptr, {}};
+    return run_host_job(j);
+}
+
+size_t gpuq_requantize_scaled_batch(int src, const void * raw, int type, void * dst, int64_t nmat, int64_t nrow,
+                                    int64_t n_per_row, const float * imatrix, const float * mat_scale) {
+    if (!requantize_args_ok(src, raw, type, dst, nmat, nrow, n_per_row, imatrix)) return 0;
+    if (!mat_scale) { set_err("gpuq_requantize_scaled_batch: null scales"); return 0; }
+    HostJob j{type, src, (const uint8_t *) raw, (uint8_t *) dst, nmat, nrow, n_per_row, imatrix, mat_scale, {}};
     return run_host_job(j);
 }
 
@@ -584,8 +624,13 @@ size_t gpuq_quantize_dev(int type, const float * d_x, void * d_dst, int64_t nblo
 size_t gpuq_requantize_dev(int src, const void * d_raw, int type, void * d_dst, int64_t nmat, int64_t nrow,
                            int64_t n_per_row, const float * d_imatrix, void * stream) {
     const int64_t n = nmat * nrow * n_per_row;
-    if (nmat <= 0 || nrow <= 0 || !d_raw || !d_dst || !raw_bytes(src, 32) || n % 32) {
+    if (nmat <= 0 || nrow <= 0 || !d_raw || !d_dst || n % 32) {
         set_err("gpuq_requantize_dev: bad arguments");
+        return 0;
+    }
+    if (!src_bytes32(src)) {   // (a staged source needs a float32 buffer: the device API keeps no scratch)
+        set_err("gpuq_requantize_dev: source type %d is decoded by its own pass: gpuq_dequantize_src_dev into a float32 "
+                "buffer, then gpuq_requantize_dev with source 0 (F32)", src);
         return 0;
     }
     Device * d = current_device();
@@ -674,8 +719,15 @@ size_t gpuq_ldlq_update_dev(const double * d_es, const double * d_u, float * d_w
 }
 
 size_t gpuq_dequantize_src_dev(int src, const void * d_raw, float * d_out, int64_t n, void * stream) {
-    if (!raw_bytes(src, 32) || n <= 0 || n % 32 || !d_raw || !d_out) { set_err("gpuq_dequantize_src_dev: bad arguments"); return 0; }
-    if (launch_decode(src, d_raw, d_out, n, (cudaStream_t) stream) != cudaSuccess) { set_err("gpuq_dequantize_src_dev: launch failed"); return 0; }
+    const int sl = src_block_len(src);
+    if (!sl || n <= 0 || n % sl || n % 32 || !d_raw || !d_out) { set_err("gpuq_dequantize_src_dev: bad arguments"); return 0; }
+    DequantTab tab{nullptr};
+    if (is_block_src(src)) {
+        Device * d = current_device();
+        tab.grid = d ? d->dq_grid(src) : nullptr;
+        if (!tab.grid && !(src == IQ4_XS || is_kquant(src))) { set_err("gpuq_dequantize_src_dev: no dequant grid for source type %d (gpuq_init first)", src); return 0; }
+    }
+    if (launch_decode(src, d_raw, d_out, n, tab, (cudaStream_t) stream) != cudaSuccess) { set_err("gpuq_dequantize_src_dev: launch failed"); return 0; }
     return (size_t) n * 4;
 }
 

@@ -16,7 +16,8 @@ constexpr int QK = 256;
 
 enum Type : int { IQ2_XXS = 16, IQ2_XS = 17, IQ3_XXS = 18, IQ1_S = 19, IQ4_NL = 20, IQ3_S = 21, IQ2_S = 22,
                   IQ4_XS = 23, IQ1_M = 29, Q8_0 = 8, Q2_K = 10, Q3_K = 11, Q4_K = 12, Q5_K = 13, Q6_K = 14 };
-enum Src : int { SRC_F32 = 0, SRC_F16 = 1, SRC_Q8_0 = 8, SRC_BF16 = 30, SRC_MXFP4 = 39 };
+enum Src : int { SRC_F32 = 0, SRC_F16 = 1, SRC_Q8_0 = 8, SRC_BF16 = 30, SRC_MXFP4 = 39, SRC_NVFP4 = 40,
+                 SRC_MXFP8 = 43 };
 
 // bytes of one block of each type (ggml-common.h block_* layouts)
 __host__ __device__ constexpr int block_bytes(int t) {
@@ -26,9 +27,24 @@ __host__ __device__ constexpr int block_bytes(int t) {
 }
 __host__ __device__ constexpr int block_len(int t) { return t == IQ4_NL || t == Q8_0 ? 32 : QK; }
 
-// source bytes a 32-value block (ggml types F32 / F16 / BF16 / Q8_0 / MXFP4)
+// Source tensors. "Inline" sources are decoded by the quantize kernels themselves, in their loads (F32, F16, BF16,
+// Q8_0, MXFP4); the other readable sources are "staged": one decode pass writes float32 first (NVFP4; the MXFP8 row
+// layout of unsloth's type 43 - an E8M0 scale byte and 32 E4M3 bytes a block, tools/requant_table.py:8-9; and every
+// 256-block k-quant and i-quant with a device to_float), after which the F32 kernels run.
+// source bytes a 32-value block of an inline source, 0 for any other
 __host__ __device__ constexpr int src_bytes32(int s) {
     return s == SRC_F32 ? 128 : s == SRC_F16 || s == SRC_BF16 ? 64 : s == SRC_Q8_0 ? 34 : s == SRC_MXFP4 ? 17 : 0;
+}
+__host__ __device__ constexpr bool is_block_src(int s) {
+    return s == IQ2_XXS || s == IQ2_XS || s == IQ2_S || s == IQ3_XXS || s == IQ3_S || s == IQ1_S || s == IQ1_M ||
+           s == IQ4_XS || s == Q2_K || s == Q3_K || s == Q4_K || s == Q5_K || s == Q6_K;
+}
+// values and bytes of one block of any readable source (0: not readable on the GPU)
+__host__ __device__ constexpr int src_block_len(int s) {
+    return src_bytes32(s) ? 32 : s == SRC_NVFP4 ? 64 : s == SRC_MXFP8 ? 32 : is_block_src(s) ? QK : 0;
+}
+__host__ __device__ constexpr int src_block_bytes(int s) {
+    return src_bytes32(s) ? src_bytes32(s) : s == SRC_NVFP4 ? 36 : s == SRC_MXFP8 ? 33 : is_block_src(s) ? block_bytes(s) : 0;
 }
 
 // ---------------------------------------------------------------------------------------------- device status

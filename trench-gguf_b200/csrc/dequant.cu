@@ -212,20 +212,47 @@ __global__ void __launch_bounds__(256) k_dequant_error(const uint8_t * __restric
     }
 }
 
+// 8 floats to out (16-byte stores when aligned), each times `s` when a per-matrix scale applies
+__device__ __forceinline__ void store8(float * out, float * y, const float * scale, int64_t vglob, int64_t per_mat) {
+    if (scale) {
+        const float s = __ldg(scale + vglob / per_mat);   // (8 values never straddle two matrices: per_mat % 8 == 0)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) y[j] = y[j] * s;
+    }
+    if ((reinterpret_cast<uintptr_t>(out) & 15) == 0) {
+        float4 * o = reinterpret_cast<float4 *>(out);
+        o[0] = make_float4(y[0], y[1], y[2], y[3]);
+        o[1] = make_float4(y[4], y[5], y[6], y[7]);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) out[j] = y[j];
+    }
+}
+
+// source values -> float32, 8 a thread (the element formats); value i of the pass is value v0 + i of the tensor,
+// whose matrix (v0 + i) / per_mat picks the scale
 template <int SRC>
-__global__ void __launch_bounds__(256) k_decode(const uint8_t * __restrict__ raw, float * __restrict__ out, int64_t n8) {
+__global__ void __launch_bounds__(256) k_decode(const uint8_t * __restrict__ raw, float * __restrict__ out, int64_t n8,
+                                                const float * __restrict__ scale, int64_t per_mat, int64_t v0) {
     const int64_t stride = (int64_t) gridDim.x * blockDim.x;
     for (int64_t i = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += stride) {
         float y[8];
         decode8<SRC>(raw, i * 8, y);
-        if ((reinterpret_cast<uintptr_t>(out) & 15) == 0) {
-            float4 * o = reinterpret_cast<float4 *>(out + i * 8);
-            o[0] = make_float4(y[0], y[1], y[2], y[3]);
-            o[1] = make_float4(y[4], y[5], y[6], y[7]);
-        } else {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) out[i * 8 + j] = y[j];
-        }
+        store8(out + i * 8, y, scale, v0 + i * 8, per_mat);
+    }
+}
+
+// a k-quant / i-quant source -> float32: ggml's to_float, a warp a super-block, then the per-matrix scale
+template <int T>
+__global__ void __launch_bounds__(256) k_decode_blocks(const uint8_t * __restrict__ q, float * __restrict__ out,
+                                                       int64_t nblocks, const uint64_t * __restrict__ grid,
+                                                       const float * __restrict__ scale, int64_t per_mat, int64_t v0) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = (int64_t) gridDim.x * (blockDim.x >> 5);
+    for (int64_t b = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); b < nblocks; b += nw) {
+        float y[8];
+        dq8<T>(q + b * block_bytes(T), lane, grid, y);
+        store8(out + b * QK + lane * 8, y, scale, v0 + b * QK + lane * 8, per_mat);
     }
 }
 
@@ -288,19 +315,49 @@ cudaError_t launch_dequant_error(int type, const void * q, const float * blk, vo
     return cudaGetLastError();
 }
 
-cudaError_t launch_decode(int src, const void * raw, float * out, int64_t n, cudaStream_t st) {
+cudaError_t launch_stage(int src, const void * raw, float * out, int64_t n, DequantTab tab, const float * scale,
+                         int64_t per_mat, int64_t v0, cudaStream_t st) {
+    const uint8_t * r = (const uint8_t *) raw;
+    if (is_block_src(src)) {
+        const int64_t nb = n / QK;
+        const int g = grid_for(nb, 8);
+#define KB(T) k_decode_blocks<T><<<g, 256, 0, st>>>(r, out, nb, tab.grid, scale, per_mat, v0)
+        switch (src) {
+            case IQ2_XXS: KB(IQ2_XXS); break;
+            case IQ2_XS:  KB(IQ2_XS); break;
+            case IQ2_S:   KB(IQ2_S); break;
+            case IQ3_XXS: KB(IQ3_XXS); break;
+            case IQ3_S:   KB(IQ3_S); break;
+            case IQ1_S:   KB(IQ1_S); break;
+            case IQ1_M:   KB(IQ1_M); break;
+            case IQ4_XS:  KB(IQ4_XS); break;
+            case Q2_K:    KB(Q2_K); break;
+            case Q3_K:    KB(Q3_K); break;
+            case Q4_K:    KB(Q4_K); break;
+            case Q5_K:    KB(Q5_K); break;
+            case Q6_K:    KB(Q6_K); break;
+            default: return cudaErrorInvalidValue;
+        }
+#undef KB
+        return cudaGetLastError();
+    }
     const int64_t n8 = n / 8;
     const int g = grid_for(n8, 256);
-    const uint8_t * r = (const uint8_t *) raw;
     switch (src) {
-        case SRC_F32:   k_decode<SRC_F32><<<g, 256, 0, st>>>(r, out, n8); break;
-        case SRC_F16:   k_decode<SRC_F16><<<g, 256, 0, st>>>(r, out, n8); break;
-        case SRC_BF16:  k_decode<SRC_BF16><<<g, 256, 0, st>>>(r, out, n8); break;
-        case SRC_Q8_0:  k_decode<SRC_Q8_0><<<g, 256, 0, st>>>(r, out, n8); break;
-        case SRC_MXFP4: k_decode<SRC_MXFP4><<<g, 256, 0, st>>>(r, out, n8); break;
+        case SRC_F32:   k_decode<SRC_F32><<<g, 256, 0, st>>>(r, out, n8, scale, per_mat, v0); break;
+        case SRC_F16:   k_decode<SRC_F16><<<g, 256, 0, st>>>(r, out, n8, scale, per_mat, v0); break;
+        case SRC_BF16:  k_decode<SRC_BF16><<<g, 256, 0, st>>>(r, out, n8, scale, per_mat, v0); break;
+        case SRC_Q8_0:  k_decode<SRC_Q8_0><<<g, 256, 0, st>>>(r, out, n8, scale, per_mat, v0); break;
+        case SRC_MXFP4: k_decode<SRC_MXFP4><<<g, 256, 0, st>>>(r, out, n8, scale, per_mat, v0); break;
+        case SRC_NVFP4: k_decode<SRC_NVFP4><<<g, 256, 0, st>>>(r, out, n8, scale, per_mat, v0); break;
+        case SRC_MXFP8: k_decode<SRC_MXFP8><<<g, 256, 0, st>>>(r, out, n8, scale, per_mat, v0); break;
         default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
+}
+
+cudaError_t launch_decode(int src, const void * raw, float * out, int64_t n, DequantTab tab, cudaStream_t st) {
+    return launch_stage(src, raw, out, n, tab, nullptr, 1, 0, st);
 }
 
 }  // namespace gq

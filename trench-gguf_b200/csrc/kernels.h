@@ -40,8 +40,12 @@ cudaError_t launch_ldlq_scale(const double * E, const double * Rd, double * Es, 
                               int64_t nblk, int k, cudaStream_t st);
 cudaError_t launch_ldlq_update(const double * Es, const double * U, float * W, int64_t ngroups, int64_t rows, int64_t ne0,
                                int k, cudaStream_t st);
-// source bytes (F32 / F16 / BF16 / Q8_0 / MXFP4) -> n floats
-cudaError_t launch_decode(int src, const void * raw, float * out, int64_t n, cudaStream_t st);
+// n values of any readable source (common.cuh src_block_len) -> n floats; tab: the dequant grid of an i-quant source
+cudaError_t launch_decode(int src, const void * raw, float * out, int64_t n, DequantTab tab, cudaStream_t st);
+// the same, value i (of this pass; value v0 + i of the tensor) multiplied by scale[(v0 + i) / per_mat] when scale
+// is not null (a per-matrix second scale, as NVFP4 experts carry)
+cudaError_t launch_stage(int src, const void * raw, float * out, int64_t n, DequantTab tab, const float * scale,
+                         int64_t per_mat, int64_t v0, cudaStream_t st);
 
 // The current device's search table of `type` (from gpuq_init), or null when the device is not initialized or the
 // type has no table. Implemented in api.cu.

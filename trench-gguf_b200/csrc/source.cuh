@@ -53,6 +53,35 @@ __device__ __forceinline__ void decode8(const uint8_t * __restrict__ raw, int64_
         const float d = half_to_float((uint16_t) (__ldg(b) | (__ldg(b + 1) << 8)));
 #pragma unroll
         for (int j = 0; j < 8; ++j) out[j] = (float) (int8_t) __ldg(b + 2 + o + j) * d;
+    } else if constexpr (SRC == SRC_NVFP4) {   // 64 values: 4 UE4M3 scales (one a 16 values), then 4 x 8 bytes of
+        const uint8_t * b = raw + (v0 / 64) * 36;   // e2m1 pairs (group j: low nibbles values 0..7, high 8..15)
+        const int o = (int) (v0 % 64), j = o / 16, sh = (o & 8) ? 4 : 0;
+        const uint8_t sb = __ldg(b + j);
+        const int ex = (sb >> 3) & 0xF, mn = sb & 7;
+        // the scale is UE4M3 times 0.5 (gguf-py's ue4m3_to_fp32): mn * 2^-10 or (8 + mn) * 2^(ex - 11), exact
+        const float d = (sb == 0 || sb == 0x7F) ? 0.0f : ex == 0 ? (float) mn * 0x1.0p-10f : (float) (8 + mn) * u2f((uint32_t) (ex + 116) << 23);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int c = (__ldg(b + 4 + 8 * j + i) >> sh) & 15;
+            const int m = c & 7;
+            const int mag = m < 5 ? m : (m == 5 ? 6 : (m == 6 ? 8 : 12));
+            out[i] = d * (float) (c & 8 ? -mag : mag);
+        }
+    } else if constexpr (SRC == SRC_MXFP8) {   // 33-byte blocks: E8M0 scale 2^(e-127) (e = 255: 0), 32 E4M3 values
+        const uint8_t * b = raw + (v0 / 32) * 33;
+        const int o = (int) (v0 % 32);
+        const uint8_t e = __ldg(b);
+        const float sc = e == 255 ? 0.0f : e == 0 ? u2f(0x00400000u) : u2f((uint32_t) e << 23);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint8_t q = __ldg(b + 1 + o + i);
+            const int ex = (q >> 3) & 0xF, mn = q & 7;
+            // E4M3 (the FN variant: no infinities; 0x7F and 0xFF the NaNs, read as +0 as the reference's table does):
+            // mn * 2^-9 or (8 + mn) * 2^(ex - 10)
+            float v = ex == 0 ? (float) mn * 0x1.0p-9f : (float) (8 + mn) * u2f((uint32_t) (ex + 117) << 23);
+            if (q & 0x80) v = -v;
+            out[i] = (ex == 15 && mn == 7) ? 0.0f * sc : v * sc;
+        }
     } else {                                   // MXFP4 block: e8m0 scale, 16 bytes of two e2m1 codes
         const uint8_t * b = raw + (v0 / 32) * 17;
         const int o = (int) (v0 % 32);          // 0, 8: low nibbles of qs[o..o+7]; 16, 24: high nibbles of qs[o-16..]

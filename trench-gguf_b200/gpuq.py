@@ -16,9 +16,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 TYPES = {"IQ2_XXS": 16, "IQ2_XS": 17, "IQ3_XXS": 18, "IQ1_S": 19, "IQ4_NL": 20, "IQ3_S": 21, "IQ2_S": 22,
          "IQ4_XS": 23, "IQ1_M": 29, "Q8_0": 8, "Q2_K": 10, "Q3_K": 11, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14}
-SOURCES = {"F32": 0, "F16": 1, "Q8_0": 8, "BF16": 30, "MXFP4": 39}
+SOURCES = {"F32": 0, "F16": 1, "Q8_0": 8, "BF16": 30, "MXFP4": 39, "NVFP4": 40, "MXFP8": 43}
 BLOCK_LEN = {t: (32 if n in ("IQ4_NL", "Q8_0") else 256) for n, t in TYPES.items()}
-SRC_BYTES32 = {0: 128, 1: 64, 30: 64, 8: 34, 39: 17}
+SRC_BYTES32 = {0: 128, 1: 64, 30: 64, 8: 34, 39: 17}   # (the five sources the quantize kernels decode inline)
 # the types ggml quantizes without an imatrix as well (k-quants' *_ref path, IQ4 with x^2 weights)
 NO_IMATRIX_OK = {8, 10, 11, 12, 13, 14, 20, 23}
 
@@ -27,7 +27,7 @@ SYMBOLS = ("gpuq_init", "gpuq_block_bytes", "gpuq_can_quantize", "gpuq_quantize"
            "gpuq_can_dequantize_type", "gpuq_dequantize_dev", "gpuq_dequantize_src_dev",
            "gpuq_last_error", "gpuq_status", "gpuq_init_devices", "gpuq_device_count", "gpuq_requantize_dev",
            "gpuq_requantize_noalloc", "gpuq_dequantize_error_dev", "gpuq_ldlq_scale_dev",
-           "gpuq_ldlq_update_dev")
+           "gpuq_ldlq_update_dev", "gpuq_requantize_scaled_batch")
 
 
 class GpuqError(RuntimeError):
@@ -71,6 +71,7 @@ def declare(gq):
         "gpuq_requantize_noalloc": (sz, [c.c_int, vp, c.c_int, vp, i64, i64, i64, vp]),
         "gpuq_dequantize_error_dev": (sz, [c.c_int, vp, vp, vp, c.c_int, i64, vp]),
         "gpuq_ldlq_scale_dev": (sz, [vp, vp, vp, i64, i64, i64, i64, vp]),
+        "gpuq_requantize_scaled_batch": (sz, [c.c_int, vp, c.c_int, vp, i64, i64, i64, vp, vp]),
         "gpuq_ldlq_update_dev": (sz, [vp, vp, vp, i64, i64, i64, i64, vp]),
     }
     for name, (res, args) in sig.items():
@@ -148,13 +149,20 @@ class Gpuq:
             raise GpuqError("gpuq_quantize_batch(type %d) returned %d, want %d: %s" % (typ, got, y.nbytes, self.error()))
         return y
 
-    def requantize(self, src, raw, typ, shape, imatrix=None, out=None):
-        """raw: the source tensor's bytes (ggml type src), shape (nmat, nrow, n_per_row) of its values"""
+    def requantize(self, src, raw, typ, shape, imatrix=None, out=None, mat_scale=None):
+        """raw: the source tensor's bytes (ggml type src), shape (nmat, nrow, n_per_row) of its values; mat_scale:
+        nmat per-matrix scales applied after decoding (NVFP4's per-expert scale), or None"""
         raw = np.ascontiguousarray(raw).view(np.uint8)
         nmat, nrow, npr = shape
         im = None if imatrix is None else np.ascontiguousarray(imatrix, dtype=np.float32)
         y = self._out(typ, nmat * nrow * npr) if out is None else out
-        got = self.lib.gpuq_requantize_batch(int(src), raw.ctypes.data, int(typ), y.ctypes.data, nmat, nrow, npr, _ptr(im))
+        if mat_scale is not None:
+            sc = np.ascontiguousarray(mat_scale, dtype=np.float32)
+            got = self.lib.gpuq_requantize_scaled_batch(int(src), raw.ctypes.data, int(typ), y.ctypes.data, nmat, nrow,
+                                                        npr, _ptr(im), sc.ctypes.data)
+        else:
+            got = self.lib.gpuq_requantize_batch(int(src), raw.ctypes.data, int(typ), y.ctypes.data, nmat, nrow, npr,
+                                                 _ptr(im))
         if got != y.nbytes:
             raise GpuqError("gpuq_requantize_batch(src %d, type %d) returned %d, want %d: %s" %
                             (src, typ, got, y.nbytes, self.error()))
