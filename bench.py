@@ -65,6 +65,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true", help="leave out the reference GPU library's leg")
+    ap.add_argument("--gate", action="store_true",
+                    help="the 384-expert IQ2_XXS tensor, host to host, one process over every visible GPU")
     ap.add_argument("--ldlq-streams", type=int, default=4,
                     help="config 5: CUDA streams the experts alternate over (the next expert's factorisation runs "
                          "beside this one's loop); 1 = one expert after another on one stream")
@@ -574,6 +576,72 @@ def run_ldlq(args, g, dev, stream, fp32, rank=0, world=1, dist=None):
     print(json.dumps(line), flush=True)
 
 
+def run_gate(args):
+    """north_star's gate: the whole 384-expert config-2 tensor (MXFP4, 384 x 2048 x 7168) re-quantized to IQ2_XXS
+    from host bytes to host bytes by ONE process through the library's own multi-device fan-out (gpuq_init_devices
+    over every visible GPU: whole experts a device, one host thread a device, each writing its slice of the output;
+    no collective), one gpuq_requantize_batch call a step - the call the reference's caller makes a batch
+    (tools/requant_experts.py:764-816). Timed on the host clock around the synchronous call, from plain numpy
+    buffers (as the reference's callers pass them) and from pinned buffers. Two experts (the first and the last) are
+    compared with the reference's host build."""
+    import torch
+    import gpuq
+    import workloads
+    ndev = torch.cuda.device_count()
+    E = args.experts if args.experts != EXPERTS_PER_GPU else 384
+    t0 = time.perf_counter()
+    raw, im = workloads.config2(experts=E, rows=ROWS, cols=COLS, seed=102)
+    gen_s = time.perf_counter() - t0
+    g = gpuq.Gpuq(devices=list(range(ndev)))
+    nbytes = E * ROWS * (COLS // 256) * 66
+    out = np.empty(nbytes, np.uint8)
+
+    def call(src, dst):
+        n = g.lib.gpuq_requantize_batch(39, ctypes.c_void_p(src), 16, ctypes.c_void_p(dst), E, ROWS, COLS, im.ctypes.data)
+        if n != nbytes:
+            raise RuntimeError("gpuq_requantize_batch: " + g.error())
+
+    def timed(src, dst):
+        call(src, dst)                                    # warm-up (buffers grown, kernels loaded)
+        ts = []
+        for _ in range(max(1, args.steps)):
+            t1 = time.perf_counter()
+            call(src, dst)
+            ts.append(time.perf_counter() - t1)
+        return statistics.median(ts), ts
+    with Clocks(0) as clk:
+        pageable_s, pageable_all = timed(raw.ctypes.data, out.ctypes.data)
+        hraw = torch.from_numpy(raw.reshape(-1)).pin_memory()
+        hout = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+        pinned_s, pinned_all = timed(hraw.data_ptr(), hout.data_ptr())
+    if not np.array_equal(hout.numpy(), out):
+        raise RuntimeError("pinned and pageable calls differ")
+    parity = None
+    if not args.no_cpu:
+        chk, kind = cpu_checker()
+        per = ROWS * (COLS // 256) * 66
+        same = tot = 0
+        for e in (0, E - 1):
+            x = chk.decode(39, raw[e].reshape(-1), ROWS * COLS).reshape(1, ROWS, COLS)
+            want = chk.quantize(16, x, im[e:e + 1], threads=os.cpu_count() or 1)
+            a, b = block_parity(out[e * per:(e + 1) * per], want, 66)
+            same, tot = same + a, tot + b
+        parity = {"blocks": tot, "identical": same, "sample": "experts 0 and %d" % (E - 1),
+                  "checker": "trench-gguf block functions built for the host (oracle/_ref)" if kind == "reference"
+                  else "C restatement (oracle/oracle.c)"}
+    line = {"metric": "seconds to re-quantize the %d-expert config-2 tensor to IQ2_XXS, host bytes to host bytes" % E,
+            "value": pageable_s, "unit": "s", "higher_is_better": False, "n_gpus": ndev, "steps": len(pageable_all),
+            "warmup": 1, "gweights_s": E * ROWS * COLS / pageable_s / 1e9,
+            "pinned": {"value": pinned_s, "unit": "s", "gweights_s": E * ROWS * COLS / pinned_s / 1e9,
+                       "all_s": pinned_all},
+            "pageable_all_s": pageable_all, "dtype": "f32", "data": "synthetic (config 2 distributions, seeded)",
+            "config": {"workload": "config 2: %d experts x %d x %d MXFP4 -> IQ2_XXS, per-expert imatrix" % (E, ROWS, COLS),
+                       "path": "one process, gpuq_init_devices over %d GPUs, one gpuq_requantize_batch call" % ndev,
+                       "h2d_bytes": int(raw.nbytes + im.nbytes), "d2h_bytes": nbytes, "input_generation_s": gen_s},
+            "target_s": 0.5, "parity": parity, "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+
+
 def init_dist(local):
     """the process group of a torchrun launch (NCCL, bound to this rank's device); anything NCCL prints while it is
     set up goes to stderr, so rank 0's stdout carries the JSON line alone"""
@@ -612,6 +680,8 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.gate:
+        return run_gate(args)
     if args.config == 5 and world > 1:
         return run_ldlq_sharded(args, rank, world, local)
     if args.config != 2:
