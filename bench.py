@@ -511,23 +511,33 @@ def run_ldlq(args, g, dev, stream, fp32, rank=0, world=1, dist=None):
         del X
     torch.cuda.synchronize()
 
-    def step():
-        return ldlq_gpu.ldlq_experts([w.clone() for w in Ws], Hs, [n] * E, gqt, ims)
+    U = torch.empty((E, ne0, ne0), dtype=torch.float64, device=dev)
+
+    def step(mid=None):
+        """ldlq_gpu.ldlq_experts's two phases, with an event between them: every expert's float64 factor, then the
+        lockstep loop of all experts"""
+        Wc = [w.clone() for w in Ws]
+        facs = [ldlq_gpu.factor_hessian(Hs[e], n, device=dev, U_out=U[e]) for e in range(E)]
+        if mid is not None:
+            mid.record()
+        return ldlq_gpu.ldlq_groups(Wc, facs, gqt, ims, U_stack=U)
     step()                                               # warm-up: cuSOLVER / cuBLAS handles, the kernels' code
     torch.cuda.synchronize()
-    times = []
+    times, factor_ms = [], []
     with Clocks(int(os.environ.get("LOCAL_RANK", "0"))) as clk:
         for _ in range(max(1, args.steps)):
             if dist:
                 dist.barrier()
             torch.cuda.synchronize()
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a, m, b = (torch.cuda.Event(enable_timing=True) for _ in range(3))
             a.record()
-            outs = step()
+            outs = step(m)
             b.record()
             torch.cuda.synchronize()
             times.append(a.elapsed_time(b))
+            factor_ms.append(a.elapsed_time(m))
     ms = statistics.median(times)
+    fms = statistics.median(factor_ms)
     t = torch.tensor([ms], dtype=torch.float64, device=dev)
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -569,6 +579,7 @@ def run_ldlq(args, g, dev, stream, fp32, rank=0, world=1, dist=None):
                                    "4096 rows), act order seq, imatrix weights; factor + lockstep loop" % E,
                        "parallelism": "expert-sharded x%d" % world},
             "per_expert_ms": ms / E, "hessian_build_ms_per_expert": hess_ms / E,
+            "phases_ms": {"factor_all_experts": fms, "lockstep_loop_all_experts": ms - fms},
             "roofline": {"bound": "fp64", "achieved": total_fl / (ms / 1e3) / 1e12, "peak": peak64, "unit": "TFLOP/s",
                          "frac": total_fl / (ms / 1e3) / 1e12 / peak64, "flop_per_expert": fl,
                          "peak_source": "trench-gguf_b200/peak.cu float64 FMA rate, measured in this run"},

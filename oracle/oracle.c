@@ -1141,15 +1141,96 @@ static int o_q8_0(const float * x, uint8_t * y) {   /* gpuq.hip:1831-1838 */
 }
 
 /* ------------------------------------------------------------------------------------------------ dispatch */
+enum { O_Q4_0 = 2, O_Q5_0 = 6, O_Q5_1 = 7 };
+static int o_is_legacy(int t) { return t == O_Q4_0 || t == O_Q5_0 || t == O_Q5_1; }
+
 static size_t o_bytes(int type) {
     switch (type) {
+        case O_Q4_0: return 18; case O_Q5_0: return 22; case O_Q5_1: return 24;
         case O_IQ2_XXS: return 66; case O_IQ2_XS: return 74; case O_IQ2_S: return 82; case O_IQ3_XXS: return 98;
         case O_IQ3_S: return 110; case O_IQ1_S: return 50; case O_IQ1_M: return 56; case O_IQ4_NL: return 18;
         case O_IQ4_XS: return 136; case O_Q2_K: return 84; case O_Q3_K: return 110; case O_Q4_K: return 144;
         case O_Q5_K: return 176; case O_Q6_K: return 210; case O_Q8_0: return 34; default: return 0;
     }
 }
-static int o_len(int type) { return type == O_IQ4_NL || type == O_Q8_0 ? 32 : QK; }
+static int o_len(int type) { return type == O_IQ4_NL || type == O_Q8_0 || o_is_legacy(type) ? 32 : QK; }
+
+/* ------------------------------------------------------------------------------------------------ Q4_0, Q5_0, Q5_1
+ * llama-quantize's fallbacks for rows a k-quant or i-quant cannot hold (tools/requant_experts.py:181-183; the
+ * reference runs them through ggml on the CPU). Without an imatrix ggml's quantize_row_q4_0_ref / q5_0_ref / q5_1_ref
+ * (32-weight blocks; d = max/-8 or max/-16 from the value of largest magnitude, or (max - min)/31 and the min);
+ * with one ggml's quantize_row_*_impl: sigma2 = the mean of x^2 over the WHOLE ROW, weights qw * sqrt(sigma2 + x^2),
+ * then make_qx_quants (Q4_0: 8 levels a side, Q5_0: 16; o_sym) or make_qkx3_quants (Q5_1: 31 levels, trials
+ * -0.9 + 0.05 k for k = 0..36; o_affine). Blocks: Q4_0 d qs[16]; Q5_0 d qh[4] qs[16]; Q5_1 d m qh[4] qs[16]. */
+static float o_sym(int n, int nmax, const float * x, int8_t * L, const float * qw);
+static float o_affine(int imat, int n, int nmax, const float * x, const float * wts, uint8_t * L, float * the_min,
+                      uint8_t * Laux, float rmin, float rdelta, int nstep, int use_mad);
+
+static void o_put_half(uint8_t * y, float f) { const uint16_t h = o_half(f); memcpy(y, &h, 2); }
+static void o_pack_nibbles(const int * L, uint8_t * qs) { for (int j = 0; j < 16; ++j) qs[j] = (uint8_t) ((L[j] & 15) | ((L[j + 16] & 15) << 4)); }
+static void o_pack_fifth(const int * L, uint8_t * qh) {
+    uint32_t h = 0;
+    for (int j = 0; j < 16; ++j) { h |= (uint32_t) ((L[j] >> 4) & 1) << j; h |= (uint32_t) ((L[j + 16] >> 4) & 1) << (j + 16); }
+    memcpy(qh, &h, 4);
+}
+
+/* one 32-weight block; w = NULL: the *_ref path */
+static void o_legacy_block(int type, const float * x, const float * w, uint8_t * y) {
+    int L[32];
+    if (type == O_Q5_1) {
+        float d, m;
+        if (!w) {
+            float mn = FLT_MAX, mx = -FLT_MAX;
+            for (int j = 0; j < 32; ++j) { if (x[j] < mn) mn = x[j]; if (x[j] > mx) mx = x[j]; }
+            d = (mx - mn) / 31;
+            const float id = d ? 1.0f / d : 0.0f;
+            m = mn;
+            for (int j = 0; j < 32; ++j) L[j] = (uint8_t) ((x[j] - mn) * id + 0.5f);
+        } else {
+            uint8_t Lu[32], aux[32];
+            float the_min;
+            d = o_affine(1, 32, 31, x, w, Lu, &the_min, aux, -0.9f, 0.05f, 36, 0);
+            m = -the_min;
+            for (int j = 0; j < 32; ++j) L[j] = Lu[j];
+        }
+        o_put_half(y, d);
+        o_put_half(y + 2, m);
+        o_pack_fifth(L, y + 4);
+        o_pack_nibbles(L, y + 8);
+        return;
+    }
+    const int nl = type == O_Q4_0 ? 8 : 16;
+    float d;
+    if (!w) {
+        float amax = 0, mx = 0;
+        for (int j = 0; j < 32; ++j) if (amax < fabsf(x[j])) { amax = fabsf(x[j]); mx = x[j]; }
+        d = mx / -nl;
+        const float id = d ? 1.0f / d : 0.0f;
+        for (int j = 0; j < 32; ++j) { const int v = (int8_t) (x[j] * id + (nl + 0.5f)); L[j] = v < 2 * nl - 1 ? v : 2 * nl - 1; }
+    } else {
+        int8_t Ls[32];
+        d = o_sym(32, nl, x, Ls, w);
+        for (int j = 0; j < 32; ++j) L[j] = Ls[j];
+    }
+    o_put_half(y, d);
+    if (type == O_Q4_0) o_pack_nibbles(L, y + 2);
+    else { o_pack_fifth(L, y + 2); o_pack_nibbles(L, y + 6); }
+}
+
+/* one row of n weights (ggml's quantize_q*_0 / q5_1 call quantize_row_*_impl a row at a time) */
+static void o_legacy_row(int type, const float * x, int64_t n, const float * qw, uint8_t * y) {
+    float sigma2 = 0, w[32];
+    if (qw) {
+        float s = 0;
+        for (int64_t j = 0; j < n; ++j) s += x[j] * x[j];
+        sigma2 = s / n;
+    }
+    for (int64_t ib = 0; ib < n / 32; ++ib) {
+        const float * xb = x + 32 * ib;
+        if (qw) for (int j = 0; j < 32; ++j) w[j] = qw[32 * ib + j] * sqrtf(sigma2 + xb[j] * xb[j]);
+        o_legacy_block(type, xb, qw ? w : NULL, y + ib * o_bytes(type));
+    }
+}
 static int o_needs_tab(int type) {
     return type == O_IQ2_XXS || type == O_IQ2_XS || type == O_IQ2_S || type == O_IQ3_XXS || type == O_IQ3_S ||
            type == O_IQ1_S || type == O_IQ1_M;
@@ -1379,6 +1460,13 @@ size_t orc_quantize_batch(int type, const float * x, void * y, int64_t nmat, int
     const int bs = o_len(type);
     if (!o_bytes(type) || nmat <= 0 || nrow <= 0 || n_per_row % bs) return 0;
     const int64_t nb_row = n_per_row / bs, nb_mat = nrow * nb_row;
+    if (o_is_legacy(type)) {   /* (row by row: the imatrix path's sigma2 is a row's) */
+        (void) nthreads;
+        for (int64_t r = 0; r < nmat * nrow; ++r)
+            o_legacy_row(type, x + r * n_per_row, n_per_row, imatrix ? imatrix + (r / nrow) * n_per_row : NULL,
+                         (uint8_t *) y + (size_t) r * nb_row * o_bytes(type));
+        return (size_t) nmat * nb_mat * o_bytes(type);
+    }
     const float * qw = (imatrix && type != O_Q8_0) ? imatrix : NULL;
     return o_blocks(type, x, qw, y, nmat * nb_mat, nb_row, 1, nb_mat, nthreads);
 }

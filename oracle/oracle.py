@@ -20,7 +20,9 @@ LIBS = {"oracle": (os.path.join(HERE, "_build", "liboracle.so"), "orc_"),
 
 TYPES = {"IQ2_XXS": 16, "IQ2_XS": 17, "IQ3_XXS": 18, "IQ1_S": 19, "IQ4_NL": 20, "IQ3_S": 21, "IQ2_S": 22,
          "IQ4_XS": 23, "IQ1_M": 29, "Q8_0": 8, "Q2_K": 10, "Q3_K": 11, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14}
-SOURCES = {"F32": 0, "F16": 1, "Q8_0": 8, "BF16": 30, "MXFP4": 39}
+SOURCES = {"F32": 0, "F16": 1, "Q8_0": 8, "BF16": 30, "MXFP4": 39, "NVFP4": 40, "MXFP8": 43}
+# the 32-weight fallback types (llama-quantize's tensor_type_fallback targets for rows a k-quant cannot hold)
+LEGACY = {"Q4_0": 2, "Q5_0": 6, "Q5_1": 7}
 
 
 def available(kind):

@@ -137,6 +137,32 @@ def test_device_api_decode_staged(gpuq, oracle, src):
     assert "gpuq_dequantize_src_dev" in gpuq.error()
 
 
+@pytest.mark.parametrize("name", ["Q4_0", "Q5_0", "Q5_1"])
+def test_legacy_fallback_types(gpuq, oracle, monkeypatch, name):
+    """the fallback types (llama-quantize's targets for rows a k-quant cannot hold: Q2_K/Q3_K -> Q4_0, Q4_K -> Q5_0,
+    Q5_K -> Q5_1, tools/requant_experts.py:181-183; the reference runs them on the CPU) == ggml's, with and without an
+    imatrix, from f32 and from BF16 / MXFP4 bytes, on rows whose mean square (the imatrix path's sigma2) spans many
+    blocks and several pipeline chunks; a row length 256 does not divide (704, Gemma-style down rows) included"""
+    t = orc.LEGACY[name]
+    rng = np.random.default_rng(61)
+    for npr in (1024, 704):
+        x = (rng.standard_t(4, (3, 40, npr)) * 0.02).astype(np.float32)
+        x[0, 1, :32] = 0
+        x[1, 2, 32:64] = 0.0125
+        im = rng.gamma(1.0, 1.0, (3, npr)).astype(np.float32)
+        for imx in (im, None):
+            want = oracle.quantize(t, x, imx)
+            assert np.array_equal(gpuq.quantize(t, x, imx), want), (name, npr, imx is None)
+    monkeypatch.setenv("GPUQ_CHUNK_MW", "1")
+    raw, im = workloads.config3(experts=2, rows=64, cols=2048, seed=62)
+    xb = oracle.decode(30, raw, raw.size).reshape(2, 64, 2048)
+    assert np.array_equal(gpuq.requantize(30, raw, t, (2, 64, 2048), im), oracle.quantize(t, xb, im))
+    raw4, im4 = workloads.config2(experts=2, rows=16, cols=7168, seed=63)
+    x4 = oracle.decode(39, raw4, raw4.size // 17 * 32).reshape(2, 16, 7168)
+    assert np.array_equal(gpuq.requantize(39, raw4, t, (2, 16, 7168), im4), oracle.quantize(t, x4, im4))
+    assert np.array_equal(gpuq.requantize(39, raw4, t, (2, 16, 7168), None), oracle.quantize(t, x4, None))
+
+
 def test_chunked_pipeline_matches_one_chunk(gpuq, oracle, monkeypatch):
     """many pipeline chunks (whole matrices and row ranges of one matrix) == the oracle"""
     raw, im = workloads.config3(experts=3, rows=16, cols=7168, seed=5)

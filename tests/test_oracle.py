@@ -79,6 +79,26 @@ def test_oracle_kquant_dequant_matches_gguf(oracle, golden, name):
         assert np.array_equal(got.view(np.uint32), ref.astype(np.float32).view(np.uint32)), (name, mode)
 
 
+@pytest.mark.parametrize("name", ["Q4_0", "Q5_0", "Q5_1"])
+def test_oracle_legacy_ref_matches_gguf(oracle, name):
+    """the fallback types without an imatrix (ggml's quantize_row_q*_ref) against gguf-py's quantizers, byte for byte,
+    on Student-t rows with an all-zero, a constant and a one-signed block"""
+    from gguf import quants as gq, GGMLQuantizationType as G
+    rng = np.random.default_rng(23)
+    x = (rng.standard_t(4, (16, 1024)) * 0.02).astype(np.float32)
+    x[1, :32] = 0
+    x[2, 32:64] = 0.0125
+    x[3, 64:128] = np.abs(x[3, 64:128])
+    t = orc.LEGACY[name]
+    got = oracle.quantize(t, x, None)
+    assert np.array_equal(got, gq.quantize(x, G[name]).reshape(-1)), name
+    # the imatrix path (ggml's quantize_row_*_impl) writes blocks of the same format that decode close to x
+    im = rng.gamma(1.0, 1.0, 1024).astype(np.float32)
+    q = oracle.quantize(t, x, im[None])
+    y = gq.dequantize(q.reshape(16, -1), G[name]).reshape(x.shape)
+    assert np.abs(y - x).max() <= 0.25 * np.abs(x).max()
+
+
 def test_oracle_q8_0_matches_gguf(oracle):
     from gguf import quants as gq, GGMLQuantizationType as G
     rng = np.random.default_rng(7)

@@ -388,6 +388,7 @@ bool run_chunks(Device & d, HostJob & j, size_t c0, size_t c1) {
         a.tab = t ? *t : SearchTab{};
         a.status = d.status;
         a.stream = d.s_run;
+        a.n_per_row = j.n_per_row;
         if (launch_quantize(j.type, a) != cudaSuccess) { set_err("kernel launch failed: %s", cudaGetErrorString(cudaGetLastError())); ok = false; break; }
         cudaEventRecord(d.ev_run[slot], d.s_run);
         cudaStreamWaitEvent(d.s_d2h, d.ev_run[slot], 0);
@@ -644,7 +645,7 @@ size_t gpuq_requantize_dev(int src, const void * d_raw, int type, void * d_dst, 
     a.src_type = src; a.src = d_raw;
     a.qw = type == Q8_0 ? nullptr : d_imatrix;
     a.qw_mod = nb_row; a.qw_div = 1; a.qw_mat = nrow * nb_row;
-    a.out = d_dst; a.nblocks = n / block_len(type);
+    a.out = d_dst; a.nblocks = n / block_len(type); a.n_per_row = n_per_row;
     const SearchTab * t = d->tab(type);
     a.tab = t ? *t : SearchTab{};
     a.status = d->status; a.stream = (cudaStream_t) stream;

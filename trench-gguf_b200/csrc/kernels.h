@@ -20,12 +20,14 @@ struct LaunchArgs {
     SearchTab tab;
     unsigned * status;
     cudaStream_t stream;
+    int64_t n_per_row;   // the row length (Q4_0 / Q5_0 / Q5_1 with an imatrix scale by a whole row's mean square)
 };
 
 cudaError_t launch_iq_grid(int type, const LaunchArgs & a);   // IQ2_XXS IQ2_XS IQ2_S IQ3_XXS IQ3_S
 cudaError_t launch_iq1(int type, const LaunchArgs & a);       // IQ1_S IQ1_M
 cudaError_t launch_iq4(int type, const LaunchArgs & a);       // IQ4_NL IQ4_XS
 cudaError_t launch_kquant(int type, const LaunchArgs & a);    // Q2_K .. Q6_K, Q8_0
+cudaError_t launch_legacy(int type, const LaunchArgs & a);    // Q4_0 Q5_0 Q5_1 (whole rows: a.n_per_row)
 
 // ggml's to_float of the i-quant types with grids and IQ4_XS: nblocks super-blocks -> nblocks*256 floats
 cudaError_t launch_dequant(int type, const void * q, float * out, int64_t nblocks, DequantTab tab, cudaStream_t st);
@@ -60,8 +62,9 @@ inline bool is_iq_grid(int t) { return t == IQ2_XXS || t == IQ2_XS || t == IQ2_S
 inline bool is_iq1(int t) { return t == IQ1_S || t == IQ1_M; }
 inline bool is_iq4(int t) { return t == IQ4_NL || t == IQ4_XS; }
 inline bool is_kquant(int t) { return t == Q2_K || t == Q3_K || t == Q4_K || t == Q5_K || t == Q6_K || t == Q8_0; }
-// the types ggml also quantizes without an imatrix (k-quants' *_ref path, IQ4 with x^2 weights)
-inline bool takes_no_imatrix(int t) { return is_kquant(t) || is_iq4(t); }
+inline bool is_legacy(int t) { return t == Q4_0 || t == Q5_0 || t == Q5_1; }
+// the types ggml also quantizes without an imatrix (k-quants' and the legacy types' *_ref paths, IQ4 with x^2 weights)
+inline bool takes_no_imatrix(int t) { return is_kquant(t) || is_iq4(t) || is_legacy(t); }
 inline bool needs_search_tab(int t) { return is_iq_grid(t) || is_iq1(t); }
 
 inline cudaError_t launch_quantize(int type, const LaunchArgs & a) {
@@ -69,6 +72,7 @@ inline cudaError_t launch_quantize(int type, const LaunchArgs & a) {
     if (is_iq1(type)) return launch_iq1(type, a);
     if (is_iq4(type)) return launch_iq4(type, a);
     if (is_kquant(type)) return launch_kquant(type, a);
+    if (is_legacy(type)) return launch_legacy(type, a);
     return cudaErrorInvalidValue;
 }
 

@@ -760,6 +760,118 @@ __global__ void __launch_bounds__(256) k_q8_0(const uint8_t * __restrict__ src, 
     }
 }
 
+// Q4_0, Q5_0, Q5_1 (llama-quantize's fallbacks for rows a k-quant or i-quant cannot hold, which the reference leaves to
+// ggml on the CPU, tools/requant_experts.py:181-183). Without an imatrix ggml's quantize_row_q4_0_ref / q5_0_ref /
+// q5_1_ref; with one quantize_row_*_impl: weights qw * sqrt(sigma2 + x^2) with sigma2 the mean square of the WHOLE
+// ROW (a sequential sum in index order), then make_qx_quants (sym_levels: 8 / 16 levels a side) or make_qkx3_quants
+// (affine_levels5: 31 levels, -0.9 + 0.05 k, 37 trials). One CTA a row: lane 0 of warp 0 forms sigma2, then one
+// thread a 32-weight block. (These are rare fallback tensors; the layout favours simplicity.)
+template <int T, int SRC, bool IMAT>
+__global__ void __launch_bounds__(128) k_legacy(const uint8_t * __restrict__ src, const float * __restrict__ qw,
+                                                int64_t qw_mod, int64_t qw_div, int64_t qw_mat,
+                                                uint8_t * __restrict__ out, int64_t n_per_row) {
+    __shared__ float s_sigma2;
+    const int64_t row = blockIdx.x, nb_row = n_per_row / 32;
+    if (IMAT) {
+        if (threadIdx.x == 0) {
+            float s = 0;
+            for (int64_t v = 0; v < n_per_row; v += 8) {
+                float x8[8];
+                decode8<SRC>(src, row * n_per_row + v, x8);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) s += x8[j] * x8[j];
+            }
+            s_sigma2 = s / n_per_row;
+        }
+        __syncthreads();
+    }
+    for (int64_t ib = threadIdx.x; ib < nb_row; ib += blockDim.x) {
+        const int64_t b = row * nb_row + ib;
+        float x[32];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) decode8<SRC>(src, b * 32 + 8 * k, x + 8 * k);
+        uint8_t L[32];
+        float d, m = 0.f;
+        if constexpr (IMAT) {
+            const float * q = qw + ((b / qw_mat) * qw_mod + (b % qw_mod) / qw_div) * 32;
+            const float sigma2 = s_sigma2;
+            float w[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) w[j] = __ldg(q + j) * sqrtf(sigma2 + x[j] * x[j]);
+            if constexpr (T == Q5_1) {
+                float the_min;
+                d = affine_levels5<32, true>(31, x, w, L, &the_min, -0.9f, 0.05f, 36);
+                m = -the_min;
+            } else {
+                d = sym_levels<32>(T == Q4_0 ? 8 : 16, x, L, w);
+            }
+        } else if constexpr (T == Q5_1) {
+            float mn = FLT_MAX, mx = -FLT_MAX;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) { if (x[j] < mn) mn = x[j]; if (x[j] > mx) mx = x[j]; }
+            d = (mx - mn) / 31;
+            const float id = d ? 1.0f / d : 0.0f;
+            m = mn;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) L[j] = (uint8_t) ((x[j] - mn) * id + 0.5f);
+        } else {
+            constexpr int nl = T == Q4_0 ? 8 : 16;
+            float amax = 0.0f, mx = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) if (amax < fabsf(x[j])) { amax = fabsf(x[j]); mx = x[j]; }
+            d = mx / -nl;
+            const float id = d ? 1.0f / d : 0.0f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const int v = (int8_t) (int) (x[j] * id + (nl + 0.5f));
+                L[j] = (uint8_t) (v < 2 * nl - 1 ? v : 2 * nl - 1);
+            }
+        }
+        uint8_t * y = out + b * block_bytes(T);
+        const uint16_t dh = half_bits(d);
+        y[0] = (uint8_t) dh; y[1] = (uint8_t) (dh >> 8);
+        int o = 2;
+        if constexpr (T == Q5_1) { const uint16_t mh = half_bits(m); y[2] = (uint8_t) mh; y[3] = (uint8_t) (mh >> 8); o = 4; }
+        if constexpr (T != Q4_0) {
+            uint32_t h = 0;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) h |= ((uint32_t) ((L[j] >> 4) & 1) << j) | ((uint32_t) ((L[j + 16] >> 4) & 1) << (j + 16));
+#pragma unroll
+            for (int k = 0; k < 4; ++k) y[o + k] = (uint8_t) (h >> (8 * k));
+            o += 4;
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) y[o + j] = (uint8_t) ((L[j] & 15) | ((L[j + 16] & 15) << 4));
+    }
+}
+
+template <int T, int SRC>
+cudaError_t launch_legacy_t(const LaunchArgs & a) {
+    const int64_t nb_row = a.n_per_row / 32;
+    if (a.n_per_row <= 0 || a.n_per_row % 32 || a.nblocks % nb_row) return cudaErrorInvalidValue;
+    const int64_t rows = a.nblocks / nb_row;
+    if (rows > 0x7FFFFFFF) return cudaErrorInvalidValue;
+    if (a.qw)
+        k_legacy<T, SRC, true><<<(unsigned) rows, 128, 0, a.stream>>>((const uint8_t *) a.src, a.qw, a.qw_mod, a.qw_div,
+                                                                      a.qw_mat, (uint8_t *) a.out, a.n_per_row);
+    else
+        k_legacy<T, SRC, false><<<(unsigned) rows, 128, 0, a.stream>>>((const uint8_t *) a.src, nullptr, 1, 1, 1,
+                                                                       (uint8_t *) a.out, a.n_per_row);
+    return cudaGetLastError();
+}
+
+template <int T>
+cudaError_t launch_legacy_src(const LaunchArgs & a) {
+    switch (a.src_type) {
+        case SRC_F32:   return launch_legacy_t<T, SRC_F32>(a);
+        case SRC_F16:   return launch_legacy_t<T, SRC_F16>(a);
+        case SRC_BF16:  return launch_legacy_t<T, SRC_BF16>(a);
+        case SRC_Q8_0:  return launch_legacy_t<T, SRC_Q8_0>(a);
+        case SRC_MXFP4: return launch_legacy_t<T, SRC_MXFP4>(a);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
 template <int T, int SRC>
 cudaError_t launch_t(const LaunchArgs & a) {
     if constexpr (T == Q8_0) {
@@ -808,6 +920,15 @@ cudaError_t launch_kquant(int type, const LaunchArgs & a) {
         case Q5_K: return launch_src<Q5_K>(a);
         case Q6_K: return launch_src<Q6_K>(a);
         case Q8_0: return launch_src<Q8_0>(a);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_legacy(int type, const LaunchArgs & a) {
+    switch (type) {
+        case Q4_0: return launch_legacy_src<Q4_0>(a);
+        case Q5_0: return launch_legacy_src<Q5_0>(a);
+        case Q5_1: return launch_legacy_src<Q5_1>(a);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -139,6 +139,7 @@ extern "C" size_t gpuq_requantize_noalloc(int src, const void * raw, int type, v
     a.tab = tab ? *tab : SearchTab{};
     a.status = status;
     a.stream = 0;
+    a.n_per_row = n_per_row;
     if (launch_quantize(type, a) != cudaSuccess) { set_last_error("gpuq_requantize_noalloc: kernel launch failed"); return 0; }
     unsigned st = 0;
     if (cudaMemcpy(dst, d_out, out_bytes, cudaMemcpyDeviceToHost) != cudaSuccess ||
