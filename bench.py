@@ -844,8 +844,13 @@ def main():
     if opw and peak:
         ach = opw * E * ROWS * COLS / (per_type_ms[top] / 1e3) / 1e12
         tb = traffic.get(top.upper(), {}).get("dram_bytes_per_weight")
+        apw = ops.get(okey, {}).get("arith_per_weight")
         roof = {"bound": "fp32", "kernel": top, "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
                 "peak_source": peak_src, "ops_per_weight": opw,
+                "arith_per_weight": apw, "compares_per_weight": ops.get(okey, {}).get("compares_per_weight"),
+                "frac_arith_only": (apw * E * ROWS * COLS / (per_type_ms[top] / 1e3) / 1e12) / peak if apw else None,
+                "counting": "achieved counts float arithmetic and comparisons (oracle/opcount.hpp); frac_arith_only "
+                            "counts only the FADD/FMUL-class operations the peak measures",
                 "traffic": tb * E * ROWS * COLS if tb else None, "traffic_unit": "bytes a launch (ncu DRAM read+write, "
                 "scaled from a 20-expert capture by the weights a launch)", "algorithmic_bytes": E * ROWS * COLS * (17 / 32 + block_b[top] / gpuq.BLOCK_LEN[TYPES[top]])}
     cb = parity = ref_gpu = None

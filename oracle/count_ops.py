@@ -2,9 +2,12 @@
 
 Runs the C restatement compiled with a counting float type (oracle/opcount.hpp; `make -C oracle ops`) on samples
 drawn like the benchmark configurations (trench-gguf_b200/workloads.py) and writes
-trench-gguf_b200/op_counts.json: for each type and mode, float adds, subtracts, multiplies, divides, square roots
-and comparisons per weight (sign flips, fabs and int<->float conversions are not counted). The counts are data
-dependent (neighbour-list lengths, on-grid rates, accepted trials), hence the per-config samples.
+trench-gguf_b200/op_counts.json: for each type and mode, per weight, the float arithmetic (adds, subtracts,
+multiplies, divides, square roots, rounds: `arith_per_weight`), the float comparisons (`compares_per_weight`) and
+their sum (`ops_per_weight`; sign flips, fabs and int<->float conversions are not counted). The FP32 roofline's
+denominator (trench-gguf_b200/peak.cu) measures the FADD/FMUL issue rate, so its fraction is given both on the sum
+and on the arithmetic alone. The counts are data dependent (neighbour-list lengths, on-grid rates, accepted trials),
+hence the per-config samples.
 usage: python oracle/count_ops.py
 """
 import ctypes
@@ -27,8 +30,9 @@ def main():
     if not os.path.exists(ops_lib):
         os.system("make -s -C %s ops" % HERE)
     L = ctypes.CDLL(ops_lib)
-    L.orc_fops.restype = ctypes.c_ulonglong
-    L.orc_fops.argtypes = [ctypes.c_int]
+    for f in (L.orc_fops, L.orc_fcmps):
+        f.restype = ctypes.c_ulonglong
+        f.argtypes = [ctypes.c_int]
     orc.LIBS["ops"] = (ops_lib, "orc_")
     tables = os.path.join(ROOT, "trench-gguf_b200", "gpuq_tables.bin")
     c = orc.Checker("ops", tables)
@@ -36,10 +40,13 @@ def main():
 
     def count(name, t, x, im, sample):
         L.orc_fops(1)
+        L.orc_fcmps(1)
         c.quantize(t, x, im, threads=1)
-        n = L.orc_fops(1)
-        out[name] = {"ops_per_weight": n / x.size, "sample": sample}
-        print("%-14s %8.1f FP32 ops / weight   (%s)" % (name, n / x.size, sample), flush=True)
+        a, k = L.orc_fops(1), L.orc_fcmps(1)
+        out[name] = {"ops_per_weight": (a + k) / x.size, "arith_per_weight": a / x.size,
+                     "compares_per_weight": k / x.size, "sample": sample}
+        print("%-14s %8.1f FP32 ops / weight = %8.1f arithmetic + %8.1f comparisons  (%s)" % (
+            name, (a + k) / x.size, a / x.size, k / x.size, sample), flush=True)
 
     raw, im = workloads.config2(experts=1, rows=64, cols=7168, seed=102)
     x2 = c.decode(39, raw, 64 * 7168).reshape(1, 64, 7168)

@@ -1651,6 +1651,7 @@ size_t orc_decode(int src, const void * raw, float * out, int64_t n) {
 #endif
 
 #ifdef ORACLE_COUNT_OPS
-thread_local unsigned long long g_fops = 0;
+thread_local unsigned long long g_fops = 0, g_fcmp = 0;
 extern "C" unsigned long long orc_fops(int reset) { const unsigned long long v = g_fops; if (reset) g_fops = 0; return v; }
+extern "C" unsigned long long orc_fcmps(int reset) { const unsigned long long v = g_fcmp; if (reset) g_fcmp = 0; return v; }
 #endif
