@@ -65,6 +65,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true", help="leave out the reference GPU library's leg")
+    ap.add_argument("--only", default=None,
+                    help="--config 1/3/4: measure only the jobs of these types (comma list, e.g. Q8_0): profiling runs")
     ap.add_argument("--gate", action="store_true",
                     help="the 384-expert IQ2_XXS tensor, host to host, one process over every visible GPU")
     ap.add_argument("--ldlq-streams", type=int, default=4,
@@ -355,6 +357,9 @@ def run_config(args):
         jobs.append(("Q8_0", 30, raw, None, shape, "Q8_0"))
         sample = {name: ("rows", 64) for name, *_ in jobs}
         workload = "config 4: BF16 8192 x 28672 -> Q2_K..Q6_K with and without imatrix, Q8_0"
+    if args.only:
+        keep = {t.strip().upper() for t in args.only.split(",")}
+        jobs = [j for j in jobs if j[0].split()[0].split("+")[0] in keep]
     results = {}
     kept = []
     total_w = 0

@@ -134,6 +134,11 @@ size_t gpuq_ldlq_scale_dev(const double * d_err, const double * d_rd, double * d
 size_t gpuq_ldlq_update_dev(const double * d_es, const double * d_u, float * d_w, int64_t ngroups, int64_t rows,
                             int64_t ne0, int64_t k, void * stream);
 
+/* A diagnostic with no counterpart in the reference: how many floats x with |x| < 2^22 round differently in the Q8_0
+ * kernels (which form ggml's roundf as trunc(x + copysign(0.5 - 2^-25, x))) than in CUDA's roundf: 0 expected; -1 if
+ * the check could not run. Synchronous, on the current device. */
+int64_t gpuq_check_q8_rounding(void);
+
 /* Scratch size of gpuq_requantize_noalloc, held on every GPU that gpuq_init prepares, from gpuq_init to exit. */
 #define GPUQ_NOALLOC_SCRATCH_BYTES ((size_t) 64 << 20)
 

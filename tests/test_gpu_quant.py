@@ -163,6 +163,27 @@ def test_legacy_fallback_types(gpuq, oracle, monkeypatch, name):
     assert np.array_equal(gpuq.requantize(39, raw4, t, (2, 16, 7168), None), oracle.quantize(t, x4, None))
 
 
+def test_q8_0_rounding_equals_roundf(gpuq):
+    """the Q8_0 kernels' own form of ggml's roundf equals CUDA's roundf on every float below 2^22 in magnitude"""
+    assert gpuq.lib.gpuq_check_q8_rounding() == 0
+
+
+def test_q8_0_nonfinite_blocks_match_the_oracle(gpuq, oracle):
+    """Q8_0 blocks holding NaN or infinities of both signs take the exact fold of ggml's amax: the block scale equals
+    the oracle's (the int8 values of a NaN product are the platform's conversion and are not compared)"""
+    rng = np.random.default_rng(71)
+    x = (rng.standard_normal((8, 512)) * 0.02).astype(np.float32)
+    x[0, 5] = np.nan
+    x[1, 31] = np.nan
+    x[2, 3], x[2, 9] = np.inf, -np.inf
+    x[3, 0] = np.nan
+    x[3, 1] = 0.9
+    got, want = gpuq.quantize(8, x).reshape(-1, 34), oracle.quantize(8, x).reshape(-1, 34)
+    assert np.array_equal(got[:, :2], want[:, :2])
+    finite = np.isfinite(x.reshape(-1, 32)).all(1)
+    assert np.array_equal(got[finite], want[finite])
+
+
 def test_chunked_pipeline_matches_one_chunk(gpuq, oracle, monkeypatch):
     """many pipeline chunks (whole matrices and row ranges of one matrix) == the oracle"""
     raw, im = workloads.config3(experts=3, rows=16, cols=7168, seed=5)

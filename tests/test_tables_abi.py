@@ -65,7 +65,7 @@ def test_search_map_and_neighbours(records, t):
 
 def header_symbols():
     text = open(HEADER).read()
-    return re.findall(r"^\s*(?:const\s+)?[a-z_0-9]+\s*\**\s*(gpuq_[a-z_]+)\s*\(", text, re.M)
+    return re.findall(r"^\s*(?:const\s+)?[a-z_0-9]+\s*\**\s*(gpuq_[a-z_0-9]+)\s*\(", text, re.M)
 
 
 def test_library_exports_every_declared_symbol():

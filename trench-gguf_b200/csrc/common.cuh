@@ -55,7 +55,7 @@ __host__ __device__ constexpr int src_block_bytes(int s) {
 // Conditions ggml would reach only through impossible states (no finite candidate in a neighbour search, a final
 // code off the grid) are reported, never trapped: the kernel records the reason in the per-device status word,
 // skips the block, and the host API turns the word into a 0 return.
-enum Status : unsigned { ST_OK = 0, ST_NO_NEIGHBOUR = 1u, ST_OFF_GRID = 2u, ST_BAD_INPUT = 4u };
+enum Status : unsigned { ST_OK = 0, ST_NO_NEIGHBOUR = 1u, ST_OFF_GRID = 2u, ST_BAD_INPUT = 4u, ST_TIMEOUT = 8u };
 
 // ---------------------------------------------------------------------------------------------- search tables
 // Device layout of one codebook (built on the host from a gpuq_tables.bin record):

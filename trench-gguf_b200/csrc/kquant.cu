@@ -724,48 +724,64 @@ __global__ void __launch_bounds__(128, kquant_min_ctas<T, IMAT>()) k_kquant(cons
     }
 }
 
-// Q8_0: amax / 127 and roundf (gpuq.hip:1831-1838); HBM-bound. 8 weights a lane, 4 lanes a block.
-template <int SRC>
-__global__ void __launch_bounds__(256) k_q8_0(const uint8_t * __restrict__ src, uint8_t * __restrict__ out, int64_t nblocks) {
-    const int64_t nthreads = (int64_t) gridDim.x * blockDim.x, total = nblocks * 4;
-    const int lane = threadIdx.x & 31;
-    // whole warps iterate together (the 4-lane shuffles below need every lane of the warp)
-    for (int64_t base = (int64_t) blockIdx.x * blockDim.x + (threadIdx.x & ~31); base < total; base += nthreads) {
-        const int64_t t = base + lane;
-        const bool active = t < total;
-        const int64_t b = t >> 2;
-        const int part = (int) (t & 3);
-        float v[8];
-        if (active) decode8<SRC>(src, b * 32 + part * 8, v);
-        else for (int j = 0; j < 8; ++j) v[j] = 0.f;
-        float amax = 0.0f;
+// Q8_0 (gpuq.hip:1831-1838): d = amax / 127, the values roundf(x * (1 / d)) as int8. One thread a 32-weight block.
+//
+// ggml's roundf (half away from zero) is formed as trunc(x + copysign(0.5 - 2^-25, x)) in float32, which equals it
+// for every finite |x| < 2^22 (here |x| <= 127 up to rounding): for x >= 0.5 the sum of x and a number just below 0.5
+// crosses the integer above x exactly when x >= k + 0.5 (the sum's rounding error, at most half an ulp of the result,
+// cannot reach the next integer from below k + 0.5, and an exact tie k + 0.5 rounds up to k + 1), and for
+// x < 0.5 - 2^-25 ... 0.5 it stays below 1 - the case where x + 0.5 would round up to 1.0 (x = 0.5 - 2^-25) is the
+// reason for the smaller addend. Non-finite x give what the conversion gives for roundf's result (NaN 0, inf
+// saturated). The equality is checked against CUDA's roundf over every float below 2^22 by a GPU test.
+__device__ __forceinline__ int round_half_away(float x) {
+    return __float2int_rz(x + copysignf(0.49999997f, x));
+}
+
+// one block: v[32] -> 34 bytes at y (any address space; 2-byte aligned). ggml's amax is a sequential fold,
+// amax = MAX(amax, fabsf(x)) with MAX(a, b) = a > b ? a : b, from 0; for a block without NaN that is the maximum of the
+// |x| (an fmax reduction); a NaN changes the fold (a NaN operand makes it NaN, the next value replaces it), so a block
+// whose sum of values is NaN (any NaN, or infinities of both signs) folds again in ggml's order.
+__device__ __forceinline__ void q8_0_block(const float * v, uint8_t * y) {
+    // (both reductions as trees: fmaxf is associative, and the sum is NaN in any order exactly when a NaN, or
+    // infinities of both signs, are present)
+    float m[16], c[16];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) amax = fmaxr(amax, fabsf(v[j]));
-        // (max is exact; the 4-lane combine gives ggml's amax for non-NaN input)
-        amax = fmaxr(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-        amax = fmaxr(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-        if (!active) continue;
-        const float d = amax / 127;
-        const float id = d ? 1.0f / d : 0.0f;
-        uint8_t * y = out + b * 34;
-        uint32_t q[2] = {0, 0};
+    for (int j = 0; j < 16; ++j) { m[j] = fmaxf(fabsf(v[j]), fabsf(v[j + 16])); c[j] = v[j] + v[j + 16]; }
 #pragma unroll
-        for (int j = 0; j < 8; ++j) q[j / 4] |= (uint32_t) (uint8_t) (int8_t) roundf(v[j] * id) << (8 * (j % 4));
-        uint16_t * y16 = reinterpret_cast<uint16_t *>(y);   // block offsets are even: 2-byte stores
-        if (part == 0) y16[0] = half_bits(d);
-        y16[1 + part * 4 + 0] = (uint16_t) (q[0] & 0xFFFF);
-        y16[1 + part * 4 + 1] = (uint16_t) (q[0] >> 16);
-        y16[1 + part * 4 + 2] = (uint16_t) (q[1] & 0xFFFF);
-        y16[1 + part * 4 + 3] = (uint16_t) (q[1] >> 16);
+    for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+        for (int j = 0; j < w; ++j) { m[j] = fmaxf(m[j], m[j + w]); c[j] = c[j] + c[j + w]; }
+    float amax = fmaxf(0.0f, m[0]);
+    const float chk = c[0];
+    if (chk != chk) {
+        amax = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) { const float a = fabsf(v[j]); amax = amax > a ? amax : a; }
+    }
+    const float d = amax / 127;
+    const float id = d ? 1.0f / d : 0.0f;
+    uint16_t * y16 = reinterpret_cast<uint16_t *>(y);
+    y16[0] = half_bits(d);
+#pragma unroll
+    for (int j = 0; j < 32; j += 2) {
+        const uint32_t lo = (uint8_t) round_half_away(v[j] * id), hi = (uint8_t) round_half_away(v[j + 1] * id);
+        y16[1 + j / 2] = (uint16_t) (lo | (hi << 8));
     }
 }
 
-// Q4_0, Q5_0, Q5_1 (llama-quantize's fallbacks for rows a k-quant or i-quant cannot hold, which the reference leaves to
-// ggml on the CPU, tools/requant_experts.py:181-183). Without an imatrix ggml's quantize_row_q4_0_ref / q5_0_ref /
-// q5_1_ref; with one quantize_row_*_impl: weights qw * sqrt(sigma2 + x^2) with sigma2 the mean square of the WHOLE
-// ROW (a sequential sum in index order), then make_qx_quants (sym_levels: 8 / 16 levels a side) or make_qkx3_quants
-// (affine_levels5: 31 levels, -0.9 + 0.05 k, 37 trials). One CTA a row: lane 0 of warp 0 forms sigma2, then one
-// thread a 32-weight block. (These are rare fallback tensors; the layout favours simplicity.)
+// the plain form (global loads and stores): blocks after the last whole tile of the bulk kernel, or every block of a
+// buffer that a bulk copy cannot address
+template <int SRC>
+__global__ void __launch_bounds__(256) k_q8_0(const uint8_t * __restrict__ src, uint8_t * __restrict__ out, int64_t nblocks) {
+    const int64_t stride = (int64_t) gridDim.x * blockDim.x;
+    for (int64_t b = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; b < nblocks; b += stride) {
+        float v[32];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) decode8<SRC>(src, b * 32 + 8 * k, v + 8 * k);
+        q8_0_block(v, out + b * 34);
+    }
+}
+
 template <int T, int SRC, bool IMAT>
 __global__ void __launch_bounds__(128) k_legacy(const uint8_t * __restrict__ src, const float * __restrict__ qw,
                                                 int64_t qw_mod, int64_t qw_div, int64_t qw_mat,
@@ -872,15 +888,121 @@ cudaError_t launch_legacy_src(const LaunchArgs & a) {
     }
 }
 
+// Q8_0 on whole tiles of 256 blocks, the bytes moved by the Blackwell copy engine: a persistent CTA keeps three
+// source tiles in flight with 1-D TMA bulk loads (cp.async.bulk, completion counted on an mbarrier a stage), its 256
+// threads quantize a tile from shared memory (one thread a block, q8_0_block) into a shared-memory copy of the 8,704
+// output bytes, and one thread writes them back with a TMA bulk store. Every wait is bounded: a wait that runs out
+// sets ST_TIMEOUT in the status word and the CTA drains its own copies (again with bounds) and returns.
+constexpr int Q8T = 256, Q8STAGES = 2, Q8OUT = Q8T * 34;
+constexpr unsigned Q8_SPIN = 1u << 22;   // try_wait rounds before a wait is declared lost
+
+__device__ __forceinline__ uint32_t smem_u32(const void * p) { return (uint32_t) __cvta_generic_to_shared(p); }
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t phase) {
+    uint32_t done;
+    asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(done) : "r"(bar), "r"(phase) : "memory");
+    return done != 0;
+}
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t phase) {
+    for (unsigned it = 0; it < Q8_SPIN; ++it) if (mbar_try(bar, phase)) return true;
+    return false;
+}
+
+template <int SRC>
+__global__ void __launch_bounds__(256) k_q8_0_bulk(const uint8_t * __restrict__ src, uint8_t * __restrict__ out,
+                                                   int64_t ntiles, unsigned * status) {
+    constexpr int IN = Q8T * src_bytes32(SRC);
+    extern __shared__ __align__(128) unsigned char q8s[];
+    uint8_t * inb = q8s;                          // Q8STAGES x IN
+    uint8_t * ob = q8s + Q8STAGES * IN;           // 2 x Q8OUT
+    __shared__ __align__(8) uint64_t full[Q8STAGES];
+    __shared__ int s_fail;
+    const int tid = threadIdx.x;
+    const int64_t first = blockIdx.x, stride = gridDim.x;
+    const int64_t count = first < ntiles ? (ntiles - 1 - first) / stride + 1 : 0;
+    if (tid == 0) {
+        s_fail = 0;
+        for (int st = 0; st < Q8STAGES; ++st) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&full[st])) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    auto issue = [&](int st, int64_t tile) {      // (thread 0) the tile's source bytes into stage st
+        const uint32_t bar = smem_u32(&full[st]);
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(IN) : "memory");
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                     ::"r"(smem_u32(inb + st * IN)), "l"(src + tile * IN), "r"(IN), "r"(bar) : "memory");
+    };
+    if (tid == 0)
+        for (int st = 0; st < Q8STAGES && st < count; ++st) issue(st, first + st * stride);
+    int64_t i = 0;
+    for (; i < count; ++i) {
+        const int st = (int) (i % Q8STAGES);
+        const uint32_t phase = (uint32_t) ((i / Q8STAGES) & 1);
+        if (tid == 0 && i >= 2) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");   // out buffer i&1 free
+        if (!mbar_wait_bounded(smem_u32(&full[st]), phase)) atomicOr(&s_fail, 1);
+        __syncthreads();
+        if (s_fail) break;
+        const uint8_t * tin = inb + st * IN;
+        uint8_t * tout = ob + (i & 1) * Q8OUT;
+        {
+            float v[32];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) decode8<SRC, false>(tin, (int64_t) tid * 32 + 8 * k, v + 8 * k);
+            q8_0_block(v, tout + tid * 34);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the staged bytes visible to the bulk store
+        __syncthreads();                                                // stage st read, out buffer written
+        if (tid == 0) {
+            const int64_t tile = first + i * stride;
+            asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
+                         ::"l"(out + tile * Q8OUT), "r"(smem_u32(tout)), "r"(Q8OUT) : "memory");
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+            if (i + Q8STAGES < count) issue(st, first + (i + Q8STAGES) * stride);
+        }
+    }
+    if (tid == 0) {
+        if (s_fail) {   // a wait ran out: report it, let the loads still in flight land (bounded) and return
+            atomicOr(status, ST_TIMEOUT);
+            for (int64_t k = i; k < count && k < i + Q8STAGES; ++k)
+                mbar_wait_bounded(smem_u32(&full[k % Q8STAGES]), (uint32_t) ((k / Q8STAGES) & 1));
+        }
+        asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");     // every store of this CTA complete
+    }
+}
+
+template <int SRC>
+size_t q8_bulk_smem() { return (size_t) Q8STAGES * Q8T * src_bytes32(SRC) + 2 * Q8OUT; }
+
 template <int T, int SRC>
 cudaError_t launch_t(const LaunchArgs & a) {
     if constexpr (T == Q8_0) {
+        const int64_t ntiles = a.nblocks / Q8T;
+        const bool aligned = ((reinterpret_cast<uintptr_t>(a.src) | reinterpret_cast<uintptr_t>(a.out)) & 15) == 0;
+        int64_t done = 0;
+        if (aligned && ntiles > 0 && a.status) {
+            int dev = 0, sms = 148, per_sm = 0;
+            cudaGetDevice(&dev);
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+            const size_t smem = q8_bulk_smem<SRC>();
+            cudaError_t e = cudaFuncSetAttribute(k_q8_0_bulk<SRC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+            if (e != cudaSuccess) return e;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_q8_0_bulk<SRC>, 256, smem) != cudaSuccess || per_sm < 1) per_sm = 1;
+            const int64_t grid = ntiles < (int64_t) sms * per_sm ? ntiles : (int64_t) sms * per_sm;
+            k_q8_0_bulk<SRC><<<(unsigned) grid, 256, smem, a.stream>>>((const uint8_t *) a.src, (uint8_t *) a.out, ntiles,
+                                                                       a.status);
+            if ((e = cudaGetLastError()) != cudaSuccess) return e;
+            done = ntiles * Q8T;
+        }
+        if (done == a.nblocks) return cudaSuccess;
+        // the blocks after the last whole tile (or every block, for buffers a bulk copy cannot address)
         int dev = 0, sms = 148;
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        const int64_t need = (a.nblocks * 4 + 255) / 256;
-        const int grid = (int) (need < (int64_t) sms * 32 ? (need > 0 ? need : 1) : (int64_t) sms * 32);
-        k_q8_0<SRC><<<grid, 256, 0, a.stream>>>((const uint8_t *) a.src, (uint8_t *) a.out, a.nblocks);
+        const int64_t rest = a.nblocks - done;
+        const int64_t need = (rest + 255) / 256;
+        const int grid = (int) (need < (int64_t) sms * 8 ? (need > 0 ? need : 1) : (int64_t) sms * 8);
+        k_q8_0<SRC><<<grid, 256, 0, a.stream>>>((const uint8_t *) a.src + (size_t) done * src_bytes32(SRC),
+                                               (uint8_t *) a.out + (size_t) done * 34, rest);
         return cudaGetLastError();
     } else {
         constexpr int WARPS = 4;
@@ -908,6 +1030,18 @@ cudaError_t launch_src(const LaunchArgs & a) {
         case SRC_MXFP4: return launch_t<T, SRC_MXFP4>(a);
         default: return cudaErrorInvalidValue;
     }
+}
+
+// every float x with 0 <= x < 2^22 (bit patterns 0 .. 0x4A7FFFFF), and -x: round_half_away(x) against CUDA's roundf
+__global__ void k_check_round(uint32_t n, unsigned long long * bad) {
+    const uint32_t stride = gridDim.x * blockDim.x;
+    unsigned long long local = 0;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const float x = __uint_as_float(i);
+        local += round_half_away(x) != (int) roundf(x);
+        local += round_half_away(-x) != (int) roundf(-x);
+    }
+    if (local) atomicAdd(bad, local);
 }
 
 }  // namespace
@@ -942,3 +1076,16 @@ cudaError_t launch_iq4(int type, const LaunchArgs & a) {
 }
 
 }  // namespace gq
+
+// A diagnostic (no counterpart in the reference): the number of floats below 2^22 in magnitude for which the Q8_0
+// kernels' rounding differs from CUDA's roundf (0 expected), -1 when the check could not run. Synchronous, current
+// device; allocates 8 bytes of device memory for the count.
+extern "C" int64_t gpuq_check_q8_rounding(void) {
+    unsigned long long * d = nullptr, h = 0;
+    if (cudaMalloc(&d, sizeof(h)) != cudaSuccess) { cudaGetLastError(); return -1; }
+    cudaMemset(d, 0, sizeof(h));
+    gq::k_check_round<<<148 * 8, 256>>>(0x4A800000u, d);
+    const bool ok = cudaGetLastError() == cudaSuccess && cudaMemcpy(&h, d, sizeof(h), cudaMemcpyDeviceToHost) == cudaSuccess;
+    cudaFree(d);
+    return ok ? (int64_t) h : -1;
+}
