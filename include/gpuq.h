@@ -119,20 +119,34 @@ size_t gpuq_requantize_dev(int src, const void * d_raw, int type, void * d_dst, 
 size_t gpuq_dequantize_error_dev(int type, const void * d_q, const float * d_blk, void * d_err, int f64, int64_t nblocks,
                                  void * stream);
 
-/* LDLQ's error feedback of column block k on the device, in two calls (no counterpart as calls in the reference: they
- * are tools/ldlq.py:428-429, `Es = E U_kk^-1; Wp[:, :, c1:] -= (Es @ U[c0:c1, c1:]).to(float32)`, as this library's
- * own float64 tensor-core kernels, every group in one launch). A group is the matrices that share one Hessian factor
- * (an expert's gate and up, or one matrix), `rows` their rows together.
- * gpuq_ldlq_scale_dev:  Es = E Rd[k], float64 (Rd: the inverses U_kk^-1 of U's 256 x 256 diagonal blocks)
- *   d_err, d_es: float64 [ngroups][rows][256]; d_rd: float64 [ngroups][nblk][256][256]. Returns the bytes of d_es.
- * gpuq_ldlq_update_dev: for every column c >= (k+1)*256: W[c] = f32(W[c] - f32(sum_i Es[i] * U[k*256 + i][c]))
+/* LDLQ's error feedback on the device, in two calls (no counterpart as calls in the reference: they are
+ * tools/ldlq.py:428-429, `Es = E U_BB^-1; Wp[:, :, c1:] -= (Es @ U[c0:c1, c1:]).to(float32)`, as this library's own
+ * float64 tensor-core kernels, every group in one launch), for a feedback block of kdim columns (256: a super-block;
+ * 32 or 8: the IQ2_XXS sub-block variant, tools/ldlq.py:262-266), block `step` = columns [step*kdim, (step+1)*kdim).
+ * A group is the matrices that share one Hessian factor (an expert's gate and up, or one matrix), `rows` their rows.
+ * gpuq_ldlq_scale_dev:  Es = E Rd[step], float64 (Rd: the inverses of U's kdim x kdim diagonal blocks)
+ *   d_err, d_es: float64 [ngroups][rows][kdim]; d_rd: float64 [ngroups][nsteps][kdim][kdim]. Returns bytes of d_es.
+ * gpuq_ldlq_update_dev: for every column c >= (step+1)*kdim: W[c] = f32(W[c] - f32(sum_i Es[i] * U[step*kdim+i][c]))
  *   (float64 sum, float32 cast and subtraction); d_w: float32 [ne0/256][ngroups][rows][256] (column-block major),
  *   d_u: float64 [ngroups][ne0][ne0]. Returns the bytes of d_w updated.
  * Float64 arrays 16-byte aligned; on `stream`, no synchronisation; 0 on a bad argument. */
 size_t gpuq_ldlq_scale_dev(const double * d_err, const double * d_rd, double * d_es, int64_t ngroups, int64_t rows,
-                           int64_t nblk, int64_t k, void * stream);
+                           int64_t nsteps, int64_t kdim, int64_t step, void * stream);
 size_t gpuq_ldlq_update_dev(const double * d_es, const double * d_u, float * d_w, int64_t ngroups, int64_t rows,
-                            int64_t ne0, int64_t k, void * stream);
+                            int64_t ne0, int64_t kdim, int64_t step, void * stream);
+
+/* The IQ2_XXS sub-block variant's two kernels (tools/ldlq.py:117-272, which the reference runs on the CPU; no
+ * counterpart in its library). gpuq_ldlq_sub_weff_dev: for a super-block's rows d_blk [rows][256] (float32), the
+ * weights d_weff = qw * sqrt(sigma2 + x^2), sigma2 = (numpy's float32 sum of x^2 over the row) / 256, row r taking the
+ * 256 importance values of row r / qw_div of d_qw. gpuq_ldlq_sub_points_dev: with d (and, for sub 8, the sub-block
+ * scales) from ggml's IQ2_XXS bytes d_q [rows][66], the groups of columns [c0, c0 + sub) choose their points again
+ * over the whole grid (sub 32 also tries the sub-block scale +-scale_search); the group fields of d_q are rewritten
+ * and d_err [rows][sub] (float64) receives x - q for the feedback. On `stream`, no synchronisation; 0 on a bad
+ * argument. */
+size_t gpuq_ldlq_sub_weff_dev(const float * d_blk, const float * d_qw, int64_t qw_div, float * d_weff, int64_t rows,
+                              void * stream);
+size_t gpuq_ldlq_sub_points_dev(const float * d_blk, const float * d_weff, void * d_q, double * d_err, int64_t rows, int sub,
+                                int c0, int scale_search, void * stream);
 
 /* A diagnostic with no counterpart in the reference: how many floats x with |x| < 2^22 round differently in the Q8_0
  * kernels (which form ggml's roundf as trunc(x + copysign(0.5 - 2^-25, x))) than in CUDA's roundf: 0 expected; -1 if

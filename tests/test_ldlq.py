@@ -39,6 +39,30 @@ def test_oracle_ldlq_matches_reference_loop(oracle, golden, name):
     assert LO.proxy_loss(W, deq_f, H, n) < LO.proxy_loss(W, deq_p, H, n)   # feedback helps
 
 
+@pytest.mark.parametrize("key,sub,ss,order", [("sub32", 32, 0, "seq"), ("sub8", 8, 0, "seq"), ("sub32_ss1", 32, 1, "seq"),
+                                              ("sub32_act", 32, 0, "act")])
+def test_oracle_iq2xxs_sub_matches_reference(oracle, golden, key, sub, ss, order):
+    """the IQ2_XXS sub-block variant (tools/ldlq.py:117-272): the restatement's bytes and proxy loss equal the
+    reference's own function's (golden file), for feedback every 32 and every 8 columns, a scale search, act order"""
+    g = golden
+    W, H, n, im = g["W"], g["H"], int(g["n"]), g["imatrix"]
+    quant, _, _ = LO.checker_quant(oracle, orc.TYPES["IQ2_XXS"])
+    U, perm, _, _ = LO.prepare_hessian(H, n, damp=0.01, order=order)
+    got, deq = LO.quantize_matrix_iq2xxs_sub(W, quant, LO.iq2xxs_grid(oracle), U, perm, im, sub=sub, scale_search=ss)
+    assert np.array_equal(got, g["IQ2_XXS_%s" % key])
+    assert LO.proxy_loss(W, deq, H, n) == float(g["IQ2_XXS_%s_loss" % key])
+
+
+def test_pairwise_sum_restatement_is_numpys():
+    """the restated float32 row sum equals numpy's own (sum over a contiguous last axis) bit for bit: the sub-block
+    variant's sigma2 and its GPU kernel follow it"""
+    rng = np.random.default_rng(4)
+    for n in (256, 128, 32, 7, 300):
+        a = (rng.standard_t(3, (64, n)) * 0.02).astype(np.float32)
+        a = a * a
+        assert np.array_equal(LO.pairwise_sum_f32(a).view(np.uint32), a.sum(1).view(np.uint32)), n
+
+
 def test_prepare_hessian_dead_columns_and_act_order():
     H, _ = LO.synthetic_hessian(512, 1024, seed=3)
     H[7, :] = 0
@@ -163,41 +187,144 @@ def test_gpu_ldlq_batch_and_larger_case(tables, oracle):
 
 
 @pytest.mark.gpu
-def test_gpu_feedback_kernels_against_torch(tables):
+@pytest.mark.parametrize("kd", [256, 32, 8])
+def test_gpu_feedback_kernels_against_torch(tables, kd):
     """gpuq_ldlq_scale_dev (Es = E U_kk^-1 as E R_kk) and gpuq_ldlq_update_dev (W -= f32(Es U_k,rest)) on random data
-    of two groups: Es equals torch's float64 product to rounding, and W equals torch's float32 subtraction of the
-    float32-cast product except where the float64 sums of the two differ in their last bits right at a float32
-    rounding boundary (at most 1 ulp, on a tiny share of the weights)"""
+    of two groups, for feedback blocks of 256 columns and the sub-block variant's 32 and 8: Es equals torch's float64
+    product to rounding, and W equals torch's float32 subtraction of the float32-cast product except where the
+    float64 sums of the two differ in their last bits right at a float32 rounding boundary (at most 1 ulp, on a tiny
+    share of the weights)"""
     torch, G, ldlq_gpu, g = _gpu_setup(tables)
     dev = torch.device("cuda")
     gen = torch.Generator(device=dev).manual_seed(3)
-    P, M, ne0, nblk = 2, 192, 1024, 4                      # (192 rows: a partial 128-row tile)
-    E = torch.randn(P, M, 256, dtype=torch.float64, device=dev, generator=gen) * 1e-3
+    P, M, ne0 = 2, 192, 1024                               # (192 rows: a partial 128-row tile)
+    nsteps = ne0 // kd
+    E = torch.randn(P, M, kd, dtype=torch.float64, device=dev, generator=gen) * 1e-3
     U = torch.triu(torch.randn(P, ne0, ne0, dtype=torch.float64, device=dev, generator=gen))
-    Rd = torch.randn(P, nblk, 256, 256, dtype=torch.float64, device=dev, generator=gen)
-    W = torch.randn(nblk, P, M, 256, dtype=torch.float32, device=dev, generator=gen)
+    Rd = torch.randn(P, nsteps, kd, kd, dtype=torch.float64, device=dev, generator=gen)
+    W = torch.randn(ne0 // 256, P, M, 256, dtype=torch.float32, device=dev, generator=gen)
     Es = torch.empty_like(E)
     st = torch.cuda.current_stream().cuda_stream
-    for k in range(nblk - 1):
-        assert g.lib.gpuq_ldlq_scale_dev(E.data_ptr(), Rd.data_ptr(), Es.data_ptr(), P, M, nblk, k, st) == E.numel() * 8
+    steps = range(nsteps - 1) if kd == 256 else [0, 1, 7, 8, nsteps - 9, nsteps - 2]
+    for k in steps:
+        assert g.lib.gpuq_ldlq_scale_dev(E.data_ptr(), Rd.data_ptr(), Es.data_ptr(), P, M, nsteps, kd, k, st) == \
+            E.numel() * 8, g.error()
         want_es = torch.bmm(E, Rd[:, k])
         torch.cuda.synchronize()
         assert torch.allclose(Es, want_es, rtol=1e-12, atol=1e-15)
         Wrows = W.permute(1, 2, 0, 3).reshape(P, M, ne0)                   # row view of the column-block-major W
-        upd = torch.bmm(Es, U[:, k * 256:(k + 1) * 256, (k + 1) * 256:]).to(torch.float32)
+        c1 = (k + 1) * kd
+        upd = torch.bmm(Es, U[:, k * kd:c1, c1:]).to(torch.float32)
         want = Wrows.clone()
-        want[:, :, (k + 1) * 256:] -= upd
-        n = g.lib.gpuq_ldlq_update_dev(Es.data_ptr(), U.data_ptr(), W.data_ptr(), P, M, ne0, k, st)
-        assert n == P * M * (ne0 - (k + 1) * 256) * 4, g.error()
+        want[:, :, c1:] -= upd
+        n = g.lib.gpuq_ldlq_update_dev(Es.data_ptr(), U.data_ptr(), W.data_ptr(), P, M, ne0, kd, k, st)
+        assert n == P * M * (ne0 - c1) * 4, g.error()
         torch.cuda.synchronize()
         got = W.permute(1, 2, 0, 3).reshape(P, M, ne0)
         ulps = (got.view(torch.int32).long() - want.view(torch.int32).long()).abs()
         assert int(ulps.max()) <= 1
         assert float((ulps != 0).double().mean()) < 1e-4
-        assert torch.equal(got[:, :, :(k + 1) * 256], want[:, :, :(k + 1) * 256])   # columns before c1 untouched
-    # argument checks
-    assert g.lib.gpuq_ldlq_update_dev(Es.data_ptr(), U.data_ptr(), W.data_ptr(), P, M, ne0, nblk - 1, st) == 0
-    assert g.lib.gpuq_ldlq_scale_dev(E.data_ptr() + 8, Rd.data_ptr(), Es.data_ptr(), P, M, nblk, 0, st) == 0
+        assert torch.equal(got[:, :, :c1], want[:, :, :c1])                # columns before c1 untouched
+    # argument checks: no columns after the last step, a misaligned pointer, a K the kernels do not have
+    assert g.lib.gpuq_ldlq_update_dev(Es.data_ptr(), U.data_ptr(), W.data_ptr(), P, M, ne0, kd, nsteps - 1, st) == 0
+    assert g.lib.gpuq_ldlq_scale_dev(E.data_ptr() + 8, Rd.data_ptr(), Es.data_ptr(), P, M, nsteps, kd, 0, st) == 0
+    assert g.lib.gpuq_ldlq_scale_dev(E.data_ptr(), Rd.data_ptr(), Es.data_ptr(), P, M, nsteps, 16, 0, st) == 0
+    assert g.lib.gpuq_ldlq_scale_dev(E.data_ptr(), Rd.data_ptr(), Es.data_ptr(), P, M, nsteps, kd, nsteps, st) == 0
+
+
+def _sub_case(rows, ne0, seed):
+    """weights with a zero row (ggml's d = 0) and a row of large outliers; an imatrix with a dead column"""
+    rng = np.random.default_rng(seed)
+    W = (rng.standard_t(5, (rows, ne0)) * 0.02).astype(np.float32)
+    W[3] = 0
+    W[5, ::37] *= 40
+    im = rng.lognormal(0.0, 1.0, ne0).astype(np.float32)
+    im[17] = 0
+    return W, im
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("sub,ss,order", [(32, 0, "seq"), (8, 0, "seq"), (32, 1, "seq"), (32, 2, "act"), (8, 0, "act")])
+def test_gpu_iq2xxs_sub_kernels_exact(tables, oracle, sub, ss, order):
+    """the sub-block variant's own kernels - ggml's pass, the weights qw * sqrt(sigma2 + x^2), the point choice over
+    the whole grid with the sign rule and the scale search - byte for byte against the restatement (which equals the
+    reference's function on the golden cases): with U = I the feedback adds exactly zero, so every byte of the GPU
+    result is the kernels' alone; two groups of 96 rows x 1024 in lockstep"""
+    torch, G, ldlq_gpu, g = _gpu_setup(tables)
+    dev = torch.device("cuda")
+    ne0 = 1024
+    gqt = ldlq_gpu.GpuQuant(g, G.TYPES["IQ2_XXS"])
+    quant, _, _ = LO.checker_quant(oracle, G.TYPES["IQ2_XXS"])
+    grid = LO.iq2xxs_grid(oracle)
+    U = np.eye(ne0)
+    nblk = ne0 // 256
+    blocks = np.arange(nblk)[::-1] if order == "act" else np.arange(nblk)
+    perm = (blocks[:, None] * 256 + np.arange(256)[None]).reshape(-1)
+    cases = [_sub_case(96, ne0, 300 + i) for i in range(2)]
+    factors = [ldlq_gpu.factor_from_U(torch.from_numpy(U).to(dev), torch.from_numpy(perm).to(dev)) for _ in cases]
+    got = ldlq_gpu.ldlq_groups_iq2xxs_sub([torch.from_numpy(W[None].copy()).to(dev) for W, _ in cases], factors, gqt,
+                                          [torch.from_numpy(im[None].copy()).to(dev) for _, im in cases], sub=sub,
+                                          scale_search=ss)
+    for (W, im), out in zip(cases, got):
+        want, _ = LO.quantize_matrix_iq2xxs_sub(W, quant, grid, U, perm, im, sub=sub, scale_search=ss)
+        out = out.cpu().numpy()[0]
+        assert np.array_equal(out, want), (out != want).any(-1).sum()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("key,sub,ss,order", [("sub32", 32, 0, "seq"), ("sub8", 8, 0, "seq"), ("sub32_ss1", 32, 1, "seq"),
+                                              ("sub32_act", 32, 0, "act")])
+def test_gpu_iq2xxs_sub_against_reference(tables, oracle, golden, key, sub, ss, order):
+    """the sub-block variant with feedback against the reference's own function (golden file: tools/ldlq.py:202 run
+    on the reference's host-built quantizer) at the reference's bar for its GPU loop"""
+    torch, G, ldlq_gpu, g = _gpu_setup(tables)
+    gd = golden
+    W, H, n, im = gd["W"], gd["H"], int(gd["n"]), gd["imatrix"]
+    dev = torch.device("cuda")
+    gqt = ldlq_gpu.GpuQuant(g, G.TYPES["IQ2_XXS"])
+    U, perm, _, _ = LO.prepare_hessian(H, n, damp=0.01, order=order)
+    got = ldlq_gpu.quantize_matrix_iq2xxs_sub_torch(torch.from_numpy(W[None].copy()).to(dev), gqt,
+                                                    torch.from_numpy(U).to(dev), torch.from_numpy(perm).to(dev),
+                                                    torch.from_numpy(im[None].copy()).to(dev), sub=sub,
+                                                    scale_search=ss).cpu().numpy()[0]
+    want = gd["IQ2_XXS_%s" % key]
+    same = (got.reshape(W.shape[0], -1, 66) == want.reshape(W.shape[0], -1, 66)).all(-1).mean()
+    assert same >= IDENTICAL_MIN, same
+    deq = oracle.dequantize(G.TYPES["IQ2_XXS"], got).reshape(W.shape)
+    loss, lw = ldlq_gpu.proxy_loss(W, deq, H, n), float(gd["IQ2_XXS_%s_loss" % key])
+    assert abs(loss - lw) <= LOSS_RTOL * lw, (loss, lw)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("sub,ss", [(32, 1), (8, 0)])
+def test_gpu_iq2xxs_sub_experts_against_restatement(tables, oracle, sub, ss):
+    """the whole GPU path of the variant - the float64 factor of each expert's own Hessian, then one lockstep loop
+    over three experts (ldlq_experts with sub) - against the restatement's float64 loop per expert: 128 x 1536"""
+    torch, G, ldlq_gpu, g = _gpu_setup(tables)
+    dev = torch.device("cuda")
+    ne1, ne0, n = 128, 1536, 4096
+    gqt = ldlq_gpu.GpuQuant(g, G.TYPES["IQ2_XXS"])
+    quant, _, _ = LO.checker_quant(oracle, G.TYPES["IQ2_XXS"], threads=os.cpu_count() or 1)
+    grid = LO.iq2xxs_grid(oracle)
+    Ws, Hs, ims = [], [], []
+    for e in range(3):
+        H, im = LO.synthetic_hessian(ne0, n, seed=90 + e)
+        W = (np.random.default_rng(95 + e).standard_t(5, (ne1, ne0)) * 0.02).astype(np.float32)
+        Ws.append(W)
+        Hs.append(H)
+        ims.append(im)
+    got = ldlq_gpu.ldlq_experts([torch.from_numpy(W[None].copy()).to(dev) for W in Ws],
+                                [torch.from_numpy(H).to(dev) for H in Hs], [n] * 3, gqt,
+                                [torch.from_numpy(im[None].copy()).to(dev) for im in ims], sub=sub, scale_search=ss)
+    for e in range(3):
+        U, perm, _, _ = LO.prepare_hessian(Hs[e], n, damp=0.01)
+        want, deq_w = LO.quantize_matrix_iq2xxs_sub(Ws[e], quant, grid, U, perm, ims[e], sub=sub, scale_search=ss)
+        out = got[e].cpu().numpy()[0]
+        same = (out.reshape(ne1, -1, 66) == want.reshape(ne1, -1, 66)).all(-1).mean()
+        assert same >= IDENTICAL_MIN, (e, same)
+        lw = LO.proxy_loss(Ws[e], deq_w, Hs[e], n)
+        deq = oracle.dequantize(G.TYPES["IQ2_XXS"], out).reshape(ne1, ne0)
+        assert abs(LO.proxy_loss(Ws[e], deq, Hs[e], n) - lw) <= LOSS_RTOL * lw
 
 
 @pytest.mark.gpu

@@ -695,28 +695,52 @@ bool misaligned(const void * p, uintptr_t a) { return (reinterpret_cast<uintptr_
 }  // namespace
 
 size_t gpuq_ldlq_scale_dev(const double * d_err, const double * d_rd, double * d_es, int64_t ngroups, int64_t rows,
-                           int64_t nblk, int64_t k, void * stream) {
-    if (!d_err || !d_rd || !d_es || ngroups <= 0 || rows <= 0 || nblk <= 0 || k < 0 || k >= nblk ||
-        misaligned(d_err, 16) || misaligned(d_rd, 16) || misaligned(d_es, 16)) {
-        set_err("gpuq_ldlq_scale_dev: bad arguments (0 <= k < nblk; every pointer 16-byte aligned)");
+                           int64_t nsteps, int64_t kdim, int64_t step, void * stream) {
+    if (!d_err || !d_rd || !d_es || ngroups <= 0 || rows <= 0 || nsteps <= 0 || step < 0 || step >= nsteps ||
+        (kdim != 256 && kdim != 32 && kdim != 8) || misaligned(d_err, 16) || misaligned(d_rd, 16) || misaligned(d_es, 16)) {
+        set_err("gpuq_ldlq_scale_dev: bad arguments (kdim 256, 32 or 8; 0 <= step < nsteps; every pointer 16-byte aligned)");
         return 0;
     }
-    const cudaError_t e = launch_ldlq_scale(d_err, d_rd, d_es, ngroups, rows, nblk, (int) k, (cudaStream_t) stream);
+    const cudaError_t e = launch_ldlq_scale(d_err, d_rd, d_es, ngroups, rows, nsteps, (int) kdim, step, (cudaStream_t) stream);
     if (e != cudaSuccess) { set_err("gpuq_ldlq_scale_dev: launch failed: %s", cudaGetErrorString(e)); return 0; }
-    return (size_t) ngroups * rows * QK * 8;
+    return (size_t) ngroups * rows * kdim * 8;
 }
 
 size_t gpuq_ldlq_update_dev(const double * d_es, const double * d_u, float * d_w, int64_t ngroups, int64_t rows,
-                            int64_t ne0, int64_t k, void * stream) {
-    if (!d_es || !d_u || !d_w || ngroups <= 0 || rows <= 0 || ne0 <= 0 || ne0 % QK || k < 0 || (k + 1) * QK >= ne0 ||
-        misaligned(d_es, 16) || misaligned(d_u, 16) || misaligned(d_w, 8)) {
-        set_err("gpuq_ldlq_update_dev: bad arguments (k must leave columns to update; ne0 %% 256 == 0; Es and U 16-byte "
-                "aligned, W 8-byte aligned)");
+                            int64_t ne0, int64_t kdim, int64_t step, void * stream) {
+    if (!d_es || !d_u || !d_w || ngroups <= 0 || rows <= 0 || ne0 <= 0 || ne0 % QK || (kdim != 256 && kdim != 32 && kdim != 8) ||
+        step < 0 || (step + 1) * kdim >= ne0 || misaligned(d_es, 16) || misaligned(d_u, 16) || misaligned(d_w, 8)) {
+        set_err("gpuq_ldlq_update_dev: bad arguments (kdim 256, 32 or 8; columns left after step; ne0 %% 256 == 0; Es "
+                "and U 16-byte aligned, W 8-byte aligned)");
         return 0;
     }
-    const cudaError_t e = launch_ldlq_update(d_es, d_u, d_w, ngroups, rows, ne0, (int) k, (cudaStream_t) stream);
+    const cudaError_t e = launch_ldlq_update(d_es, d_u, d_w, ngroups, rows, ne0, (int) kdim, step, (cudaStream_t) stream);
     if (e != cudaSuccess) { set_err("gpuq_ldlq_update_dev: launch failed: %s", cudaGetErrorString(e)); return 0; }
-    return (size_t) ngroups * rows * (ne0 - (k + 1) * QK) * 4;
+    return (size_t) ngroups * rows * (ne0 - (step + 1) * kdim) * 4;
+}
+
+size_t gpuq_ldlq_sub_weff_dev(const float * d_blk, const float * d_qw, int64_t qw_div, float * d_weff, int64_t rows,
+                              void * stream) {
+    if (!d_blk || !d_qw || !d_weff || rows <= 0 || qw_div <= 0) { set_err("gpuq_ldlq_sub_weff_dev: bad arguments"); return 0; }
+    const cudaError_t e = launch_sub_weff(d_blk, d_qw, qw_div, d_weff, rows, (cudaStream_t) stream);
+    if (e != cudaSuccess) { set_err("gpuq_ldlq_sub_weff_dev: launch failed: %s", cudaGetErrorString(e)); return 0; }
+    return (size_t) rows * QK * 4;
+}
+
+size_t gpuq_ldlq_sub_points_dev(const float * d_blk, const float * d_weff, void * d_q, double * d_err, int64_t rows, int sub,
+                                int c0, int scale_search, void * stream) {
+    if (!d_blk || !d_weff || !d_q || !d_err || rows <= 0 || (sub != 32 && sub != 8) || c0 < 0 || c0 % sub ||
+        c0 + sub > QK || scale_search < 0 || scale_search > 15) {
+        set_err("gpuq_ldlq_sub_points_dev: bad arguments (sub 32 or 8, c0 a multiple of sub below 256, scale_search 0..15)");
+        return 0;
+    }
+    Device * d = current_device();
+    const uint64_t * grid = d ? d->dq_grid(IQ2_XXS) : nullptr;
+    if (!grid) { set_err("gpuq_ldlq_sub_points_dev: no IQ2_XXS grid (gpuq_init first)"); return 0; }
+    const cudaError_t e = launch_sub_points(d_blk, d_weff, (uint8_t *) d_q, d_err, rows, sub, c0, scale_search, grid,
+                                            (cudaStream_t) stream);
+    if (e != cudaSuccess) { set_err("gpuq_ldlq_sub_points_dev: launch failed: %s", cudaGetErrorString(e)); return 0; }
+    return (size_t) rows * sub * 8;
 }
 
 size_t gpuq_dequantize_src_dev(int src, const void * d_raw, float * d_out, int64_t n, void * stream) {

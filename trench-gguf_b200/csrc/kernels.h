@@ -34,14 +34,21 @@ cudaError_t launch_dequant(int type, const void * q, float * out, int64_t nblock
 // LDLQ block error E = blk - to_float(q), float32 maths, stored as float64 (f64) or float32
 cudaError_t launch_dequant_error(int type, const void * q, const float * blk, void * err, bool f64, int64_t nblocks,
                                  DequantTab tab, cudaStream_t st);
-// LDLQ's error-feedback steps of block k (ldlq.cu), every group (matrices sharing one factor) in one launch:
-// scale Es = E Rd[k] (Rd [ngroups][nblk][256][256] f64: U_kk^-1), E and Es [ngroups][rows][256] f64;
-// update W~[:, c] = f32(W~[:, c] - f32(Es U[k*256.., c])) for c >= (k+1)*256, W~ column-block major
-// [nblk][ngroups][rows][256] f32, U [ngroups][ne0][ne0] f64
+// LDLQ's error-feedback steps (ldlq.cu), every group (matrices sharing one factor) in one launch, for feedback blocks
+// of kd columns (256: super-blocks; 32 or 8: the IQ2_XXS sub-block variant), step = the block's index:
+// scale Es = E Rd[step] (Rd [ngroups][ne0/kd][kd][kd] f64: U's diagonal blocks inverted), E and Es [ngroups][rows][kd];
+// update W~[:, c] = f32(W~[:, c] - f32(Es U[step*kd.., c])) for c >= (step+1)*kd, W~ column-block major
+// [ne0/256][ngroups][rows][256] f32, U [ngroups][ne0][ne0] f64
 cudaError_t launch_ldlq_scale(const double * E, const double * Rd, double * Es, int64_t ngroups, int64_t rows,
-                              int64_t nblk, int k, cudaStream_t st);
+                              int64_t nsteps, int kd, int64_t step, cudaStream_t st);
 cudaError_t launch_ldlq_update(const double * Es, const double * U, float * W, int64_t ngroups, int64_t rows, int64_t ne0,
-                               int k, cudaStream_t st);
+                               int kd, int64_t step, cudaStream_t st);
+// the IQ2_XXS sub-block variant of LDLQ (ldlq_sub.cu): the weights qw * sqrt(sigma2 + x^2) of a super-block's rows
+// (sigma2: numpy's float32 row sum of x^2 / 256; row r takes importance row r / qw_div), and the points of the groups
+// in columns [c0, c0 + sub) chosen again over the whole grid (sub 32: with scale search; 8), err = x - q (float64)
+cudaError_t launch_sub_weff(const float * blk, const float * qw, int64_t qw_div, float * weff, int64_t rows, cudaStream_t st);
+cudaError_t launch_sub_points(const float * blk, const float * weff, uint8_t * q, double * err, int64_t rows, int sub,
+                              int c0, int scale_search, const uint64_t * grid, cudaStream_t st);
 // n values of any readable source (common.cuh src_block_len) -> n floats; tab: the dequant grid of an i-quant source
 cudaError_t launch_decode(int src, const void * raw, float * out, int64_t n, DequantTab tab, cudaStream_t st);
 // the same, value i (of this pass; value v0 + i of the tensor) multiplied by scale[(v0 + i) / per_mat] when scale

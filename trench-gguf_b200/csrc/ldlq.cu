@@ -29,12 +29,14 @@ namespace gq {
 namespace {
 
 constexpr int UBM = 128, UBN = 64, UBK = 32, UTHREADS = 256, USTAGES = 2;
-constexpr int APAD = UBK + 4;   // doubles a row of the A (E) tile
-constexpr int BPAD = UBN + 4;   // doubles a row of the B (G) tile
+constexpr int BPAD = UBN + 4;   // doubles a row of the B (U) tile
 
-struct UpdSmem {
+// K = KD (256: a super-block; 32 or 8: the IQ2_XXS sub-block variant), staged UBK (or all of a shorter K) at a time;
+// A rows padded by 4 doubles (conflict-free fragment loads for both strides)
+template <int KD> struct UpdSmem {
+    static constexpr int KC = KD < UBK ? KD : UBK, APAD = KC + 4;
     double a[USTAGES][UBM * APAD];
-    double b[USTAGES][UBK * BPAD];
+    double b[USTAGES][KC * BPAD];
 };
 
 __device__ __forceinline__ void cp_async16(void * smem, const void * gmem) {
@@ -51,36 +53,41 @@ __device__ __forceinline__ void dmma_8x8x4(double (&d)[2], double a, double b) {
                  : "d"(a), "d"(b));
 }
 
-// One tile of A [rows][256] (group g) times B [256][ldb] (columns n0 .. n0+63), float64. SUB: W~ -= f32(product) at
-// columns n0.. of the column-block-major W~; else the product is stored to Out [ngroups][rows][256] at columns n0..
-template <bool SUB>
+// One tile of A [rows][KD] (group g) times B [KD][ldb] (columns n0 .. n0+63, those below ncol), float64. SUB:
+// W~ -= f32(product) at columns n0.. of the column-block-major W~; else the product is stored to Out
+// [ngroups][rows][KD] at columns n0..
+template <bool SUB, int KD>
 __global__ void __launch_bounds__(UTHREADS, 2) k_ldlq_gemm(const double * __restrict__ A, const double * __restrict__ B,
                                                            int64_t b_group_stride, int64_t ldb, int64_t n_first,
-                                                           void * __restrict__ out, int64_t ngroups, int64_t rows) {
+                                                           int64_t ncol, void * __restrict__ out, int64_t ngroups,
+                                                           int64_t rows) {
+    using SM = UpdSmem<KD>;
+    constexpr int KC = SM::KC, APAD = SM::APAD;
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    UpdSmem & sm = *reinterpret_cast<UpdSmem *>(smem_raw);
+    SM & sm = *reinterpret_cast<SM *>(smem_raw);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int wm = warp >> 1, wn = warp & 1;             // 4 x 2 warps
     const int64_t g = blockIdx.z;
     const int64_t m0 = (int64_t) blockIdx.y * UBM;
     const int64_t n0 = n_first + (int64_t) blockIdx.x * UBN;   // first column of the tile (in B's columns)
-    const double * Eg = A + g * rows * QK;
+    const double * Eg = A + g * rows * KD;
     const double * Gk = B + g * b_group_stride;
-    const int64_t ne0 = ldb;
 
     auto load = [&](int stage, int kk) {
-        // A: 128 rows x 32 doubles = 2,048 16-byte pieces; B: 32 rows x 64 doubles = 1,024 pieces
+        // A: 128 rows x KC doubles; B: KC rows x 64 doubles (columns at or past ncol read as 0), 16-byte pieces
 #pragma unroll
-        for (int i = tid; i < UBM * (UBK / 2); i += UTHREADS) {
-            const int r = i / (UBK / 2), ch = i % (UBK / 2);
+        for (int i = tid; i < UBM * (KC / 2); i += UTHREADS) {
+            const int r = i / (KC / 2), ch = i % (KC / 2);
             double * dst = &sm.a[stage][r * APAD + ch * 2];
-            if (m0 + r < rows) cp_async16(dst, Eg + (m0 + r) * QK + kk + ch * 2);
+            if (m0 + r < rows) cp_async16(dst, Eg + (m0 + r) * KD + kk + ch * 2);
             else { dst[0] = 0.0; dst[1] = 0.0; }
         }
 #pragma unroll
-        for (int i = tid; i < UBK * (UBN / 2); i += UTHREADS) {
+        for (int i = tid; i < KC * (UBN / 2); i += UTHREADS) {
             const int r = i / (UBN / 2), ch = i % (UBN / 2);
-            cp_async16(&sm.b[stage][r * BPAD + ch * 2], Gk + (int64_t) (kk + r) * ne0 + n0 + ch * 2);
+            double * dst = &sm.b[stage][r * BPAD + ch * 2];
+            if (n0 + ch * 2 < ncol) cp_async16(dst, Gk + (int64_t) (kk + r) * ldb + n0 + ch * 2);
+            else { dst[0] = 0.0; dst[1] = 0.0; }
         }
     };
 
@@ -90,13 +97,13 @@ __global__ void __launch_bounds__(UTHREADS, 2) k_ldlq_gemm(const double * __rest
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j][0] = acc[i][j][1] = 0.0;
 
-    constexpr int NKT = QK / UBK;
+    constexpr int NKT = KD / KC;
     load(0, 0);
     cp_commit();
 #pragma unroll 1
     for (int kt = 0; kt < NKT; ++kt) {
         if (kt + 1 < NKT) {
-            load((kt + 1) & 1, (kt + 1) * UBK);
+            load((kt + 1) & 1, (kt + 1) * KC);
             cp_commit();
             cp_wait<1>();
         } else {
@@ -106,7 +113,7 @@ __global__ void __launch_bounds__(UTHREADS, 2) k_ldlq_gemm(const double * __rest
         const double * As = sm.a[kt & 1] + (wm * 32 + (lane >> 2)) * APAD + (lane & 3);
         const double * Bs = sm.b[kt & 1] + (lane & 3) * BPAD + wn * 32 + (lane >> 2);
 #pragma unroll
-        for (int kq = 0; kq < UBK / 4; ++kq) {
+        for (int kq = 0; kq < KC / 4; ++kq) {
             double a[4], b[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) a[i] = As[i * 8 * APAD + kq * 4];
@@ -127,6 +134,7 @@ __global__ void __launch_bounds__(UTHREADS, 2) k_ldlq_gemm(const double * __rest
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int64_t col = n0 + wn * 32 + j * 8 + (lane & 3) * 2;
+            if (col >= ncol) continue;
             if constexpr (SUB) {
                 const int64_t blk = col / QK, cc = col % QK;
                 float2 * p = reinterpret_cast<float2 *>(static_cast<float *>(out) + ((blk * ngroups + g) * rows + row) * QK + cc);
@@ -135,7 +143,7 @@ __global__ void __launch_bounds__(UTHREADS, 2) k_ldlq_gemm(const double * __rest
                 w.y = w.y - (float) acc[i][j][1];
                 *p = w;
             } else {
-                *reinterpret_cast<double2 *>(static_cast<double *>(out) + (g * rows + row) * QK + col) =
+                *reinterpret_cast<double2 *>(static_cast<double *>(out) + (g * rows + row) * KD + col) =
                     make_double2(acc[i][j][0], acc[i][j][1]);
             }
         }
@@ -144,31 +152,44 @@ __global__ void __launch_bounds__(UTHREADS, 2) k_ldlq_gemm(const double * __rest
 
 }  // namespace
 
-cudaError_t launch_ldlq_scale(const double * E, const double * Rd, double * Es, int64_t ngroups, int64_t rows,
-                              int64_t nblk, int k, cudaStream_t st) {
-    if (ngroups <= 0 || rows <= 0 || k < 0 || k >= nblk || ngroups > 65535) return cudaErrorInvalidValue;
-    const size_t smem = sizeof(UpdSmem);
-    const cudaError_t e = cudaFuncSetAttribute(k_ldlq_gemm<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+template <bool SUB, int KD>
+cudaError_t launch_gemm(const double * A, const double * B, int64_t b_group_stride, int64_t ldb, int64_t n_first,
+                        int64_t ncol, void * out, int64_t ngroups, int64_t rows, cudaStream_t st) {
+    const size_t smem = sizeof(UpdSmem<KD>);
+    const cudaError_t e = cudaFuncSetAttribute(k_ldlq_gemm<SUB, KD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
     if (e != cudaSuccess) return e;
-    const dim3 grid(QK / UBN, (unsigned) ((rows + UBM - 1) / UBM), (unsigned) ngroups);
-    if (grid.y > 65535) return cudaErrorInvalidValue;
-    k_ldlq_gemm<false><<<grid, UTHREADS, smem, st>>>(E, Rd + (int64_t) k * QK * QK, nblk * QK * QK, QK, 0, Es, ngroups,
-                                                     rows);
+    const dim3 grid((unsigned) ((ncol - n_first + UBN - 1) / UBN), (unsigned) ((rows + UBM - 1) / UBM), (unsigned) ngroups);
+    if (grid.y > 65535 || ngroups > 65535) return cudaErrorInvalidValue;
+    k_ldlq_gemm<SUB, KD><<<grid, UTHREADS, smem, st>>>(A, B, b_group_stride, ldb, n_first, ncol, out, ngroups, rows);
     return cudaGetLastError();
 }
 
+// Es = E Rd[step] for the step-th KD x KD diagonal block (Rd: [ngroups][nsteps][KD][KD])
+cudaError_t launch_ldlq_scale(const double * E, const double * Rd, double * Es, int64_t ngroups, int64_t rows,
+                              int64_t nsteps, int kd, int64_t step, cudaStream_t st) {
+    if (ngroups <= 0 || rows <= 0 || step < 0 || step >= nsteps) return cudaErrorInvalidValue;
+    const double * B = Rd + step * (int64_t) kd * kd;
+    const int64_t gs = nsteps * (int64_t) kd * kd;
+    switch (kd) {
+        case 256: return launch_gemm<false, 256>(E, B, gs, kd, 0, kd, Es, ngroups, rows, st);
+        case 32:  return launch_gemm<false, 32>(E, B, gs, kd, 0, kd, Es, ngroups, rows, st);
+        case 8:   return launch_gemm<false, 8>(E, B, gs, kd, 0, kd, Es, ngroups, rows, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+// W~[:, c] -= f32(Es U[a.., c]) for every column c >= a + kd, a = step * kd (U: [ngroups][ne0][ne0])
 cudaError_t launch_ldlq_update(const double * Es, const double * U, float * W, int64_t ngroups, int64_t rows, int64_t ne0,
-                               int k, cudaStream_t st) {
-    if (ngroups <= 0 || rows <= 0 || ne0 % QK || k < 0 || (int64_t) (k + 1) * QK >= ne0 || ngroups > 65535)
-        return cudaErrorInvalidValue;
-    const size_t smem = sizeof(UpdSmem);
-    const cudaError_t e = cudaFuncSetAttribute(k_ldlq_gemm<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
-    if (e != cudaSuccess) return e;
-    const int64_t c1 = (int64_t) (k + 1) * QK, rest = ne0 - c1;
-    const dim3 grid((unsigned) (rest / UBN), (unsigned) ((rows + UBM - 1) / UBM), (unsigned) ngroups);
-    if (grid.y > 65535) return cudaErrorInvalidValue;
-    k_ldlq_gemm<true><<<grid, UTHREADS, smem, st>>>(Es, U + (int64_t) k * QK * ne0, ne0 * ne0, ne0, c1, W, ngroups, rows);
-    return cudaGetLastError();
+                               int kd, int64_t step, cudaStream_t st) {
+    const int64_t a = step * kd, c1 = a + kd;
+    if (ngroups <= 0 || rows <= 0 || ne0 % QK || step < 0 || c1 >= ne0) return cudaErrorInvalidValue;
+    const double * B = U + a * ne0;
+    switch (kd) {
+        case 256: return launch_gemm<true, 256>(Es, B, ne0 * ne0, ne0, c1, ne0, W, ngroups, rows, st);
+        case 32:  return launch_gemm<true, 32>(Es, B, ne0 * ne0, ne0, c1, ne0, W, ngroups, rows, st);
+        case 8:   return launch_gemm<true, 8>(Es, B, ne0 * ne0, ne0, c1, ne0, W, ngroups, rows, st);
+        default: return cudaErrorInvalidValue;
+    }
 }
 
 }  // namespace gq

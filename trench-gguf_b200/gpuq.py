@@ -28,7 +28,8 @@ SYMBOLS = ("gpuq_init", "gpuq_block_bytes", "gpuq_can_quantize", "gpuq_quantize"
            "gpuq_can_dequantize_type", "gpuq_dequantize_dev", "gpuq_dequantize_src_dev",
            "gpuq_last_error", "gpuq_status", "gpuq_init_devices", "gpuq_device_count", "gpuq_requantize_dev",
            "gpuq_requantize_noalloc", "gpuq_dequantize_error_dev", "gpuq_ldlq_scale_dev",
-           "gpuq_ldlq_update_dev", "gpuq_requantize_scaled_batch", "gpuq_check_q8_rounding")
+           "gpuq_ldlq_update_dev", "gpuq_requantize_scaled_batch", "gpuq_check_q8_rounding",
+           "gpuq_ldlq_sub_weff_dev", "gpuq_ldlq_sub_points_dev")
 
 
 class GpuqError(RuntimeError):
@@ -71,10 +72,12 @@ def declare(gq):
         "gpuq_requantize_dev": (sz, [c.c_int, vp, c.c_int, vp, i64, i64, i64, vp, vp]),
         "gpuq_requantize_noalloc": (sz, [c.c_int, vp, c.c_int, vp, i64, i64, i64, vp]),
         "gpuq_dequantize_error_dev": (sz, [c.c_int, vp, vp, vp, c.c_int, i64, vp]),
-        "gpuq_ldlq_scale_dev": (sz, [vp, vp, vp, i64, i64, i64, i64, vp]),
+        "gpuq_ldlq_scale_dev": (sz, [vp, vp, vp, i64, i64, i64, i64, i64, vp]),
+        "gpuq_ldlq_sub_weff_dev": (sz, [vp, vp, i64, vp, i64, vp]),
+        "gpuq_ldlq_sub_points_dev": (sz, [vp, vp, vp, vp, i64, c.c_int, c.c_int, c.c_int, vp]),
         "gpuq_requantize_scaled_batch": (sz, [c.c_int, vp, c.c_int, vp, i64, i64, i64, vp, vp]),
         "gpuq_check_q8_rounding": (c.c_int64, []),
-        "gpuq_ldlq_update_dev": (sz, [vp, vp, vp, i64, i64, i64, i64, vp]),
+        "gpuq_ldlq_update_dev": (sz, [vp, vp, vp, i64, i64, i64, i64, i64, vp]),
     }
     for name, (res, args) in sig.items():
         f = getattr(gq, name)

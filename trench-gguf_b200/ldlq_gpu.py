@@ -348,20 +348,93 @@ def ldlq_groups(Ws, factors, gqt, imatrices, weights="imatrix", feedback=True, b
         if not feedback or k + 1 == nblk:
             continue
         gqt.error(raw[k], Wb[k], torch.float64, out=E)
-        if lib.gpuq_ldlq_scale_dev(E.data_ptr(), Rd.data_ptr(), Es.data_ptr(), P, M, nblk, k, st) != E.numel() * 8:
-            raise RuntimeError("gpuq_ldlq_scale_dev: " + lib.gpuq_last_error().decode())
-        want = P * M * (ne0 - (k + 1) * bs) * 4
-        if lib.gpuq_ldlq_update_dev(Es.data_ptr(), U.data_ptr(), Wb.data_ptr(), P, M, ne0, k, st) != want:
-            raise RuntimeError("gpuq_ldlq_update_dev: " + lib.gpuq_last_error().decode())
-    # bytes back to ggml's row layout, each block at its own column position
+        _feedback(lib, E, Rd, Es, U, Wb, P, M, ne0, bs, k, st)
+    return _rows_back(raw, perms, P, B, ne1, bs)
+
+
+def _feedback(lib, E, Rd, Es, U, Wb, P, M, ne0, kd, step, st):
+    """Es = E Rd[step]; W~[:, c] -= f32(Es U[step*kd.., c]) for the columns after the step's kd columns"""
+    if lib.gpuq_ldlq_scale_dev(E.data_ptr(), Rd.data_ptr(), Es.data_ptr(), P, M, ne0 // kd, kd, step, st) != E.numel() * 8:
+        raise RuntimeError("gpuq_ldlq_scale_dev: " + lib.gpuq_last_error().decode())
+    want = P * M * (ne0 - (step + 1) * kd) * 4
+    if lib.gpuq_ldlq_update_dev(Es.data_ptr(), U.data_ptr(), Wb.data_ptr(), P, M, ne0, kd, step, st) != want:
+        raise RuntimeError("gpuq_ldlq_update_dev: " + lib.gpuq_last_error().decode())
+
+
+def _rows_back(raw, perms, P, B, ne1, bs):
+    """[nblk][P*B*ne1][tsize] block-major bytes back to ggml's row layout, each block at its own column position"""
+    torch = _torch()
+    nblk, tsize = raw.shape[0], raw.shape[-1]
     raw = raw.view(nblk, P, B, ne1, tsize)
     outs = []
     for g in range(P):
         pos = perms[g].view(nblk, bs)[:, 0] // bs
-        rows = torch.empty((nblk, B, ne1, tsize), dtype=torch.uint8, device=dev)
+        rows = torch.empty((nblk, B, ne1, tsize), dtype=torch.uint8, device=raw.device)
         rows.index_copy_(0, pos, raw[:, g])
         outs.append(rows.permute(1, 2, 0, 3).reshape(B, ne1, nblk * tsize))
     return outs
+
+
+def _sub_rd(Rd, kd):
+    """the inverses of U's kd x kd diagonal blocks, [nblk * 256/kd, kd, kd]: the diagonal blocks of the inverses of
+    its 256 x 256 ones (a triangular matrix's inverse has the inverses of its diagonal blocks on its diagonal)"""
+    nblk, bs = Rd.shape[0], Rd.shape[1]
+    ns = bs // kd
+    d = _torch().diagonal(Rd.view(nblk, ns, kd, ns, kd), dim1=1, dim2=3)      # [nblk, kd, kd, ns]
+    return d.permute(0, 3, 1, 2).reshape(nblk * ns, kd, kd).contiguous()
+
+
+def ldlq_groups_iq2xxs_sub(Ws, factors, gqt, imatrices, sub=32, scale_search=0, bs=QK, U_stack=None):
+    """The IQ2_XXS sub-block variant (tools/ldlq.py:202-272) over every group at once: per super-block, ggml's
+    IQ2_XXS pass (one launch over all groups' rows) fixes d and the sub-block scales, the weights
+    qw * sqrt(sigma2 + x^2) are formed (one launch), then every `sub` columns (32 or 8) the groups' 8-weight points
+    are chosen again over the whole grid on the updated weights (32: also the scales l-K..l+K, K = scale_search) and
+    their float64 error is fed into every later column by the float64 tensor-core GEMMs with K = sub. Same arguments
+    and result as ldlq_groups (importance: the imatrix rows, as the reference's variant)."""
+    torch = _torch()
+    if gqt.typ != 16:
+        raise ValueError("the sub-block variant is IQ2_XXS's (type 16), not type %d" % gqt.typ)
+    if sub not in (32, 8) or not 0 <= int(scale_search) <= 15:
+        raise ValueError("sub must be 32 or 8 and scale_search 0..15")
+    lib = gqt.gq
+    P = len(Ws)
+    B, ne1, ne0 = Ws[0].shape
+    nblk, M, tsize = ne0 // bs, B * ne1, gqt.tsize
+    dev = Ws[0].device
+    perms = [f.perm for f in factors]
+    Wb = torch.empty((nblk, P, M, bs), dtype=torch.float32, device=dev)
+    qw = torch.empty((nblk, P * B, bs), dtype=torch.float32, device=dev)
+    for g in range(P):
+        Wb[:, g] = Ws[g].index_select(2, perms[g]).reshape(M, nblk, bs).transpose(0, 1)
+        qw[:, g * B:(g + 1) * B] = imatrices[g].to(torch.float32).index_select(1, perms[g]).reshape(B, nblk, bs) \
+            .transpose(0, 1)
+    raw = torch.empty((nblk, P * M, tsize), dtype=torch.uint8, device=dev)
+    U = U_stack if U_stack is not None else torch.stack([f.U for f in factors])
+    Rd = torch.stack([_sub_rd(f.Rd, sub) for f in factors])                # [P, ne0/sub, sub, sub]
+    weff = torch.empty((P * M, bs), dtype=torch.float32, device=dev)
+    E = torch.empty((P, M, sub), dtype=torch.float64, device=dev)
+    Es = torch.empty_like(E)
+    st = _stream()
+    for k in range(nblk):
+        slab = Wb[k].view(P * M, bs)
+        gqt.quant_slab(slab, qw[k], raw[k], ne1)
+        if lib.gpuq_ldlq_sub_weff_dev(slab.data_ptr(), qw[k].data_ptr(), ne1, weff.data_ptr(), P * M, st) != weff.numel() * 4:
+            raise RuntimeError("gpuq_ldlq_sub_weff_dev: " + lib.gpuq_last_error().decode())
+        for j in range(bs // sub):
+            a = k * bs + j * sub
+            if lib.gpuq_ldlq_sub_points_dev(slab.data_ptr(), weff.data_ptr(), raw[k].data_ptr(), E.data_ptr(), P * M,
+                                            sub, j * sub, int(scale_search), st) != E.numel() * 8:
+                raise RuntimeError("gpuq_ldlq_sub_points_dev: " + lib.gpuq_last_error().decode())
+            if a + sub < ne0:
+                _feedback(lib, E, Rd, Es, U, Wb, P, M, ne0, sub, a // sub, st)
+    return _rows_back(raw, perms, P, B, ne1, bs)
+
+
+def quantize_matrix_iq2xxs_sub_torch(W, gqt, U, perm, imatrix, sub=32, scale_search=0, bs=QK):
+    """tools/ldlq.py:202's contract on the device: W f32 [B, ne1, ne0] (B matrices sharing U, perm), U [ne0, ne0]
+    float64 (Hinv = U^T U, in perm's order), perm [ne0], imatrix [B, ne0] -> uint8 [B, ne1, nblk*66]"""
+    return ldlq_groups_iq2xxs_sub([W], [factor_from_U(U, perm, None, bs)], gqt, [imatrix], sub=sub,
+                                  scale_search=scale_search, bs=bs)[0]
 
 
 def quantize_matrix_torch(W, gqt, U=None, perm=None, diag_n=None, imatrix=None, weights="imatrix", feedback=True,
@@ -381,15 +454,19 @@ def quantize_matrix_torch(W, gqt, U=None, perm=None, diag_n=None, imatrix=None, 
     return ldlq_groups([W], [factor_from_U(U, perm, diag_n, bs)], gqt, [imatrix], weights=weights, bs=bs)[0]
 
 
-def ldlq_experts(Ws, Hs, ns, gqt, imatrices, damp=0.01, order="seq", weights="imatrix", bs=QK):
+def ldlq_experts(Ws, Hs, ns, gqt, imatrices, damp=0.01, order="seq", weights="imatrix", bs=QK, sub=0,
+                 scale_search=0):
     """Every expert of a tensor on this GPU: each Hessian factored (float64) into one stacked U, then the loop of all
     experts in lockstep (one launch of each kernel a block for all of them). Ws[e]: f32 [B, ne1, ne0] (device),
-    Hs[e]: [ne0, ne0], ns[e]: rows H was summed over, imatrices[e]: [B, ne0]. Returns the experts' bytes."""
+    Hs[e]: [ne0, ne0], ns[e]: rows H was summed over, imatrices[e]: [B, ne0]. sub = 32 or 8 (IQ2_XXS): the sub-block
+    variant (the reference's --sub / --scale-search). Returns the experts' bytes."""
     torch = _torch()
     ne0 = Ws[0].shape[2]
     U = torch.empty((len(Ws), ne0, ne0), dtype=torch.float64, device=Ws[0].device)
     factors = [factor_hessian(Hs[e], ns[e], damp=damp, order=order, bs=bs, device=Ws[e].device, U_out=U[e])
                for e in range(len(Ws))]
+    if sub:
+        return ldlq_groups_iq2xxs_sub(Ws, factors, gqt, imatrices, sub=sub, scale_search=scale_search, bs=bs, U_stack=U)
     return ldlq_groups(Ws, factors, gqt, imatrices, weights=weights, bs=bs, U_stack=U)
 
 
