@@ -93,7 +93,8 @@ size_t gpuq_dequantize_src_dev(int src, const void * d_raw, float * d_out, int64
 const char * gpuq_last_error(void);
 
 /* The current device's status word: bit 0 a neighbour search found no finite candidate, bit 1 a final code fell
- * off the grid (ggml would trap; both mean non-finite input). reset != 0 clears it. Synchronises the device. */
+ * off the grid (ggml would trap; both mean non-finite input), bit 2 an input the kernel refused, bit 3 a bounded wait
+ * inside a kernel (TMA copies, tensor-core products) ran out. reset != 0 clears it. Synchronises the device. */
 unsigned gpuq_status(int reset);
 
 /* gpuq_init on several devices: the host API then shards every call over them (whole matrices - experts - or row
@@ -147,6 +148,21 @@ size_t gpuq_ldlq_sub_weff_dev(const float * d_blk, const float * d_qw, int64_t q
                               void * stream);
 size_t gpuq_ldlq_sub_points_dev(const float * d_blk, const float * d_weff, void * d_q, double * d_err, int64_t rows, int sub,
                                 int c0, int scale_search, void * stream);
+
+/* The Hessian of a layer's inputs on the tensor cores: H = (S X)^T (S X) (accumulate 0) or H += (S X)^T (S X)
+ * (accumulate 1), the float32 GEMM a row chunk of
+ * tools/hessian_from_dump.py:73-79 (`_xtx`: `H += (xc.T @ xc).double()`) for one chunk as one call.
+ * d_x: [rows][ld_x] values of type src (0: F32, 30: BF16 - the activation dumps' type), the first dim of a row used;
+ * d_scale: NULL, or a float32 per row (a gated Hessian's routing weight: x * s in float32); d_h: float64 [dim][dim]
+ * row-major, written or added to (exactly symmetric if it was). The sums over the rows are float32-accurate (bf16
+ * tensor-core products of an exact three-part split of each float32 value, float32 accumulation over at most 1,024
+ * rows; a BF16 source without a scale needs one product), then added in float64. d_scratch: gpuq_xtx_scratch_bytes(src, rows, dim, d_scale != NULL)
+ * bytes, 16-byte aligned, owned by the caller (the parts of X laid out as tensor-core operands). On `stream`, no
+ * synchronisation. Returns the bytes of X read, 0 on a bad argument (see gpuq_last_error). A wait inside the kernel
+ * that runs out sets bit 3 of gpuq_status. No counterpart in the reference's library (it runs torch's GEMM). */
+size_t gpuq_xtx_scratch_bytes(int src, int64_t rows, int64_t dim, int scaled);
+size_t gpuq_xtx_dev(int src, const void * d_x, int64_t ld_x, const float * d_scale, int64_t rows, int64_t dim, double * d_h,
+                    int accumulate, void * d_scratch, size_t scratch_bytes, void * stream);
 
 /* A diagnostic with no counterpart in the reference: how many floats x with |x| < 2^22 round differently in the Q8_0
  * kernels (which form ggml's roundf as trunc(x + copysign(0.5 - 2^-25, x))) than in CUDA's roundf: 0 expected; -1 if

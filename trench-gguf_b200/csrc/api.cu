@@ -743,6 +743,29 @@ size_t gpuq_ldlq_sub_points_dev(const float * d_blk, const float * d_weff, void 
     return (size_t) rows * sub * 8;
 }
 
+size_t gpuq_xtx_scratch_bytes(int src, int64_t rows, int64_t dim, int scaled) {
+    if ((src != SRC_F32 && src != SRC_BF16) || rows <= 0 || dim <= 0) return 0;
+    return xtx_scratch_bytes(src, rows, dim, scaled != 0);
+}
+
+size_t gpuq_xtx_dev(int src, const void * d_x, int64_t ld_x, const float * d_scale, int64_t rows, int64_t dim, double * d_h,
+                    int accumulate, void * d_scratch, size_t scratch_bytes, void * stream) {
+    const size_t need = gpuq_xtx_scratch_bytes(src, rows, dim, d_scale != nullptr);
+    const size_t esz = src == SRC_BF16 ? 2 : 4;
+    if (!need || !d_x || !d_h || !d_scratch || ld_x < dim || scratch_bytes < need || misaligned(d_scratch, 16) ||
+        misaligned(d_x, esz) || misaligned(d_h, 8) || misaligned(d_scale, 4)) {
+        set_err("gpuq_xtx_dev: bad arguments (source 0 (F32) or 30 (BF16), ld_x >= dim, scratch of "
+                "gpuq_xtx_scratch_bytes bytes, 16-byte aligned)");
+        return 0;
+    }
+    Device * d = current_device();
+    if (!d) { set_err("gpuq_xtx_dev: current device not initialized"); return 0; }
+    const cudaError_t e = launch_xtx(src, d_x, ld_x, d_scale, rows, dim, d_h, accumulate != 0, d_scratch, scratch_bytes,
+                                     d->status, (cudaStream_t) stream);
+    if (e != cudaSuccess) { set_err("gpuq_xtx_dev: launch failed: %s", cudaGetErrorString(e)); return 0; }
+    return (size_t) rows * dim * esz;
+}
+
 size_t gpuq_dequantize_src_dev(int src, const void * d_raw, float * d_out, int64_t n, void * stream) {
     const int sl = src_block_len(src);
     if (!sl || n <= 0 || n % sl || n % 32 || !d_raw || !d_out) { set_err("gpuq_dequantize_src_dev: bad arguments"); return 0; }

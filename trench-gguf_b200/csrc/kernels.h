@@ -49,6 +49,12 @@ cudaError_t launch_ldlq_update(const double * Es, const double * U, float * W, i
 cudaError_t launch_sub_weff(const float * blk, const float * qw, int64_t qw_div, float * weff, int64_t rows, cudaStream_t st);
 cudaError_t launch_sub_points(const float * blk, const float * weff, uint8_t * q, double * err, int64_t rows, int sub,
                               int c0, int scale_search, const uint64_t * grid, cudaStream_t st);
+// H += X^T X on the tensor cores (xtx.cu): X [rows][ld] float32 or bf16, optional row scale, float32-accurate sums
+// added in float64 to H [dim][dim]; scratch: the bf16 parts of X laid out as tensor-core operands
+int xtx_parts(int src, bool scaled);
+size_t xtx_scratch_bytes(int src, int64_t rows, int64_t dim, bool scaled);
+cudaError_t launch_xtx(int src, const void * x, int64_t ldx, const float * scale, int64_t rows, int64_t dim, double * H,
+                       int accumulate, void * scratch, size_t scratch_bytes, unsigned * status, cudaStream_t st);
 // n values of any readable source (common.cuh src_block_len) -> n floats; tab: the dequant grid of an i-quant source
 cudaError_t launch_decode(int src, const void * raw, float * out, int64_t n, DequantTab tab, cudaStream_t st);
 // the same, value i (of this pass; value v0 + i of the tensor) multiplied by scale[(v0 + i) / per_mat] when scale
