@@ -72,6 +72,9 @@ def parse():
     ap.add_argument("--ldlq-streams", type=int, default=4,
                     help="config 5: CUDA streams the experts alternate over (the next expert's factorisation runs "
                          "beside this one's loop); 1 = one expert after another on one stream")
+    ap.add_argument("--ldlq-sub", type=int, default=0, choices=[0, 32, 8],
+                    help="config 5: the IQ2_XXS sub-block variant (feedback every 32 or 8 columns)")
+    ap.add_argument("--scale-search", type=int, default=0, help="config 5 with --ldlq-sub 32: sub-block scales tried")
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5],
                     help="2 (default): the metric's own workload; 1, 3, 4, 5: the other benchmark configurations, "
                          "one GPU, one JSON line each (measurement modes beside the contract)")
@@ -476,6 +479,23 @@ def ldlq_flops(ne1, ne0, bs=256):
     return {"cholesky": ne0 ** 3 / 3, "triangular_inverse": ne0 ** 3 / 3, "loop": float(loop)}
 
 
+def hessian_line(hess_ms, torch_ms, h_err, n, ne0):
+    """the Hessian build's figures: ms an expert (the kernel's three launches: parts, products, mirror), the
+    reference's torch recipe on the same rows, and the tensor-core roofline: six bf16 products of the three-part split
+    over the d (d + 1) / 2 elements of the upper triangle, 2 n flop each, against the measured bf16 peak"""
+    ms = statistics.median(hess_ms)
+    flop = 6 * 2 * n * ne0 * (ne0 + 1) / 2
+    peak = load_json(os.path.join("..", "MEASURED_PEAKS.json")).get("bf16_tflops")
+    tf = flop / (ms / 1e3) / 1e12
+    return {"ms_per_expert": ms, "torch_float32_ms": torch_ms,
+            "speedup_vs_torch": (torch_ms / ms) if torch_ms else None,
+            "error_over_sum_abs_terms": h_err,
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s",
+                         "frac": tf / peak if peak else None, "flop_per_expert": flop,
+                         "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst), of measured",
+                         "float32_equivalent_tflops": 2 * n * ne0 * ne0 / (ms / 1e3) / 1e12}}
+
+
 def run_ldlq(args, g, dev, stream, fp32, rank=0, world=1, dist=None):
     """config 5: LDLQ re-quantization of experts 2048 x 7168 to IQ2_XXS, each with its own Hessian built from n = 4096
     activation rows X = (Z + A B) diag(g) (rank-32 structure, lognormal gains) by tools/hessian_from_dump.py:73-79's
@@ -487,13 +507,15 @@ def run_ldlq(args, g, dev, stream, fp32, rank=0, world=1, dist=None):
     block quantizer) on rank 0."""
     import torch
     import ldlq_gpu
+    import hessian_gpu
     E = args.experts if args.experts != EXPERTS_PER_GPU else 8
     n, rk, ne1, ne0 = 4096, 32, ROWS, COLS
     gen = torch.Generator(device=dev).manual_seed(105 + 1000 * rank)
     torch.backends.cuda.matmul.allow_tf32 = False       # (the reference's float32 GEMM is a full float32 one)
     gqt = ldlq_gpu.GpuQuant(g.lib, 16)
+    xtx = hessian_gpu.Xtx(g.lib, dev)
     Hs, ims, Ws = [], [], []
-    hess_ms = 0.0
+    hess_ms, torch_ms, h_err = [], None, None
     for e in range(E):
         Z = torch.randn(n, ne0, device=dev, generator=gen)
         A = torch.randn(n, rk, device=dev, generator=gen)
@@ -501,15 +523,33 @@ def run_ldlq(args, g, dev, stream, fp32, rank=0, world=1, dist=None):
         gain = torch.exp(torch.randn(ne0, device=dev, generator=gen))
         X = (Z + A @ B) * gain[None]
         del Z, A, B
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        H = torch.zeros(ne0, ne0, dtype=torch.float64, device=dev)
-        for c0 in range(0, n, 1024):                     # row chunks: float32 X^T X, float64 accumulation
-            xc = X[c0:c0 + 1024]
-            H += (xc.T @ xc).double()
-        b.record()
-        torch.cuda.synchronize()
-        hess_ms += a.elapsed_time(b)
+        # H = X^T X by the tensor-core kernel, the reference's 8192-row chunks (here one), timed on its own as input
+        # preparation (not part of the step)
+        reps = 3 if e == 0 else 1
+        for _ in range(reps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            H = xtx(((X[c0:c0 + 8192], None) for c0 in range(0, n, 8192)), ne0)
+            b.record()
+            torch.cuda.synchronize()
+        hess_ms.append(a.elapsed_time(b))
+        if e == 0 and rank == 0:
+            # the reference's own recipe (tools/hessian_from_dump.py:73-79: torch float32 GEMMs, float64 sum), timed
+            # for comparison, and both against the float64 product
+            for _ in range(2):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                Ht = torch.zeros(ne0, ne0, dtype=torch.float64, device=dev)
+                for c0 in range(0, n, 8192):
+                    xc = X[c0:c0 + 8192]
+                    Ht += (xc.T @ xc).double()
+                b.record()
+                torch.cuda.synchronize()
+            torch_ms = a.elapsed_time(b)
+            Xd = X.double()
+            want, bound = Xd.T @ Xd, Xd.abs().T @ Xd.abs()
+            h_err = {"kernel": float(((H - want).abs() / bound).max()), "torch_f32_gemm": float(((Ht - want).abs() / bound).max())}
+            del Xd, want, bound, Ht
         Hs.append(H)
         ims.append((torch.diagonal(H) / n).float()[None].contiguous())
         Ws.append((torch.distributions.StudentT(5.0).sample((1, ne1, ne0)).to(dev) * 0.02 / (5.0 / 3.0) ** 0.5).float())
@@ -525,6 +565,9 @@ def run_ldlq(args, g, dev, stream, fp32, rank=0, world=1, dist=None):
         facs = [ldlq_gpu.factor_hessian(Hs[e], n, device=dev, U_out=U[e]) for e in range(E)]
         if mid is not None:
             mid.record()
+        if args.ldlq_sub:
+            return ldlq_gpu.ldlq_groups_iq2xxs_sub(Wc, facs, gqt, ims, sub=args.ldlq_sub, scale_search=args.scale_search,
+                                                   U_stack=U)
         return ldlq_gpu.ldlq_groups(Wc, facs, gqt, ims, U_stack=U)
     step()                                               # warm-up: cuSOLVER / cuBLAS handles, the kernels' code
     torch.cuda.synchronize()
@@ -563,13 +606,20 @@ def run_ldlq(args, g, dev, stream, fp32, rank=0, world=1, dist=None):
         t0 = time.perf_counter()
         quant, dequant, tsize = LO.checker_quant(chk, 16, threads=os.cpu_count() or 1)
         U, perm, _, _ = LO.prepare_hessian(H0, n, damp=0.01)
-        want, deq_w = LO.quantize_matrix(W0, quant, dequant, tsize, U=U, perm=perm, imatrix=im0, feedback=True)
-        cpu_s = time.perf_counter() - t0
         got = outs[0].cpu().numpy()[0]
+        if args.ldlq_sub:   # (rows are independent given U: the first 256 rows, the restatement being numpy-vectorised)
+            W0, got, rows_checked = W0[:256], got[:256], 256
+            want, deq_w = LO.quantize_matrix_iq2xxs_sub(W0, quant, LO.iq2xxs_grid(chk), U, perm, im0, sub=args.ldlq_sub,
+                                                        scale_search=args.scale_search)
+        else:
+            rows_checked = ne1
+            want, deq_w = LO.quantize_matrix(W0, quant, dequant, tsize, U=U, perm=perm, imatrix=im0, feedback=True)
+        cpu_s = time.perf_counter() - t0
         same, nb = block_parity(got, want, tsize)
-        deq = chk.dequantize(16, got).reshape(ne1, ne0)
+        deq = chk.dequantize(16, got).reshape(rows_checked, ne0)
         lw, lg = LO.proxy_loss(W0, deq_w, H0, n), LO.proxy_loss(W0, deq, H0, n)
         parity = {"blocks": nb, "identical": same, "share": same / nb, "proxy_loss_rel_diff": abs(lg - lw) / lw,
+                  "rows_checked": rows_checked,
                   "checker": "the reference loop restated (oracle/ldlq_oracle.py, float64) with %s" % (
                       "the reference's host block quantizer" if kind == "reference" else "the C restatement"),
                   "cpu_s": cpu_s}
@@ -581,9 +631,11 @@ def run_ldlq(args, g, dev, stream, fp32, rank=0, world=1, dist=None):
             "n_gpus": world, "steps": len(times), "warmup": 1, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "dtype": "f32 weights, f64 factor and feedback", "data": "synthetic (config 5, seeded)",
             "config": {"workload": "config 5: %d experts a GPU, 2048 x 7168 -> IQ2_XXS, own Hessian each (7168^2 from "
-                                   "4096 rows), act order seq, imatrix weights; factor + lockstep loop" % E,
+                                   "4096 rows), act order seq, imatrix weights; factor + lockstep loop%s" % (
+                                       E, "" if not args.ldlq_sub else "; the sub-block variant, feedback every %d "
+                                       "columns, scale search %d" % (args.ldlq_sub, args.scale_search)),
                        "parallelism": "expert-sharded x%d" % world},
-            "per_expert_ms": ms / E, "hessian_build_ms_per_expert": hess_ms / E,
+            "per_expert_ms": ms / E, "hessian_build": hessian_line(hess_ms, torch_ms, h_err, n, ne0),
             "phases_ms": {"factor_all_experts": fms, "lockstep_loop_all_experts": ms - fms},
             "roofline": {"bound": "fp64", "achieved": total_fl / (ms / 1e3) / 1e12, "peak": peak64, "unit": "TFLOP/s",
                          "frac": total_fl / (ms / 1e3) / 1e12 / peak64, "flop_per_expert": fl,
