@@ -149,6 +149,14 @@ size_t gpuq_ldlq_sub_weff_dev(const float * d_blk, const float * d_qw, int64_t q
 size_t gpuq_ldlq_sub_points_dev(const float * d_blk, const float * d_weff, void * d_q, double * d_err, int64_t rows, int sub,
                                 int c0, int scale_search, void * stream);
 
+/* LDLQ's triangular inverse as products on the float64 tensor-core path: C = alpha A B (+ beta C, beta != 0),
+ * row-major float64 A [M][lda], B [K][ldb], C [M][ldc]; tri 1: B is lower-triangular (K == N) and tri 2: A is
+ * lower-triangular (K == M) - the blocks of the product the triangle makes zero are skipped; tri 0: a full product.
+ * K, N, lda, ldb even; A and B 16-byte aligned. On `stream`, no synchronisation; returns the bytes of C written, 0 on
+ * a bad argument. No counterpart in the reference (its factorisation is torch's cholesky_inverse). */
+size_t gpuq_dgemm_dev(int tri, int64_t M, int64_t N, int64_t K, double alpha, const double * d_a, int64_t lda,
+                      const double * d_b, int64_t ldb, double beta, double * d_c, int64_t ldc, void * stream);
+
 /* The Hessian of a layer's inputs on the tensor cores: H = (S X)^T (S X) (accumulate 0) or H += (S X)^T (S X)
  * (accumulate 1), the float32 GEMM a row chunk of
  * tools/hessian_from_dump.py:73-79 (`_xtx`: `H += (xc.T @ xc).double()`) for one chunk as one call.

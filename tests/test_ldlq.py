@@ -232,6 +232,52 @@ def test_gpu_feedback_kernels_against_torch(tables, kd):
     assert g.lib.gpuq_ldlq_scale_dev(E.data_ptr(), Rd.data_ptr(), Es.data_ptr(), P, M, nsteps, kd, nsteps, st) == 0
 
 
+@pytest.mark.gpu
+@pytest.mark.parametrize("tri,M,N,K", [(0, 300, 130, 96), (1, 200, 512, 512), (2, 384, 66, 384), (1, 1000, 768, 768),
+                                       (2, 1536, 1536, 1536)])
+def test_gpu_dgemm_against_torch(tables, tri, M, N, K):
+    """gpuq_dgemm_dev (the triangular inverse's products on the float64 tensor-core path) against torch's float64
+    product: a full product, B lower-triangular, A lower-triangular (the skipped blocks are the triangle's zeros),
+    sub-matrices with their row strides, ragged tiles; to float64 rounding"""
+    torch, G, ldlq_gpu, g = _gpu_setup(tables)
+    dev = torch.device("cuda")
+    gen = torch.Generator(device=dev).manual_seed(M + N + K)
+    A = torch.randn(M, K + 6, dtype=torch.float64, device=dev, generator=gen)[:, 2:K + 2]   # (row stride K + 6)
+    B = torch.randn(K, N, dtype=torch.float64, device=dev, generator=gen)
+    if tri == 1:
+        B = torch.tril(B)
+    if tri == 2:
+        A = torch.tril(torch.randn(M, K, dtype=torch.float64, device=dev, generator=gen))
+    C = torch.full((M, N), float("nan"), dtype=torch.float64, device=dev)
+    ldlq_gpu._dgemm(tri, A, B, C, alpha=-0.5)
+    want = -0.5 * (A @ B)
+    torch.cuda.synchronize()
+    scale = (A.abs() @ B.abs()).max()
+    assert float((C - want).abs().max()) <= 1e-13 * float(scale)
+    st = torch.cuda.current_stream().cuda_stream
+    assert g.lib.gpuq_dgemm_dev(3, M, N, K, 1.0, A.data_ptr(), A.stride(0), B.data_ptr(), N, 0.0, C.data_ptr(), N, st) == 0
+    assert g.lib.gpuq_dgemm_dev(0, M, N, K, 1.0, A.data_ptr() + 8, A.stride(0), B.data_ptr(), N, 0.0, C.data_ptr(), N,
+                                st) == 0
+
+
+@pytest.mark.gpu
+def test_gpu_lower_inverse(tables):
+    """the GPU triangular inverse by halves (own float64 products) against a triangular solve of the identity, on a
+    well-conditioned lower factor of 2,560 columns (three levels of halving)"""
+    torch, G, ldlq_gpu, g = _gpu_setup(tables)
+    dev = torch.device("cuda")
+    gen = torch.Generator(device=dev).manual_seed(21)
+    m = 2560
+    X = torch.randn(m, m, dtype=torch.float64, device=dev, generator=gen)
+    L = torch.linalg.cholesky(X @ X.T / m + torch.eye(m, dtype=torch.float64, device=dev)).contiguous()
+    out = torch.empty_like(L)
+    ldlq_gpu._lower_inverse(L, out)
+    want = torch.linalg.solve_triangular(L, torch.eye(m, dtype=torch.float64, device=dev), upper=False)
+    torch.cuda.synchronize()
+    assert torch.equal(torch.triu(out, 1), torch.zeros_like(out))
+    assert float((out - want).abs().max()) <= 1e-11 * float(want.abs().max())
+
+
 def _sub_case(rows, ne0, seed):
     """weights with a zero row (ggml's d = 0) and a row of large outliers; an imatrix with a dead column"""
     rng = np.random.default_rng(seed)

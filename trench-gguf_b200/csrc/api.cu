@@ -743,6 +743,20 @@ size_t gpuq_ldlq_sub_points_dev(const float * d_blk, const float * d_weff, void 
     return (size_t) rows * sub * 8;
 }
 
+size_t gpuq_dgemm_dev(int tri, int64_t M, int64_t N, int64_t K, double alpha, const double * d_a, int64_t lda,
+                      const double * d_b, int64_t ldb, double beta, double * d_c, int64_t ldc, void * stream) {
+    if (tri < 0 || tri > 2 || M <= 0 || N <= 0 || K <= 0 || !d_a || !d_b || !d_c || (K & 1) || (N & 1) || (lda & 1) ||
+        (ldb & 1) || lda < K || ldb < N || ldc < N || (tri == 1 && K != N) || (tri == 2 && K != M) ||
+        misaligned(d_a, 16) || misaligned(d_b, 16) || misaligned(d_c, 8)) {
+        set_err("gpuq_dgemm_dev: bad arguments (tri 0, 1 (B lower, K == N) or 2 (A lower, K == M); K, N, lda, ldb even; "
+                "A and B 16-byte aligned)");
+        return 0;
+    }
+    const cudaError_t e = launch_dgemm(tri, d_a, lda, d_b, ldb, d_c, ldc, M, N, K, alpha, beta, (cudaStream_t) stream);
+    if (e != cudaSuccess) { set_err("gpuq_dgemm_dev: launch failed: %s", cudaGetErrorString(e)); return 0; }
+    return (size_t) M * N * 8;
+}
+
 size_t gpuq_xtx_scratch_bytes(int src, int64_t rows, int64_t dim, int scaled) {
     if ((src != SRC_F32 && src != SRC_BF16) || rows <= 0 || dim <= 0) return 0;
     return xtx_scratch_bytes(src, rows, dim, scaled != 0);

@@ -150,6 +150,96 @@ __global__ void __launch_bounds__(UTHREADS, 2) k_ldlq_gemm(const double * __rest
     }
 }
 
+// C = alpha A B (+ beta C), float64 row-major (A [M][lda], B [K][ldb], C [M][ldc]), on the same tiles as
+// k_ldlq_gemm with a K range per tile: TRI_NONE every k; TRI_B_LOWER B lower-triangular (B[k][n] = 0 for k < n: an
+// N-tile starting at n0 needs k >= n0); TRI_A_LOWER A lower-triangular (A[m][k] = 0 for k > m: an M-tile ending at
+// m1 needs k < m1). The triangular factor's own triangle is read as stored (its zeros included), so the sums are
+// a full product's, in the same order, skipping only the blocks that are zero.
+template <int TRI>
+__global__ void __launch_bounds__(UTHREADS, 2) k_dgemm(const double * __restrict__ A, int64_t lda,
+                                                       const double * __restrict__ B, int64_t ldb, double * C, int64_t ldc,
+                                                       int64_t M, int64_t N, int64_t K, double alpha, double beta) {
+    using SM = UpdSmem<UBK>;
+    constexpr int KC = UBK, APAD = SM::APAD;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    SM & sm = *reinterpret_cast<SM *>(smem_raw);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int wm = warp >> 1, wn = warp & 1;
+    const int64_t m0 = (int64_t) blockIdx.y * UBM, n0 = (int64_t) blockIdx.x * UBN;
+    int64_t k_lo = 0, k_hi = K;
+    if (TRI == 1) k_lo = n0 / KC * KC;
+    if (TRI == 2) k_hi = m0 + UBM < K ? m0 + UBM : K;
+    const int64_t nkt = k_hi > k_lo ? (k_hi - k_lo + KC - 1) / KC : 0;
+
+    auto load = [&](int stage, int64_t kk) {
+#pragma unroll
+        for (int i = tid; i < UBM * (KC / 2); i += UTHREADS) {
+            const int r = i / (KC / 2), ch = i % (KC / 2);
+            double * dst = &sm.a[stage][r * APAD + ch * 2];
+            if (m0 + r < M && kk + ch * 2 < K) cp_async16(dst, A + (m0 + r) * lda + kk + ch * 2);
+            else { dst[0] = 0.0; dst[1] = 0.0; }
+        }
+#pragma unroll
+        for (int i = tid; i < KC * (UBN / 2); i += UTHREADS) {
+            const int r = i / (UBN / 2), ch = i % (UBN / 2);
+            double * dst = &sm.b[stage][r * BPAD + ch * 2];
+            if (kk + r < K && n0 + ch * 2 < N) cp_async16(dst, B + (kk + r) * ldb + n0 + ch * 2);
+            else { dst[0] = 0.0; dst[1] = 0.0; }
+        }
+    };
+
+    double acc[4][4][2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j][0] = acc[i][j][1] = 0.0;
+    if (nkt > 0) {
+        load(0, k_lo);
+        cp_commit();
+    }
+#pragma unroll 1
+    for (int64_t kt = 0; kt < nkt; ++kt) {
+        if (kt + 1 < nkt) {
+            load((int) ((kt + 1) & 1), k_lo + (kt + 1) * KC);
+            cp_commit();
+            cp_wait<1>();
+        } else {
+            cp_wait<0>();
+        }
+        __syncthreads();
+        const double * As = sm.a[kt & 1] + (wm * 32 + (lane >> 2)) * APAD + (lane & 3);
+        const double * Bs = sm.b[kt & 1] + (lane & 3) * BPAD + wn * 32 + (lane >> 2);
+#pragma unroll
+        for (int kq = 0; kq < KC / 4; ++kq) {
+            double a[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) a[i] = As[i * 8 * APAD + kq * 4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) b[j] = Bs[kq * 4 * BPAD + j * 8];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) dmma_8x8x4(acc[i][j], a[i], b[j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int64_t row = m0 + wm * 32 + i * 8 + (lane >> 2);
+        if (row >= M) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int64_t col = n0 + wn * 32 + j * 8 + (lane & 3) * 2;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                if (col + h >= N) continue;
+                double * c = C + row * ldc + col + h;
+                *c = beta != 0.0 ? alpha * acc[i][j][h] + beta * *c : alpha * acc[i][j][h];
+            }
+        }
+    }
+}
+
 }  // namespace
 
 template <bool SUB, int KD>
@@ -190,6 +280,31 @@ cudaError_t launch_ldlq_update(const double * Es, const double * U, float * W, i
         case 8:   return launch_gemm<true, 8>(Es, B, ne0 * ne0, ne0, c1, ne0, W, ngroups, rows, st);
         default: return cudaErrorInvalidValue;
     }
+}
+
+}  // namespace gq
+
+namespace gq {
+
+cudaError_t launch_dgemm(int tri, const double * A, int64_t lda, const double * B, int64_t ldb, double * C, int64_t ldc,
+                         int64_t M, int64_t N, int64_t K, double alpha, double beta, cudaStream_t st) {
+    if (M <= 0 || N <= 0 || K <= 0 || tri < 0 || tri > 2) return cudaErrorInvalidValue;
+    const size_t smem = sizeof(UpdSmem<UBK>);
+    const dim3 grid((unsigned) ((N + UBN - 1) / UBN), (unsigned) ((M + UBM - 1) / UBM));
+    if (grid.y > 65535) return cudaErrorInvalidValue;
+    cudaError_t e = cudaSuccess;
+    switch (tri) {
+        case 0: e = cudaFuncSetAttribute(k_dgemm<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+                if (e == cudaSuccess) k_dgemm<0><<<grid, UTHREADS, smem, st>>>(A, lda, B, ldb, C, ldc, M, N, K, alpha, beta);
+                break;
+        case 1: e = cudaFuncSetAttribute(k_dgemm<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+                if (e == cudaSuccess) k_dgemm<1><<<grid, UTHREADS, smem, st>>>(A, lda, B, ldb, C, ldc, M, N, K, alpha, beta);
+                break;
+        default: e = cudaFuncSetAttribute(k_dgemm<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+                 if (e == cudaSuccess) k_dgemm<2><<<grid, UTHREADS, smem, st>>>(A, lda, B, ldb, C, ldc, M, N, K, alpha, beta);
+                 break;
+    }
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 }  // namespace gq

@@ -29,7 +29,8 @@ SYMBOLS = ("gpuq_init", "gpuq_block_bytes", "gpuq_can_quantize", "gpuq_quantize"
            "gpuq_last_error", "gpuq_status", "gpuq_init_devices", "gpuq_device_count", "gpuq_requantize_dev",
            "gpuq_requantize_noalloc", "gpuq_dequantize_error_dev", "gpuq_ldlq_scale_dev",
            "gpuq_ldlq_update_dev", "gpuq_requantize_scaled_batch", "gpuq_check_q8_rounding",
-           "gpuq_ldlq_sub_weff_dev", "gpuq_ldlq_sub_points_dev", "gpuq_xtx_scratch_bytes", "gpuq_xtx_dev")
+           "gpuq_ldlq_sub_weff_dev", "gpuq_ldlq_sub_points_dev", "gpuq_xtx_scratch_bytes", "gpuq_xtx_dev",
+           "gpuq_dgemm_dev")
 
 
 class GpuqError(RuntimeError):
@@ -75,6 +76,7 @@ def declare(gq):
         "gpuq_ldlq_scale_dev": (sz, [vp, vp, vp, i64, i64, i64, i64, i64, vp]),
         "gpuq_ldlq_sub_weff_dev": (sz, [vp, vp, i64, vp, i64, vp]),
         "gpuq_xtx_scratch_bytes": (sz, [c.c_int, i64, i64, c.c_int]),
+        "gpuq_dgemm_dev": (sz, [c.c_int, i64, i64, i64, c.c_double, vp, i64, vp, i64, c.c_double, vp, i64, vp]),
         "gpuq_xtx_dev": (sz, [c.c_int, vp, i64, vp, i64, i64, vp, c.c_int, vp, sz, vp]),
         "gpuq_ldlq_sub_points_dev": (sz, [vp, vp, vp, vp, i64, c.c_int, c.c_int, c.c_int, vp]),
         "gpuq_requantize_scaled_batch": (sz, [c.c_int, vp, c.c_int, vp, i64, i64, i64, vp, vp]),

@@ -129,90 +129,77 @@ def _trmm_left_lower(T, B, leaf):
     return _torch().cat([top, bot], 0)
 
 
-class _Trmm:
-    """cuBLAS's float64 triangular-times-full product (cublasDtrmm: a plain library call), bound with ctypes to the
-    cuBLAS that torch has loaded, one handle a device. Row-major torch matrices are column-major transposes, so
-    B @ T (T lower) is the column-major T^T B^T with an upper T^T on the left, and T @ B is B^T T^T on the right."""
-    _handles = {}
-
-    def __init__(self):
-        import ctypes
-        import glob
-        import os
-        torch = _torch()
-        base = os.path.join(os.path.dirname(torch.__file__), "..", "nvidia", "cublas", "lib")
-        paths = sorted(glob.glob(os.path.join(base, "libcublas.so*")))
-        if not paths:
-            raise RuntimeError("cuBLAS library not found beside torch")
-        c = ctypes
-        self.c = c
-        self.lib = c.CDLL(paths[0])
-        self.lib.cublasCreate_v2.argtypes = [c.POINTER(c.c_void_p)]
-        self.lib.cublasSetStream_v2.argtypes = [c.c_void_p, c.c_void_p]
-        self.lib.cublasDtrmm_v2.argtypes = [c.c_void_p, c.c_int, c.c_int, c.c_int, c.c_int, c.c_int, c.c_int,
-                                            c.POINTER(c.c_double), c.c_void_p, c.c_int, c.c_void_p, c.c_int,
-                                            c.c_void_p, c.c_int]
-
-    def _handle(self, dev):
-        h = self._handles.get(dev)
-        if h is None:
-            h = self.c.c_void_p()
-            if self.lib.cublasCreate_v2(self.c.byref(h)) != 0:
-                raise RuntimeError("cublasCreate failed")
-            self._handles[dev] = h
-        if self.lib.cublasSetStream_v2(h, self.c.c_void_p(_stream())) != 0:
-            raise RuntimeError("cublasSetStream failed")
-        return h
-
-    def _call(self, side, T, B, C, m, n, alpha):
-        for t in (T, B, C):
-            assert t.dtype == _torch().float64 and t.is_cuda and t.stride(1) == 1
-        h = self._handle(T.device.index)
-        a = self.c.c_double(alpha)
-        rc = self.lib.cublasDtrmm_v2(h, side, 1, 0, 0, m, n, self.c.byref(a), T.data_ptr(), T.stride(0), B.data_ptr(),
-                                     B.stride(0), C.data_ptr(), C.stride(0))
-        if rc != 0:
-            raise RuntimeError("cublasDtrmm failed (%d)" % rc)
-
-    def right_lower(self, B, T, C, alpha=1.0):
-        """C = alpha B @ T, T lower-triangular (h x h), B (m x h)"""
-        self._call(0, T, B, C, T.shape[0], B.shape[0], alpha)
-
-    def left_lower(self, T, B, C, alpha=1.0):
-        """C = alpha T @ B, T lower-triangular (h x h), B (h x n)"""
-        self._call(1, T, B, C, B.shape[1], T.shape[0], alpha)
+_LIB = []
 
 
-_TRMM = []
+def _lib():
+    """this library's handle for the device-independent entry points (gpuq_dgemm_dev needs no gpuq_init)"""
+    if not _LIB:
+        _LIB.append(G.open_library())
+    return _LIB[0]
+
+
+def _dgemm(tri, A, B, C, alpha=1.0):
+    """C = alpha A @ B on this library's float64 tensor-core GEMM (row-major float64 device matrices, row strides as
+    they lie), the zero blocks of a lower-triangular B (tri 1) or A (tri 2) skipped"""
+    torch = _torch()
+    for t in (A, B, C):
+        assert t.dtype == torch.float64 and t.is_cuda and t.stride(1) == 1
+    M, K = A.shape
+    N = B.shape[1]
+    got = _lib().gpuq_dgemm_dev(tri, M, N, K, alpha, A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0), 0.0,
+                                C.data_ptr(), C.stride(0), torch.cuda.current_stream(A.device).cuda_stream)
+    if got != M * N * 8:
+        raise RuntimeError("gpuq_dgemm_dev: " + _lib().gpuq_last_error().decode())
+
+
+def _split(lo, hi, leaf, nodes, leaves):
+    """the halving tree of [lo, hi): internal nodes (lo, h, hi) deepest last, leaves (lo, hi); h a multiple of 256"""
+    m = hi - lo
+    if m <= leaf:
+        leaves.append((lo, hi))
+        return
+    h = lo + (m // 2 + QK - 1) // QK * QK
+    nodes.append((lo, h, hi))
+    _split(lo, h, leaf, nodes, leaves)
+    _split(h, hi, leaf, nodes, leaves)
 
 
 def _lower_inverse(L, out, leaf=512):
-    """out = L^-1 for a lower-triangular L, by halves: [[A, 0], [B, C]]^-1 = [[A^-1, 0], [-C^-1 B A^-1, C^-1]]; the
-    off-diagonal block two triangular-times-full products (cuBLAS dtrmm on the GPU; n^3/3 multiply-adds in all, as a
-    triangular inverse), the leaves triangular solves against the identity"""
+    """out = L^-1 for a lower-triangular L, by halves: [[A, 0], [B, C]]^-1 = [[A^-1, 0], [-C^-1 B A^-1, C^-1]].
+    The leaves (diagonal blocks of at most `leaf` columns) are inverted together, one batched triangular solve
+    against the identity a leaf size; the tree's nodes are then closed bottom-up, each off-diagonal block two
+    triangular-times-full products (on the GPU this library's float64 tensor-core GEMM with the triangle's zero
+    blocks skipped: n^3/3 multiply-adds in all, as a triangular inverse)"""
     torch = _torch()
-    m = L.shape[0]
-    if m <= leaf:
-        out.copy_(torch.linalg.solve_triangular(L, torch.eye(m, dtype=L.dtype, device=L.device), upper=False))
-        return
     if L.stride(1) != 1 or out.stride(1) != 1:   # (the triangular products want row-major operands)
         res = torch.empty(out.shape, dtype=out.dtype, device=out.device)
         _lower_inverse(L.contiguous(), res, leaf)
         out.copy_(res)
         return
-    h = (m // 2 + QK - 1) // QK * QK
-    _lower_inverse(L[:h, :h], out[:h, :h], leaf)
-    _lower_inverse(L[h:, h:], out[h:, h:], leaf)
-    out[:h, h:].zero_()
-    if L.is_cuda and L.dtype == torch.float64:
-        if not _TRMM:
-            _TRMM.append(_Trmm())
-        t = torch.empty((m - h, h), dtype=L.dtype, device=L.device)
-        _TRMM[0].right_lower(L[h:, :h], out[:h, :h], t)              # B A^-1
-        _TRMM[0].left_lower(out[h:, h:], t, out[h:, :h], -1.0)      # -C^-1 (B A^-1)
-        return
-    x = _trmm_left_lower(out[h:, h:], _trmm_right_lower(L[h:, :h], out[:h, :h], leaf), leaf)
-    out[h:, :h].copy_(x.neg_())
+    m = L.shape[0]
+    nodes, leaves = [], []
+    _split(0, m, leaf, nodes, leaves)
+    for size in sorted({hi - lo for lo, hi in leaves}):
+        group = [(lo, hi) for lo, hi in leaves if hi - lo == size]
+        blocks = torch.stack([L[lo:hi, lo:hi] for lo, hi in group])
+        eye = torch.eye(size, dtype=L.dtype, device=L.device).expand(len(group), size, size)
+        inv = torch.linalg.solve_triangular(blocks, eye, upper=False)
+        for (lo, hi), b in zip(group, inv):
+            out[lo:hi, lo:hi] = b
+    gpu = L.is_cuda and L.dtype == torch.float64
+    for lo, h, hi in reversed(nodes):             # children before parents
+        out[lo:h, h:hi].zero_()
+        if gpu:
+            t = torch.empty((hi - h, h - lo), dtype=L.dtype, device=L.device)
+            _dgemm(1, L[h:hi, lo:h], out[lo:h, lo:h], t)                  # B A^-1 (A^-1 lower)
+            _dgemm(2, out[h:hi, h:hi], t, out[h:hi, lo:h], -1.0)          # -C^-1 (B A^-1) (C^-1 lower)
+        else:
+            x = _trmm_left_lower(out[h:hi, h:hi], _trmm_right_lower(L[h:hi, lo:h], out[lo:h, lo:h], leaf), leaf)
+            out[h:hi, lo:h].copy_(x.neg_())
+    # (the blocks above the diagonal of the leaves' own rows were never written by a node: zero them)
+    for lo, hi in leaves:
+        out[lo:hi, hi:].zero_()
 
 
 class Factor:
