@@ -1141,19 +1141,19 @@ static int o_q8_0(const float * x, uint8_t * y) {   /* gpuq.hip:1831-1838 */
 }
 
 /* ------------------------------------------------------------------------------------------------ dispatch */
-enum { O_Q4_0 = 2, O_Q5_0 = 6, O_Q5_1 = 7 };
+enum { O_F16 = 1, O_Q4_0 = 2, O_Q5_0 = 6, O_Q5_1 = 7 };
 static int o_is_legacy(int t) { return t == O_Q4_0 || t == O_Q5_0 || t == O_Q5_1; }
 
 static size_t o_bytes(int type) {
     switch (type) {
-        case O_Q4_0: return 18; case O_Q5_0: return 22; case O_Q5_1: return 24;
+        case O_F16: return 2; case O_Q4_0: return 18; case O_Q5_0: return 22; case O_Q5_1: return 24;
         case O_IQ2_XXS: return 66; case O_IQ2_XS: return 74; case O_IQ2_S: return 82; case O_IQ3_XXS: return 98;
         case O_IQ3_S: return 110; case O_IQ1_S: return 50; case O_IQ1_M: return 56; case O_IQ4_NL: return 18;
         case O_IQ4_XS: return 136; case O_Q2_K: return 84; case O_Q3_K: return 110; case O_Q4_K: return 144;
         case O_Q5_K: return 176; case O_Q6_K: return 210; case O_Q8_0: return 34; default: return 0;
     }
 }
-static int o_len(int type) { return type == O_IQ4_NL || type == O_Q8_0 || o_is_legacy(type) ? 32 : QK; }
+static int o_len(int type) { return type == O_F16 ? 1 : type == O_IQ4_NL || type == O_Q8_0 || o_is_legacy(type) ? 32 : QK; }
 
 /* ------------------------------------------------------------------------------------------------ Q4_0, Q5_0, Q5_1
  * llama-quantize's fallbacks for rows a k-quant or i-quant cannot hold (tools/requant_experts.py:181-183; the
@@ -1460,6 +1460,12 @@ size_t orc_quantize_batch(int type, const float * x, void * y, int64_t nmat, int
     const int bs = o_len(type);
     if (!o_bytes(type) || nmat <= 0 || nrow <= 0 || n_per_row % bs) return 0;
     const int64_t nb_row = n_per_row / bs, nb_mat = nrow * nb_row;
+    if (type == O_F16) {   /* ggml_quantize_chunk's F16: ggml_fp32_to_fp16_row, value by value (the imatrix unused) */
+        (void) nthreads;
+        uint16_t * h = (uint16_t *) y;
+        for (int64_t i = 0; i < nmat * nb_mat; ++i) h[i] = o_half(x[i]);
+        return (size_t) nmat * nb_mat * 2;
+    }
     if (o_is_legacy(type)) {   /* (row by row: the imatrix path's sigma2 is a row's) */
         (void) nthreads;
         for (int64_t r = 0; r < nmat * nrow; ++r)

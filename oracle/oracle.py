@@ -23,6 +23,9 @@ TYPES = {"IQ2_XXS": 16, "IQ2_XS": 17, "IQ3_XXS": 18, "IQ1_S": 19, "IQ4_NL": 20, 
 SOURCES = {"F32": 0, "F16": 1, "Q8_0": 8, "BF16": 30, "MXFP4": 39, "NVFP4": 40, "MXFP8": 43}
 # the 32-weight fallback types (llama-quantize's tensor_type_fallback targets for rows a k-quant cannot hold)
 LEGACY = {"Q4_0": 2, "Q5_0": 6, "Q5_1": 7}
+# the last fallback (tools/requant_experts.py:187-192: rows that fit neither the type nor its fallback): F16, ggml's
+# float -> half value by value
+F16 = 1
 
 
 def available(kind):

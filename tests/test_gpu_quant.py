@@ -365,3 +365,57 @@ def test_nonfinite_inputs(gpuq, oracle):
         with pytest.raises(G.GpuqError, match="status"):
             gpuq.quantize(t, x, im[None])
         assert np.array_equal(gpuq.quantize(t, ok, im[None]), oracle.quantize(t, ok, im[None])), name
+
+
+# ------------------------------------------------------------------------------------------------ F16 (last fallback)
+@pytest.mark.parametrize("n", [100, 7, 1000, 4096])
+def test_f16_target_host_any_row_length(gpuq, oracle, n):
+    """F16 - the type trench-gguf writes for rows that fit neither the asked type nor its fallback, i.e. rows that
+    are not a multiple of 32 - through gpuq_quantize_batch from float32 rows of any length (specials included): the
+    oracle's bytes (ggml's conversion), the imatrix ignored; gpuq_can_quantize reports it with and without one"""
+    rng = np.random.default_rng(n)
+    x = (rng.standard_normal((3, 5, n)) * np.exp2(rng.integers(-20, 12, (3, 5, n)))).astype(np.float32)
+    x.reshape(-1)[::97] = np.nan
+    x.reshape(-1)[5::89] = np.inf
+    x.reshape(-1)[7::83] = 70000.0
+    want = oracle.quantize(1, x)
+    assert gpuq.lib.gpuq_can_quantize(1, 0) == 1 and gpuq.lib.gpuq_can_quantize(1, 1) == 1
+    assert np.array_equal(gpuq.quantize(1, x), want)
+    assert np.array_equal(gpuq.quantize(1, x, np.ones((3, n), np.float32)), want)
+
+
+def test_f16_target_requantize_sources(gpuq, oracle):
+    """F16 from the GPU-read sources: BF16 and F16 rows of a length that is not a multiple of 32, MXFP4 experts
+    (whole 32-value blocks), the oracle's decode then ggml's conversion; a block source with a ragged row refused"""
+    rng = np.random.default_rng(31)
+    n = 1000
+    bf = ((rng.standard_normal((2, 3, n)).astype(np.float32).view(np.uint32) + 0x8000) >> 16).astype(np.uint16)
+    x = (bf.astype(np.uint32) << 16).view(np.float32)
+    assert np.array_equal(gpuq.requantize(30, bf, 1, (2, 3, n)), oracle.quantize(1, x))
+    h = (rng.standard_normal((2, 3, n)) * 100).astype(np.float16)
+    assert np.array_equal(gpuq.requantize(1, h.view(np.uint16), 1, (2, 3, n)), oracle.quantize(1, h.astype(np.float32)))
+    raw, _ = workloads.config2(experts=2, rows=4, cols=7168, seed=9)
+    x = oracle.decode(39, raw, 2 * 4 * 7168).reshape(2, 4, 7168)
+    assert np.array_equal(gpuq.requantize(39, raw, 1, (2, 4, 7168)), oracle.quantize(1, x))
+    with pytest.raises(G.GpuqError):
+        gpuq.requantize(39, raw, 1, (2, 4 * 7168 // 100, 100))
+
+
+def test_f16_target_device_api_and_chunks(gpuq, oracle):
+    """F16 through gpuq_requantize_dev from a float32 source of ragged rows, and through the host pipeline cut into
+    many chunks (GPUQ_CHUNK_MW=1): both the oracle's bytes"""
+    import torch
+    rng = np.random.default_rng(32)
+    x = (rng.standard_normal((2, 700, 1001)) * 3).astype(np.float32)
+    want = oracle.quantize(1, x)
+    dx = torch.from_numpy(x).cuda()
+    out = torch.empty(x.size * 2, dtype=torch.uint8, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    got = gpuq.lib.gpuq_requantize_dev(0, dx.data_ptr(), 1, out.data_ptr(), 2, 700, 1001, None, st)
+    assert got == x.size * 2, gpuq.error()
+    assert np.array_equal(out.cpu().numpy(), want)
+    os.environ["GPUQ_CHUNK_MW"] = "1"
+    try:
+        assert np.array_equal(gpuq.quantize(1, x), want)
+    finally:
+        del os.environ["GPUQ_CHUNK_MW"]

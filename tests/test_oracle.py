@@ -220,3 +220,23 @@ def test_oracle_nonfinite_matches_reference(oracle, reference, name):
         for c in (oracle, reference):
             with pytest.raises(RuntimeError):
                 c.quantize(t, x, im[None])
+
+
+def f16_inputs(n, seed):
+    """float32 values over half's whole range: normals, subnormals, ties, overflow to infinity, zeros, inf, NaN"""
+    rng = np.random.default_rng(seed)
+    x = (rng.standard_normal(n) * np.exp2(rng.integers(-30, 20, n))).astype(np.float32)
+    ties = (np.arange(1, 65, dtype=np.float32) + np.float32(0.5)) * np.float32(2.0 ** -10)   # halfway between halves
+    special = np.float32([0.0, -0.0, np.inf, -np.inf, 65504.0, 65520.0, 1e6, -1e6, 6e-8, 2.98e-8, -5.9e-8, 1e-40])
+    return np.concatenate([x, ties, special, np.float32([np.nan, -np.nan])])
+
+
+def test_oracle_f16_is_ggml_conversion(oracle):
+    """F16, trench-gguf's last fallback (tools/requant_experts.py:187-192; ggml_quantize_chunk's F16 path): the oracle's
+    conversion equals IEEE round-to-nearest-even (numpy's float16) on every non-NaN value, subnormals, ties and
+    overflow included, and writes ggml's NaN (sign | 0x7E00)"""
+    x = f16_inputs(100000, 5)
+    got = oracle.quantize(orc.F16, x[None]).view(np.uint16)
+    fin = ~np.isnan(x)
+    assert np.array_equal(got[fin], x[fin].astype(np.float16).view(np.uint16))
+    assert np.array_equal(got[~fin], np.where(np.signbit(x[~fin]), 0xFE00, 0x7E00).astype(np.uint16))

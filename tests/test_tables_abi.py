@@ -80,10 +80,10 @@ def test_library_exports_every_declared_symbol():
 def test_block_bytes_and_source_types():
     lib = gpuq.open_library()
     want = {16: 66, 17: 74, 18: 98, 19: 50, 20: 18, 21: 110, 22: 82, 23: 136, 29: 56, 8: 34, 10: 84, 11: 110,
-            12: 144, 13: 176, 14: 210, 2: 18, 6: 22, 7: 24}
+            12: 144, 13: 176, 14: 210, 2: 18, 6: 22, 7: 24, 1: 2}   # (1: F16, ggml's last fallback, 2 bytes a value)
     for t, b in want.items():
         assert lib.gpuq_block_bytes(t) == b
-    for t in (0, 1, 3, 15, 24, 30, 39):
+    for t in (0, 3, 15, 24, 30, 39):
         assert lib.gpuq_block_bytes(t) == 0
     # the reference's five sources, NVFP4 and unsloth's MXFP8 rows, the k-/i-quants with a device to_float; not
     # Q4_0 (2) or IQ4_NL (20), whose to_float this library does not have

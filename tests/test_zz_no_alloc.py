@@ -77,3 +77,13 @@ def test_noalloc_rejects_oversized_calls(tables):
                                         huge, huge, 7168, im.ctypes.data)
     assert got == 0
     assert "limit" in g.error()
+
+
+def test_noalloc_f16_target_ragged_rows(tables):
+    """F16 (the fallback for rows that are not a multiple of 32) through the no-alloc entry point from float32 rows of
+    1,001 values: the allocating entry point's bytes"""
+    g = G.Gpuq(device=0, tables=tables)
+    x = (np.random.default_rng(33).standard_normal((2, 50, 1001)) * 7).astype(np.float32)
+    a, b = both(g, G.SOURCES["F32"], x, G.TYPES["F16"], (2, 50, 1001), None)
+    assert np.array_equal(a, b)
+    assert np.array_equal(a.view(np.uint16), x.reshape(-1).astype(np.float16).view(np.uint16))

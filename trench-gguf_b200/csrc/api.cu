@@ -233,6 +233,7 @@ Device * current_device() {
 }
 
 size_t raw_bytes(int src, int64_t n) {
+    if (elementwise_src(src) && n >= 0) return (size_t) n * (src == SRC_F32 ? 4 : 2);   // (exact for any count)
     const int bl = src_block_len(src);
     return bl && n >= 0 ? (size_t) (n / bl) * src_block_bytes(src) : 0;
 }
@@ -315,7 +316,7 @@ bool run_chunks(Device & d, HostJob & j, size_t c0, size_t c1) {
     if (cudaSetDevice(d.id) != cudaSuccess) { set_err("cudaSetDevice(%d) failed", d.id); return false; }
     const int bs = block_len(j.type), bb = block_bytes(j.type);
     const int64_t nb_row = j.n_per_row / bs;
-    const bool want_qw = j.imatrix && j.type != Q8_0;   // (Q8_0 ignores the imatrix, as ggml_quantize_chunk)
+    const bool want_qw = j.imatrix && j.type != Q8_0 && j.type != F16;   // (both ignore it, as ggml_quantize_chunk)
     if (want_qw) {
         const size_t qb = (size_t) j.nmat * j.n_per_row * 4;
         if (!grow((void **) &d.d_qw, &d.cap_qw, qb)) return false;
@@ -570,7 +571,11 @@ bool requantize_args_ok(int src, const void * raw, int type, const void * dst, i
     if (nmat <= 0 || nrow <= 0) { set_err("empty batch"); return false; }
     if (!raw || !dst) { set_err("null source or destination"); return false; }
     if (!type_ok(type, n_per_row, imatrix)) return false;
-    if (n_per_row % sl) { set_err("row length %lld is not a multiple of source type %d's %d-value blocks", (long long) n_per_row, src, sl); return false; }
+    // (an F16 target takes rows of any length from a source without blocks: F16 is the fallback for such rows)
+    if (n_per_row % sl && !(type == F16 && elementwise_src(src))) {
+        set_err("row length %lld is not a multiple of source type %d's %d-value blocks", (long long) n_per_row, src, sl);
+        return false;
+    }
     if (is_block_src(src) && src != IQ4_XS && !is_kquant(src) && !g_active[0]->dq_grid(src)) {
         set_err("source type %d: no dequant grid (gpuq_init first)", src); return false;
     }
@@ -625,7 +630,7 @@ size_t gpuq_quantize_dev(int type, const float * d_x, void * d_dst, int64_t nblo
 size_t gpuq_requantize_dev(int src, const void * d_raw, int type, void * d_dst, int64_t nmat, int64_t nrow,
                            int64_t n_per_row, const float * d_imatrix, void * stream) {
     const int64_t n = nmat * nrow * n_per_row;
-    if (nmat <= 0 || nrow <= 0 || !d_raw || !d_dst || n % 32) {
+    if (nmat <= 0 || nrow <= 0 || !d_raw || !d_dst || (n % 32 && !(type == F16 && elementwise_src(src)))) {
         set_err("gpuq_requantize_dev: bad arguments");
         return 0;
     }
@@ -643,7 +648,7 @@ size_t gpuq_requantize_dev(int src, const void * d_raw, int type, void * d_dst, 
     const int64_t nb_row = n_per_row / block_len(type);
     LaunchArgs a{};
     a.src_type = src; a.src = d_raw;
-    a.qw = type == Q8_0 ? nullptr : d_imatrix;
+    a.qw = type == Q8_0 || type == F16 ? nullptr : d_imatrix;
     a.qw_mod = nb_row; a.qw_div = 1; a.qw_mat = nrow * nb_row;
     a.out = d_dst; a.nblocks = n / block_len(type); a.n_per_row = n_per_row;
     const SearchTab * t = d->tab(type);

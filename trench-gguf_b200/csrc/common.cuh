@@ -16,7 +16,7 @@ constexpr int QK = 256;
 
 enum Type : int { IQ2_XXS = 16, IQ2_XS = 17, IQ3_XXS = 18, IQ1_S = 19, IQ4_NL = 20, IQ3_S = 21, IQ2_S = 22,
                   IQ4_XS = 23, IQ1_M = 29, Q8_0 = 8, Q2_K = 10, Q3_K = 11, Q4_K = 12, Q5_K = 13, Q6_K = 14,
-                  Q4_0 = 2, Q5_0 = 6, Q5_1 = 7 };
+                  Q4_0 = 2, Q5_0 = 6, Q5_1 = 7, F16 = 1 };
 enum Src : int { SRC_F32 = 0, SRC_F16 = 1, SRC_Q8_0 = 8, SRC_BF16 = 30, SRC_MXFP4 = 39, SRC_NVFP4 = 40,
                  SRC_MXFP8 = 43 };
 
@@ -25,10 +25,10 @@ __host__ __device__ constexpr int block_bytes(int t) {
     return t == IQ2_XXS ? 66 : t == IQ2_XS ? 74 : t == IQ2_S ? 82 : t == IQ3_XXS ? 98 : t == IQ3_S ? 110 :
            t == IQ1_S ? 50 : t == IQ1_M ? 56 : t == IQ4_NL ? 18 : t == IQ4_XS ? 136 : t == Q2_K ? 84 :
            t == Q3_K ? 110 : t == Q4_K ? 144 : t == Q5_K ? 176 : t == Q6_K ? 210 : t == Q8_0 ? 34 :
-           t == Q4_0 ? 18 : t == Q5_0 ? 22 : t == Q5_1 ? 24 : 0;
+           t == Q4_0 ? 18 : t == Q5_0 ? 22 : t == Q5_1 ? 24 : t == F16 ? 2 : 0;
 }
 __host__ __device__ constexpr int block_len(int t) {
-    return t == IQ4_NL || t == Q8_0 || t == Q4_0 || t == Q5_0 || t == Q5_1 ? 32 : QK;
+    return t == F16 ? 1 : t == IQ4_NL || t == Q8_0 || t == Q4_0 || t == Q5_0 || t == Q5_1 ? 32 : QK;
 }
 
 // Source tensors. "Inline" sources are decoded by the quantize kernels themselves, in their loads (F32, F16, BF16,
@@ -39,6 +39,8 @@ __host__ __device__ constexpr int block_len(int t) {
 __host__ __device__ constexpr int src_bytes32(int s) {
     return s == SRC_F32 ? 128 : s == SRC_F16 || s == SRC_BF16 ? 64 : s == SRC_Q8_0 ? 34 : s == SRC_MXFP4 ? 17 : 0;
 }
+// one value a unit (no block structure): rows of any length when nothing downstream needs 32-value blocks
+__host__ __device__ constexpr bool elementwise_src(int s) { return s == SRC_F32 || s == SRC_F16 || s == SRC_BF16; }
 __host__ __device__ constexpr bool is_block_src(int s) {
     return s == IQ2_XXS || s == IQ2_XS || s == IQ2_S || s == IQ3_XXS || s == IQ3_S || s == IQ1_S || s == IQ1_M ||
            s == IQ4_XS || s == Q2_K || s == Q3_K || s == Q4_K || s == Q5_K || s == Q6_K;

@@ -81,7 +81,9 @@ inline bool is_iq4(int t) { return t == IQ4_NL || t == IQ4_XS; }
 inline bool is_kquant(int t) { return t == Q2_K || t == Q3_K || t == Q4_K || t == Q5_K || t == Q6_K || t == Q8_0; }
 inline bool is_legacy(int t) { return t == Q4_0 || t == Q5_0 || t == Q5_1; }
 // the types ggml also quantizes without an imatrix (k-quants' and the legacy types' *_ref paths, IQ4 with x^2 weights)
-inline bool takes_no_imatrix(int t) { return is_kquant(t) || is_iq4(t) || is_legacy(t); }
+inline bool takes_no_imatrix(int t) { return is_kquant(t) || is_iq4(t) || is_legacy(t) || t == F16; }
+// F16 (f16.cu): ggml's float -> half of every value (a.nblocks values; any count for F32/F16/BF16 sources)
+cudaError_t launch_f16(const LaunchArgs & a);
 inline bool needs_search_tab(int t) { return is_iq_grid(t) || is_iq1(t); }
 
 inline cudaError_t launch_quantize(int type, const LaunchArgs & a) {
@@ -90,6 +92,7 @@ inline cudaError_t launch_quantize(int type, const LaunchArgs & a) {
     if (is_iq4(type)) return launch_iq4(type, a);
     if (is_kquant(type)) return launch_kquant(type, a);
     if (is_legacy(type)) return launch_legacy(type, a);
+    if (type == F16) return launch_f16(a);
     return cudaErrorInvalidValue;
 }
 

@@ -98,10 +98,11 @@ extern "C" size_t gpuq_requantize_noalloc(int src, const void * raw, int type, v
         return 0;
     }
     const int64_t n = nmat * nrow * n_per_row;   // < 64 Mi: no overflow in the byte counts below
-    if (n % 32) { set_last_error("gpuq_requantize_noalloc: the value count must be a multiple of 32"); return 0; }
-    const bool want_qw = imatrix && type != Q8_0;   // (Q8_0 ignores the imatrix, as ggml_quantize_chunk)
+    const bool any_len = type == F16 && elementwise_src(src);   // (F16 takes rows of any length from these)
+    if (n % 32 && !any_len) { set_last_error("gpuq_requantize_noalloc: the value count must be a multiple of 32"); return 0; }
+    const bool want_qw = imatrix && type != Q8_0 && type != F16;   // (both ignore it, as ggml_quantize_chunk)
     const size_t qw_bytes = want_qw ? (size_t) nmat * n_per_row * 4 : 0;
-    const size_t in_bytes = (size_t) (n / 32) * sb;
+    const size_t in_bytes = any_len ? (size_t) n * (src == SRC_F32 ? 4 : 2) : (size_t) (n / 32) * sb;
     const int64_t nblocks = n / bl;
     const size_t out_bytes = (size_t) nblocks * bb;
     const size_t need = 256 + up256(qw_bytes) + up256(in_bytes) + up256(out_bytes);

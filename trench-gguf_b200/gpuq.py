@@ -16,12 +16,13 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 TYPES = {"IQ2_XXS": 16, "IQ2_XS": 17, "IQ3_XXS": 18, "IQ1_S": 19, "IQ4_NL": 20, "IQ3_S": 21, "IQ2_S": 22,
          "IQ4_XS": 23, "IQ1_M": 29, "Q8_0": 8, "Q2_K": 10, "Q3_K": 11, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14,
-         "Q4_0": 2, "Q5_0": 6, "Q5_1": 7}
+         "Q4_0": 2, "Q5_0": 6, "Q5_1": 7, "F16": 1}
 SOURCES = {"F32": 0, "F16": 1, "Q8_0": 8, "BF16": 30, "MXFP4": 39, "NVFP4": 40, "MXFP8": 43}
-BLOCK_LEN = {t: (32 if n in ("IQ4_NL", "Q8_0", "Q4_0", "Q5_0", "Q5_1") else 256) for n, t in TYPES.items()}
+BLOCK_LEN = {t: (1 if n == "F16" else 32 if n in ("IQ4_NL", "Q8_0", "Q4_0", "Q5_0", "Q5_1") else 256)
+             for n, t in TYPES.items()}
 SRC_BYTES32 = {0: 128, 1: 64, 30: 64, 8: 34, 39: 17}   # (the five sources the quantize kernels decode inline)
 # the types ggml quantizes without an imatrix as well (k-quants' *_ref path, IQ4 with x^2 weights)
-NO_IMATRIX_OK = {8, 10, 11, 12, 13, 14, 20, 23, 2, 6, 7}
+NO_IMATRIX_OK = {8, 10, 11, 12, 13, 14, 20, 23, 2, 6, 7, 1}   # (F16 and Q8_0 ignore one)
 
 SYMBOLS = ("gpuq_init", "gpuq_block_bytes", "gpuq_can_quantize", "gpuq_quantize", "gpuq_quantize_batch",
            "gpuq_can_dequantize", "gpuq_requantize", "gpuq_requantize_batch", "gpuq_quantize_dev",
