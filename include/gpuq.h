@@ -26,7 +26,9 @@ extern "C" {
  * invalidates it. Replaces gpuq_init, gpuq/gpuq.hip:2059-2080. */
 int gpuq_init(const char * tables, int device);
 
-/* Bytes of one block of `type`, 0 for a type this library does not produce. Replaces gpuq.hip:2082-2101. */
+/* Bytes of one block of `type`, 0 for a type this library does not produce. Replaces gpuq.hip:2082-2101. Beyond the
+ * reference's types: Q4_0, Q5_0, Q5_1 (32-value blocks) and F16 (type 1, "blocks" of one value, 2 bytes: ggml's
+ * float -> half of every value, the fallback trench-gguf writes for rows that are not a multiple of 32). */
 size_t gpuq_block_bytes(int type);
 
 /* 1 when gpuq_quantize* takes `type` with (with_imatrix = 1) or without (0) an importance matrix.
@@ -55,7 +57,8 @@ size_t gpuq_requantize(int src, const void * raw, int type, void * dst, int64_t 
                        const float * imatrix);
 
 /* The batched form: nmat matrices, matrix m weighted by imatrix row m; n_per_row a multiple of the source's block
- * (32 values; NVFP4 64; k-/i-quant sources 256). Replaces gpuq.hip:2237-2250. */
+ * (32 values; NVFP4 64; k-/i-quant sources 256) - any length for the F16 target from F32, F16 or BF16 sources.
+ * Replaces gpuq.hip:2237-2250. */
 size_t gpuq_requantize_batch(int src, const void * raw, int type, void * dst, int64_t nmat, int64_t nrow,
                              int64_t n_per_row, const float * imatrix);
 
