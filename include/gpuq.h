@@ -159,6 +159,11 @@ size_t gpuq_ldlq_sub_points_dev(const float * d_blk, const float * d_weff, void 
  * a bad argument. No counterpart in the reference (its factorisation is torch's cholesky_inverse). */
 size_t gpuq_dgemm_dev(int tri, int64_t M, int64_t N, int64_t K, double alpha, const double * d_a, int64_t lda,
                       const double * d_b, int64_t ldb, double beta, double * d_c, int64_t ldc, void * stream);
+/* `batch` such products of one shape in one launch, product i on d_a + i stride_a, d_b + i stride_b, d_c + i stride_c
+ * (strides in doubles; even for A and B); returns the bytes of every C written. */
+size_t gpuq_dgemm_batched_dev(int tri, int64_t M, int64_t N, int64_t K, double alpha, const double * d_a, int64_t lda,
+                              const double * d_b, int64_t ldb, double beta, double * d_c, int64_t ldc, int64_t batch,
+                              int64_t stride_a, int64_t stride_b, int64_t stride_c, void * stream);
 
 /* The Hessian of a layer's inputs on the tensor cores: H = (S X)^T (S X) (accumulate 0) or H += (S X)^T (S X)
  * (accumulate 1), the float32 GEMM a row chunk of

@@ -748,18 +748,26 @@ size_t gpuq_ldlq_sub_points_dev(const float * d_blk, const float * d_weff, void 
     return (size_t) rows * sub * 8;
 }
 
-size_t gpuq_dgemm_dev(int tri, int64_t M, int64_t N, int64_t K, double alpha, const double * d_a, int64_t lda,
-                      const double * d_b, int64_t ldb, double beta, double * d_c, int64_t ldc, void * stream) {
+size_t gpuq_dgemm_batched_dev(int tri, int64_t M, int64_t N, int64_t K, double alpha, const double * d_a, int64_t lda,
+                              const double * d_b, int64_t ldb, double beta, double * d_c, int64_t ldc, int64_t batch,
+                              int64_t stride_a, int64_t stride_b, int64_t stride_c, void * stream) {
     if (tri < 0 || tri > 2 || M <= 0 || N <= 0 || K <= 0 || !d_a || !d_b || !d_c || (K & 1) || (N & 1) || (lda & 1) ||
         (ldb & 1) || lda < K || ldb < N || ldc < N || (tri == 1 && K != N) || (tri == 2 && K != M) ||
+        batch <= 0 || batch > 65535 || (batch > 1 && ((stride_a & 1) || (stride_b & 1))) ||
         misaligned(d_a, 16) || misaligned(d_b, 16) || misaligned(d_c, 8)) {
         set_err("gpuq_dgemm_dev: bad arguments (tri 0, 1 (B lower, K == N) or 2 (A lower, K == M); K, N, lda, ldb even; "
                 "A and B 16-byte aligned)");
         return 0;
     }
-    const cudaError_t e = launch_dgemm(tri, d_a, lda, d_b, ldb, d_c, ldc, M, N, K, alpha, beta, (cudaStream_t) stream);
+    const cudaError_t e = launch_dgemm(tri, d_a, lda, d_b, ldb, d_c, ldc, M, N, K, alpha, beta, batch, stride_a, stride_b,
+                                       stride_c, (cudaStream_t) stream);
     if (e != cudaSuccess) { set_err("gpuq_dgemm_dev: launch failed: %s", cudaGetErrorString(e)); return 0; }
-    return (size_t) M * N * 8;
+    return (size_t) batch * M * N * 8;
+}
+
+size_t gpuq_dgemm_dev(int tri, int64_t M, int64_t N, int64_t K, double alpha, const double * d_a, int64_t lda,
+                      const double * d_b, int64_t ldb, double beta, double * d_c, int64_t ldc, void * stream) {
+    return gpuq_dgemm_batched_dev(tri, M, N, K, alpha, d_a, lda, d_b, ldb, beta, d_c, ldc, 1, 0, 0, 0, stream);
 }
 
 size_t gpuq_xtx_scratch_bytes(int src, int64_t rows, int64_t dim, int scaled) {

@@ -51,8 +51,10 @@ cudaError_t launch_sub_points(const float * blk, const float * weff, uint8_t * q
                               int c0, int scale_search, const uint64_t * grid, cudaStream_t st);
 // C = alpha A B (+ beta C), float64 row-major, with a triangular factor's zero blocks skipped (tri 1: B lower, 2: A
 // lower), on the float64 tensor-core path (ldlq.cu)
+// (batch products of the same shape, operand i at A + i sa, B + i sb, C + i sc)
 cudaError_t launch_dgemm(int tri, const double * A, int64_t lda, const double * B, int64_t ldb, double * C, int64_t ldc,
-                         int64_t M, int64_t N, int64_t K, double alpha, double beta, cudaStream_t st);
+                         int64_t M, int64_t N, int64_t K, double alpha, double beta, int64_t batch, int64_t sa,
+                         int64_t sb, int64_t sc, cudaStream_t st);
 // H += X^T X on the tensor cores (xtx.cu): X [rows][ld] float32 or bf16, optional row scale, float32-accurate sums
 // added in float64 to H [dim][dim]; scratch: the bf16 parts of X laid out as tensor-core operands
 int xtx_parts(int src, bool scaled);

@@ -158,7 +158,11 @@ __global__ void __launch_bounds__(UTHREADS, 2) k_ldlq_gemm(const double * __rest
 template <int TRI>
 __global__ void __launch_bounds__(UTHREADS, 2) k_dgemm(const double * __restrict__ A, int64_t lda,
                                                        const double * __restrict__ B, int64_t ldb, double * C, int64_t ldc,
-                                                       int64_t M, int64_t N, int64_t K, double alpha, double beta) {
+                                                       int64_t M, int64_t N, int64_t K, double alpha, double beta,
+                                                       int64_t sa, int64_t sb, int64_t sc) {
+    A += blockIdx.z * sa;                                 // (grid z: products of one shape at fixed strides)
+    B += blockIdx.z * sb;
+    C += blockIdx.z * sc;
     using SM = UpdSmem<UBK>;
     constexpr int KC = UBK, APAD = SM::APAD;
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -287,21 +291,25 @@ cudaError_t launch_ldlq_update(const double * Es, const double * U, float * W, i
 namespace gq {
 
 cudaError_t launch_dgemm(int tri, const double * A, int64_t lda, const double * B, int64_t ldb, double * C, int64_t ldc,
-                         int64_t M, int64_t N, int64_t K, double alpha, double beta, cudaStream_t st) {
-    if (M <= 0 || N <= 0 || K <= 0 || tri < 0 || tri > 2) return cudaErrorInvalidValue;
+                         int64_t M, int64_t N, int64_t K, double alpha, double beta, int64_t batch, int64_t sa,
+                         int64_t sb, int64_t sc, cudaStream_t st) {
+    if (M <= 0 || N <= 0 || K <= 0 || tri < 0 || tri > 2 || batch <= 0 || batch > 65535) return cudaErrorInvalidValue;
     const size_t smem = sizeof(UpdSmem<UBK>);
-    const dim3 grid((unsigned) ((N + UBN - 1) / UBN), (unsigned) ((M + UBM - 1) / UBM));
+    const dim3 grid((unsigned) ((N + UBN - 1) / UBN), (unsigned) ((M + UBM - 1) / UBM), (unsigned) batch);
     if (grid.y > 65535) return cudaErrorInvalidValue;
     cudaError_t e = cudaSuccess;
     switch (tri) {
         case 0: e = cudaFuncSetAttribute(k_dgemm<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
-                if (e == cudaSuccess) k_dgemm<0><<<grid, UTHREADS, smem, st>>>(A, lda, B, ldb, C, ldc, M, N, K, alpha, beta);
+                if (e == cudaSuccess)
+                    k_dgemm<0><<<grid, UTHREADS, smem, st>>>(A, lda, B, ldb, C, ldc, M, N, K, alpha, beta, sa, sb, sc);
                 break;
         case 1: e = cudaFuncSetAttribute(k_dgemm<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
-                if (e == cudaSuccess) k_dgemm<1><<<grid, UTHREADS, smem, st>>>(A, lda, B, ldb, C, ldc, M, N, K, alpha, beta);
+                if (e == cudaSuccess)
+                    k_dgemm<1><<<grid, UTHREADS, smem, st>>>(A, lda, B, ldb, C, ldc, M, N, K, alpha, beta, sa, sb, sc);
                 break;
         default: e = cudaFuncSetAttribute(k_dgemm<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
-                 if (e == cudaSuccess) k_dgemm<2><<<grid, UTHREADS, smem, st>>>(A, lda, B, ldb, C, ldc, M, N, K, alpha, beta);
+                 if (e == cudaSuccess)
+                     k_dgemm<2><<<grid, UTHREADS, smem, st>>>(A, lda, B, ldb, C, ldc, M, N, K, alpha, beta, sa, sb, sc);
                  break;
     }
     return e != cudaSuccess ? e : cudaGetLastError();

@@ -31,7 +31,7 @@ SYMBOLS = ("gpuq_init", "gpuq_block_bytes", "gpuq_can_quantize", "gpuq_quantize"
            "gpuq_requantize_noalloc", "gpuq_dequantize_error_dev", "gpuq_ldlq_scale_dev",
            "gpuq_ldlq_update_dev", "gpuq_requantize_scaled_batch", "gpuq_check_q8_rounding",
            "gpuq_ldlq_sub_weff_dev", "gpuq_ldlq_sub_points_dev", "gpuq_xtx_scratch_bytes", "gpuq_xtx_dev",
-           "gpuq_dgemm_dev")
+           "gpuq_dgemm_dev", "gpuq_dgemm_batched_dev")
 
 
 class GpuqError(RuntimeError):
@@ -78,6 +78,8 @@ def declare(gq):
         "gpuq_ldlq_sub_weff_dev": (sz, [vp, vp, i64, vp, i64, vp]),
         "gpuq_xtx_scratch_bytes": (sz, [c.c_int, i64, i64, c.c_int]),
         "gpuq_dgemm_dev": (sz, [c.c_int, i64, i64, i64, c.c_double, vp, i64, vp, i64, c.c_double, vp, i64, vp]),
+        "gpuq_dgemm_batched_dev": (sz, [c.c_int, i64, i64, i64, c.c_double, vp, i64, vp, i64, c.c_double, vp, i64, i64,
+                                        i64, i64, i64, vp]),
         "gpuq_xtx_dev": (sz, [c.c_int, vp, i64, vp, i64, i64, vp, c.c_int, vp, sz, vp]),
         "gpuq_ldlq_sub_points_dev": (sz, [vp, vp, vp, vp, i64, c.c_int, c.c_int, c.c_int, vp]),
         "gpuq_requantize_scaled_batch": (sz, [c.c_int, vp, c.c_int, vp, i64, i64, i64, vp, vp]),

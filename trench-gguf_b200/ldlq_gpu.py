@@ -139,40 +139,65 @@ def _lib():
     return _LIB[0]
 
 
-def _dgemm(tri, A, B, C, alpha=1.0):
+def _dgemm(tri, A, B, C, alpha=1.0, batch=1, strides=(0, 0, 0)):
     """C = alpha A @ B on this library's float64 tensor-core GEMM (row-major float64 device matrices, row strides as
-    they lie), the zero blocks of a lower-triangular B (tri 1) or A (tri 2) skipped"""
+    they lie), the zero blocks of a lower-triangular B (tri 1) or A (tri 2) skipped; with batch > 1 the same product
+    also on the operands `strides` (in doubles) further on, batch - 1 times, in the same launch"""
     torch = _torch()
     for t in (A, B, C):
         assert t.dtype == torch.float64 and t.is_cuda and t.stride(1) == 1
     M, K = A.shape
     N = B.shape[1]
-    got = _lib().gpuq_dgemm_dev(tri, M, N, K, alpha, A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0), 0.0,
-                                C.data_ptr(), C.stride(0), torch.cuda.current_stream(A.device).cuda_stream)
-    if got != M * N * 8:
-        raise RuntimeError("gpuq_dgemm_dev: " + _lib().gpuq_last_error().decode())
+    got = _lib().gpuq_dgemm_batched_dev(tri, M, N, K, alpha, A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0), 0.0,
+                                        C.data_ptr(), C.stride(0), batch, strides[0], strides[1], strides[2],
+                                        torch.cuda.current_stream(A.device).cuda_stream)
+    if got != batch * M * N * 8:
+        raise RuntimeError("gpuq_dgemm_batched_dev: " + _lib().gpuq_last_error().decode())
 
 
-def _split(lo, hi, leaf, nodes, leaves):
-    """the halving tree of [lo, hi): internal nodes (lo, h, hi) deepest last, leaves (lo, hi); h a multiple of 256"""
+def _split(lo, hi, leaf, nodes, leaves, depth=0):
+    """the halving tree of [lo, hi): internal nodes (depth, lo, h, hi), leaves (lo, hi); h a multiple of 256"""
     m = hi - lo
     if m <= leaf:
         leaves.append((lo, hi))
         return
     h = lo + (m // 2 + QK - 1) // QK * QK
-    nodes.append((lo, h, hi))
-    _split(lo, h, leaf, nodes, leaves)
-    _split(h, hi, leaf, nodes, leaves)
+    nodes.append((depth, lo, h, hi))
+    _split(lo, h, leaf, nodes, leaves, depth + 1)
+    _split(h, hi, leaf, nodes, leaves, depth + 1)
 
 
-def _lower_inverse(L, out, leaf=512):
+def _node_groups(nodes):
+    """the nodes of each depth, deepest first, as runs of one shape at one spacing (one batched launch a run)"""
+    out = []
+    for depth in sorted({d for d, _, _, _ in nodes}, reverse=True):
+        shapes = {}
+        for d, lo, h, hi in nodes:
+            if d == depth:
+                shapes.setdefault((h - lo, hi - h), []).append((lo, h, hi))
+        for level in shapes.values():
+            level.sort()
+            run = [level[0]]
+            for node in level[1:]:
+                span = run[1][0] - run[0][0] if len(run) > 1 else node[0] - run[0][0]
+                if node[0] - run[-1][0] == span:
+                    run.append(node)
+                else:
+                    out.append(run)
+                    run = [node]
+            out.append(run)
+    return out
+
+
+def _lower_inverse(L, out, leaf=256):
     """out = L^-1 for a lower-triangular L, by halves: [[A, 0], [B, C]]^-1 = [[A^-1, 0], [-C^-1 B A^-1, C^-1]].
     The leaves (diagonal blocks of at most `leaf` columns) are inverted together, one batched triangular solve
     against the identity a leaf size; the tree's nodes are then closed bottom-up, each off-diagonal block two
     triangular-times-full products (on the GPU this library's float64 tensor-core GEMM with the triangle's zero
-    blocks skipped: n^3/3 multiply-adds in all, as a triangular inverse)"""
+    blocks skipped: n^3/3 multiply-adds in all, as a triangular inverse), the nodes of one depth and shape in one
+    launch"""
     torch = _torch()
-    if L.stride(1) != 1 or out.stride(1) != 1:   # (the triangular products want row-major operands)
+    if L.stride(1) != 1 or out.stride(1) != 1 or out.stride(0) != L.stride(0):   # (row-major, one row stride)
         res = torch.empty(out.shape, dtype=out.dtype, device=out.device)
         _lower_inverse(L.contiguous(), res, leaf)
         out.copy_(res)
@@ -188,15 +213,21 @@ def _lower_inverse(L, out, leaf=512):
         for (lo, hi), b in zip(group, inv):
             out[lo:hi, lo:hi] = b
     gpu = L.is_cuda and L.dtype == torch.float64
-    for lo, h, hi in reversed(nodes):             # children before parents
-        out[lo:h, h:hi].zero_()
+    for run in _node_groups(nodes):               # children before parents; a run of equal nodes in one launch
+        for lo, h, hi in run:
+            out[lo:h, h:hi].zero_()
         if gpu:
-            t = torch.empty((hi - h, h - lo), dtype=L.dtype, device=L.device)
-            _dgemm(1, L[h:hi, lo:h], out[lo:h, lo:h], t)                  # B A^-1 (A^-1 lower)
-            _dgemm(2, out[h:hi, h:hi], t, out[h:hi, lo:h], -1.0)          # -C^-1 (B A^-1) (C^-1 lower)
+            lo, h, hi = run[0]
+            nb, span = len(run), (run[1][0] - lo if len(run) > 1 else 0)
+            t = torch.empty((nb, hi - h, h - lo), dtype=L.dtype, device=L.device)
+            diag = span * (L.stride(0) + 1)                                  # (the next node: span rows and columns on)
+            tstr = (hi - h) * (h - lo)
+            _dgemm(1, L[h:hi, lo:h], out[lo:h, lo:h], t[0], 1.0, nb, (diag, diag, tstr))       # B A^-1
+            _dgemm(2, out[h:hi, h:hi], t[0], out[h:hi, lo:h], -1.0, nb, (diag, tstr, diag))    # -C^-1 (B A^-1)
         else:
-            x = _trmm_left_lower(out[h:hi, h:hi], _trmm_right_lower(L[h:hi, lo:h], out[lo:h, lo:h], leaf), leaf)
-            out[h:hi, lo:h].copy_(x.neg_())
+            for lo, h, hi in run:
+                x = _trmm_left_lower(out[h:hi, h:hi], _trmm_right_lower(L[h:hi, lo:h], out[lo:h, lo:h], leaf), leaf)
+                out[h:hi, lo:h].copy_(x.neg_())
     # (the blocks above the diagonal of the leaves' own rows were never written by a node: zero them)
     for lo, hi in leaves:
         out[lo:hi, hi:].zero_()
