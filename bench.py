@@ -641,6 +641,12 @@ def run_ldlq(args, g, dev, stream, fp32, rank=0, world=1, dist=None):
                          "frac": total_fl / (ms / 1e3) / 1e12 / peak64, "flop_per_expert": fl,
                          "peak_source": "trench-gguf_b200/peak.cu float64 FMA rate, measured in this run"},
             "parity": parity, "clocks": clk.summary()}
+    if parity:   # the CPU path beside it: the reference's loop on this host's cores for the rows the parity checked
+        line["cpu_baseline"] = {"value": parity["rows_checked"] * ne0 / parity["cpu_s"] / 1e9, "unit": "Gweights/s",
+                                "kind": "port", "cores": os.cpu_count() or 1,
+                                "sample": "expert 0's first %d rows: the reference's loop (tools/ldlq.py, restated in "
+                                          "numpy, float64) with %s, the float64 factor included" % (
+                                              parity["rows_checked"], parity["checker"].split(" with ", 1)[-1])}
     print(json.dumps(line), flush=True)
 
 
