@@ -89,6 +89,46 @@ def test_prepare_hessian_torch_equals_restatement():
         assert np.array_equal(U1, np.triu(U1))
 
 
+def _emulated_dgemm(tri, A, B, C, alpha=1.0, batch=1, strides=(0, 0, 0)):
+    """gpuq_dgemm_batched_dev's contract on CPU tensors: product i on the operands strides[k] * i doubles further on
+    in their storage (the same pointer arithmetic the kernel does), the triangle of A (tri 2) or B (tri 1) read as
+    stored"""
+    import torch
+    for i in range(batch):
+        Ai, Bi, Ci = (torch.as_strided(T, T.shape, T.stride(), T.storage_offset() + i * st)
+                      for T, st in zip((A, B, C), strides))
+        Ci.copy_(alpha * (Ai @ Bi))
+
+
+def test_lower_inverse_batched_runs_on_cpu():
+    """the GPU inverse's grouping of the halving tree (the nodes of a depth and shape, evenly spaced, in one batched
+    launch) and its operand strides, driven on the CPU with an emulated batched product: every node closed once,
+    the inverse a triangular solve's, for sizes whose trees have uneven halves"""
+    pytest.importorskip("torch")
+    import torch
+    import ldlq_gpu
+    gen = torch.Generator().manual_seed(3)
+    for m in (256, 700, 1536, 2560, 3840, 7168 // 4 * 2):
+        nodes, leaves = [], []
+        ldlq_gpu._split(0, m, 256, nodes, leaves)
+        runs = ldlq_gpu._node_groups(nodes)
+        assert sorted(n for r in runs for n in r) == sorted((lo, h, hi) for _, lo, h, hi in nodes)
+        for r in runs:
+            assert len({(h - lo, hi - h) for lo, h, hi in r}) == 1
+            assert len({b[0] - a[0] for a, b in zip(r, r[1:])}) <= 1
+        X = torch.randn(m, m, dtype=torch.float64, generator=gen)
+        L = torch.linalg.cholesky(X @ X.T / m + torch.eye(m, dtype=torch.float64)).contiguous()
+        out = torch.full_like(L, float("nan"))
+        for lo, hi in leaves:
+            out[lo:hi, lo:hi] = torch.linalg.solve_triangular(L[lo:hi, lo:hi], torch.eye(hi - lo, dtype=torch.float64),
+                                                              upper=False)
+            out[lo:hi, hi:] = 0
+        ldlq_gpu._close_runs(L, out, runs, _emulated_dgemm)
+        want = torch.linalg.solve_triangular(L, torch.eye(m, dtype=torch.float64), upper=False)
+        assert not torch.isnan(out).any(), m
+        assert float((out - want).abs().max()) <= 1e-12 * float(want.abs().max()), m
+
+
 # ------------------------------------------------------------------------------------------------ GPU
 def _gpu_setup(tables):
     import torch

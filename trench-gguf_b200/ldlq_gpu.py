@@ -189,6 +189,23 @@ def _node_groups(nodes):
     return out
 
 
+def _close_runs(L, out, runs, dgemm):
+    """the off-diagonal blocks of the inverse, run by run (children before parents): for the nodes (lo, h, hi) of a
+    run - one shape, evenly spaced - out[h:hi, lo:h] = -out[h:hi, h:hi] (L[h:hi, lo:h] out[lo:h, lo:h]) as two
+    batched products, node i's operands `span` rows and columns after node i - 1's (L and out share a row stride)"""
+    torch = _torch()
+    for run in runs:
+        for lo, h, hi in run:
+            out[lo:h, h:hi].zero_()
+        lo, h, hi = run[0]
+        nb, span = len(run), (run[1][0] - lo if len(run) > 1 else 0)
+        t = torch.empty((nb, hi - h, h - lo), dtype=L.dtype, device=L.device)
+        diag = span * (L.stride(0) + 1)
+        tstr = (hi - h) * (h - lo)
+        dgemm(1, L[h:hi, lo:h], out[lo:h, lo:h], t[0], 1.0, nb, (diag, diag, tstr))        # B A^-1 (A^-1 lower)
+        dgemm(2, out[h:hi, h:hi], t[0], out[h:hi, lo:h], -1.0, nb, (diag, tstr, diag))     # -C^-1 (B A^-1)
+
+
 def _lower_inverse(L, out, leaf=256):
     """out = L^-1 for a lower-triangular L, by halves: [[A, 0], [B, C]]^-1 = [[A^-1, 0], [-C^-1 B A^-1, C^-1]].
     The leaves (diagonal blocks of at most `leaf` columns) are inverted together, one batched triangular solve
@@ -212,22 +229,13 @@ def _lower_inverse(L, out, leaf=256):
         inv = torch.linalg.solve_triangular(blocks, eye, upper=False)
         for (lo, hi), b in zip(group, inv):
             out[lo:hi, lo:hi] = b
-    gpu = L.is_cuda and L.dtype == torch.float64
-    for run in _node_groups(nodes):               # children before parents; a run of equal nodes in one launch
-        for lo, h, hi in run:
+    if L.is_cuda and L.dtype == torch.float64:
+        _close_runs(L, out, _node_groups(nodes), _dgemm)
+    else:
+        for _, lo, h, hi in sorted(nodes, reverse=True):   # children before parents
             out[lo:h, h:hi].zero_()
-        if gpu:
-            lo, h, hi = run[0]
-            nb, span = len(run), (run[1][0] - lo if len(run) > 1 else 0)
-            t = torch.empty((nb, hi - h, h - lo), dtype=L.dtype, device=L.device)
-            diag = span * (L.stride(0) + 1)                                  # (the next node: span rows and columns on)
-            tstr = (hi - h) * (h - lo)
-            _dgemm(1, L[h:hi, lo:h], out[lo:h, lo:h], t[0], 1.0, nb, (diag, diag, tstr))       # B A^-1
-            _dgemm(2, out[h:hi, h:hi], t[0], out[h:hi, lo:h], -1.0, nb, (diag, tstr, diag))    # -C^-1 (B A^-1)
-        else:
-            for lo, h, hi in run:
-                x = _trmm_left_lower(out[h:hi, h:hi], _trmm_right_lower(L[h:hi, lo:h], out[lo:h, lo:h], leaf), leaf)
-                out[h:hi, lo:h].copy_(x.neg_())
+            x = _trmm_left_lower(out[h:hi, h:hi], _trmm_right_lower(L[h:hi, lo:h], out[lo:h, lo:h], leaf), leaf)
+            out[h:hi, lo:h].copy_(x.neg_())
     # (the blocks above the diagonal of the leaves' own rows were never written by a node: zero them)
     for lo, hi in leaves:
         out[lo:hi, hi:].zero_()
