@@ -382,6 +382,34 @@ def test_gpu_iq2xxs_sub_against_reference(tables, oracle, golden, key, sub, ss, 
 
 
 @pytest.mark.gpu
+def test_gpu_iq2xxs_sub_gate_and_up_share_the_factor(tables, oracle):
+    """the sub-block variant on an expert's gate and up together (B = 2 matrices sharing U and the column order, each
+    with its own imatrix row: row r of the slab weighted by imatrix row r / ne1), against the restatement run on each
+    matrix alone, act order"""
+    torch, G, ldlq_gpu, g = _gpu_setup(tables)
+    dev = torch.device("cuda")
+    ne1, ne0, n = 64, 1024, 2048
+    H, im = LO.synthetic_hessian(ne0, n, seed=61)
+    rng = np.random.default_rng(62)
+    Ws = np.stack([(rng.standard_t(5, (ne1, ne0)) * 0.02).astype(np.float32) for _ in range(2)])
+    ims = np.stack([im, (im * (0.25 + rng.random(ne0))).astype(np.float32)])
+    U, perm, _, _ = LO.prepare_hessian(H, n, damp=0.01, order="act")
+    gqt = ldlq_gpu.GpuQuant(g, G.TYPES["IQ2_XXS"])
+    got = ldlq_gpu.quantize_matrix_iq2xxs_sub_torch(torch.from_numpy(Ws).to(dev), gqt, torch.from_numpy(U).to(dev),
+                                                    torch.from_numpy(perm).to(dev), torch.from_numpy(ims).to(dev),
+                                                    sub=32, scale_search=1).cpu().numpy()
+    quant, _, _ = LO.checker_quant(oracle, G.TYPES["IQ2_XXS"])
+    grid = LO.iq2xxs_grid(oracle)
+    for b in range(2):
+        want, deq_w = LO.quantize_matrix_iq2xxs_sub(Ws[b], quant, grid, U, perm, ims[b], sub=32, scale_search=1)
+        same = (got[b].reshape(ne1, -1, 66) == want.reshape(ne1, -1, 66)).all(-1).mean()
+        assert same >= IDENTICAL_MIN, (b, same)
+        lw = LO.proxy_loss(Ws[b], deq_w, H, n)
+        deq = oracle.dequantize(G.TYPES["IQ2_XXS"], got[b]).reshape(ne1, ne0)
+        assert abs(LO.proxy_loss(Ws[b], deq, H, n) - lw) <= LOSS_RTOL * lw
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("sub,ss", [(32, 1), (8, 0)])
 def test_gpu_iq2xxs_sub_experts_against_restatement(tables, oracle, sub, ss):
     """the whole GPU path of the variant - the float64 factor of each expert's own Hessian, then one lockstep loop

@@ -284,16 +284,25 @@ void host_copy(void * dst, const void * src, size_t n) {
     for (auto & t : th) t.join();
 }
 
+// chunks of about target_values each; the first is a quarter of that (a matrix or a quarter of the rows), so the
+// pipeline's first copy - the one nothing overlaps - is short
 std::vector<Chunk> make_chunks(int64_t nmat, int64_t nrow, int64_t n_per_row, int64_t target_values) {
     std::vector<Chunk> c;
     const int64_t per_mat = nrow * n_per_row;
     if (per_mat >= target_values) {
         const int64_t rows = std::max<int64_t>(1, target_values / n_per_row);
-        for (int64_t m = 0; m < nmat; ++m)
-            for (int64_t r = 0; r < nrow; r += rows) c.push_back({m, m + 1, r, std::min(nrow, r + rows)});
+        const int64_t first = std::max<int64_t>(1, rows / 4);
+        for (int64_t m = 0; m < nmat; ++m) {
+            int64_t r = 0;
+            if (m == 0 && first < rows && first < nrow) { c.push_back({0, 1, 0, first}); r = first; }
+            for (; r < nrow; r += rows) c.push_back({m, m + 1, r, std::min(nrow, r + rows)});
+        }
     } else {
         const int64_t mats = std::max<int64_t>(1, target_values / per_mat);
-        for (int64_t m = 0; m < nmat; m += mats) c.push_back({m, std::min(nmat, m + mats), 0, nrow});
+        const int64_t first = std::max<int64_t>(1, mats / 4);
+        int64_t m = 0;
+        if (first < mats && first < nmat) { c.push_back({0, first, 0, nrow}); m = first; }
+        for (; m < nmat; m += mats) c.push_back({m, std::min(nmat, m + mats), 0, nrow});
     }
     return c;
 }
