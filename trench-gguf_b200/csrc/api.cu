@@ -269,10 +269,11 @@ struct HostJob {
     std::atomic<bool> cancel{false};   // set by a device worker that failed: the others stop before their next chunk
 };
 
-// host memcpy split over a few threads for large pieces (one thread copies ~10 GB/s, less than a PCIe 5 link)
+// host memcpy split over up to 8 threads for large pieces (one thread copies ~10 GB/s, less than a PCIe 5 link): the
+// pageable sources into the pinned slots and the results out to pageable destinations
 void host_copy(void * dst, const void * src, size_t n) {
-    constexpr size_t PIECE = (size_t) 8 << 20;
-    const int nt = (int) std::min<size_t>(4, n / PIECE);
+    constexpr size_t PIECE = (size_t) 4 << 20;
+    const int nt = (int) std::min<size_t>(8, n / PIECE);
     if (nt <= 1) { std::memcpy(dst, src, n); return; }
     std::vector<std::thread> th;
     const size_t per = (n / nt + 63) & ~(size_t) 63;
@@ -348,7 +349,7 @@ bool run_chunks(Device & d, HostJob & j, size_t c0, size_t c1) {
     auto finish = [&](int slot) {   // host side of a slot's D2H: copy staged bytes to the caller's buffer
         if (!pend[slot].on) return;
         if (cudaEventSynchronize(d.ev_d2h[slot]) != cudaSuccess) ok = false;
-        else if (!dst_pinned) std::memcpy(pend[slot].dst, d.h_out[slot], pend[slot].bytes);
+        else if (!dst_pinned) host_copy(pend[slot].dst, d.h_out[slot], pend[slot].bytes);
         pend[slot].on = false;
     };
     // the imatrix and scale copies must land before the first kernel
