@@ -72,6 +72,8 @@ def parse():
     ap.add_argument("--ldlq-streams", type=int, default=4,
                     help="config 5: CUDA streams the experts alternate over (the next expert's factorisation runs "
                          "beside this one's loop); 1 = one expert after another on one stream")
+    ap.add_argument("--ldlq-type", default="iq2_xxs",
+                    help="config 5: the target type (the reference's LDLQ_TYPES: i-quants, Q4_K, Q5_K, Q6_K, IQ4_XS)")
     ap.add_argument("--ldlq-sub", type=int, default=0, choices=[0, 32, 8],
                     help="config 5: the IQ2_XXS sub-block variant (feedback every 32 or 8 columns)")
     ap.add_argument("--scale-search", type=int, default=0, help="config 5 with --ldlq-sub 32: sub-block scales tried")
@@ -512,7 +514,10 @@ def run_ldlq(args, g, dev, stream, fp32, rank=0, world=1, dist=None):
     n, rk, ne1, ne0 = 4096, 32, ROWS, COLS
     gen = torch.Generator(device=dev).manual_seed(105 + 1000 * rank)
     torch.backends.cuda.matmul.allow_tf32 = False       # (the reference's float32 GEMM is a full float32 one)
-    gqt = ldlq_gpu.GpuQuant(g.lib, 16)
+    lt = TYPES[args.ldlq_type]
+    if args.ldlq_sub and lt != 16:
+        raise SystemExit("--ldlq-sub is the IQ2_XXS variant")
+    gqt = ldlq_gpu.GpuQuant(g.lib, lt)
     xtx = hessian_gpu.Xtx(g.lib, dev)
     Hs, ims, Ws = [], [], []
     hess_ms, torch_ms, h_err = [], None, None
@@ -604,7 +609,7 @@ def run_ldlq(args, g, dev, stream, fp32, rank=0, world=1, dist=None):
         W0 = Ws[0][0].cpu().numpy()
         im0 = ims[0][0].cpu().numpy()
         t0 = time.perf_counter()
-        quant, dequant, tsize = LO.checker_quant(chk, 16, threads=os.cpu_count() or 1)
+        quant, dequant, tsize = LO.checker_quant(chk, lt, threads=os.cpu_count() or 1)
         U, perm, _, _ = LO.prepare_hessian(H0, n, damp=0.01)
         got = outs[0].cpu().numpy()[0]
         if args.ldlq_sub:   # (rows are independent given U: the first 256 rows, the restatement being numpy-vectorised)
@@ -616,7 +621,7 @@ def run_ldlq(args, g, dev, stream, fp32, rank=0, world=1, dist=None):
             want, deq_w = LO.quantize_matrix(W0, quant, dequant, tsize, U=U, perm=perm, imatrix=im0, feedback=True)
         cpu_s = time.perf_counter() - t0
         same, nb = block_parity(got, want, tsize)
-        deq = chk.dequantize(16, got).reshape(rows_checked, ne0)
+        deq = chk.dequantize(lt, got).reshape(rows_checked, ne0)
         lw, lg = LO.proxy_loss(W0, deq_w, H0, n), LO.proxy_loss(W0, deq, H0, n)
         parity = {"blocks": nb, "identical": same, "share": same / nb, "proxy_loss_rel_diff": abs(lg - lw) / lw,
                   "rows_checked": rows_checked,
@@ -627,12 +632,13 @@ def run_ldlq(args, g, dev, stream, fp32, rank=0, world=1, dist=None):
     total_fl = E * sum(fl.values())
     peak64 = fp64_peak_tflops(int(os.environ.get("LOCAL_RANK", "0")))
     rate = world * E * ne1 * ne0 / (ms / 1e3) / 1e9
-    line = {"metric": "Gweights/s LDLQ-requantized to IQ2_XXS, config 5", "value": rate, "unit": "Gweights/s",
+    line = {"metric": "Gweights/s LDLQ-requantized to %s, config 5" % args.ldlq_type.upper(), "value": rate,
+            "unit": "Gweights/s",
             "n_gpus": world, "steps": len(times), "warmup": 1, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "dtype": "f32 weights, f64 factor and feedback", "data": "synthetic (config 5, seeded)",
-            "config": {"workload": "config 5: %d experts a GPU, 2048 x 7168 -> IQ2_XXS, own Hessian each (7168^2 from "
+            "config": {"workload": "config 5: %d experts a GPU, 2048 x 7168 -> %s, own Hessian each (7168^2 from "
                                    "4096 rows), act order seq, imatrix weights; factor + lockstep loop%s" % (
-                                       E, "" if not args.ldlq_sub else "; the sub-block variant, feedback every %d "
+                                       E, args.ldlq_type.upper(), "" if not args.ldlq_sub else "; the sub-block variant, feedback every %d "
                                        "columns, scale search %d" % (args.ldlq_sub, args.scale_search)),
                        "parallelism": "expert-sharded x%d" % world},
             "per_expert_ms": ms / E, "hessian_build": hessian_line(hess_ms, torch_ms, h_err, n, ne0),

@@ -43,7 +43,10 @@ constexpr int XT_BM = 128, XT_BN = 256;           // the tile of H (rows x colum
 constexpr int XT_ABYTES = XT_BM / 8 * XT_UNIT;    // 8 KB
 constexpr int XT_NH = 128;                        // the columns of one product (N): half the tile
 constexpr int XT_HBYTES = XT_NH / 8 * XT_UNIT;    // 8 KB: a half of the B tile
-constexpr int XT_TMEM_COLS = 512;                 // [large | small] float32 accumulators, each two halves of 128
+// [large | small] float32 accumulators, each two halves of 128: all of an SM's tensor memory. One CTA an SM is all
+// the shared memory allows, so no other CTA of this kernel waits on the allocation; a CTA of another kernel holding
+// columns (a library GEMM on another stream) only delays it until that CTA ends
+constexpr int XT_TMEM_COLS = 512;
 constexpr int XT_SEG = 32;                        // K tiles (1,024 rows of X) summed in float32 before float64
 constexpr int XT_THREADS = 192, XT_EPI_THREADS = 128;   // warp 0 copies, warp 1 multiplies, warps 2-5 the epilogue
 constexpr int XT_SMEM_BUDGET = 220 * 1024;
