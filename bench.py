@@ -143,6 +143,18 @@ def cpu_checker():
     return orc.Checker("reference" if kind == "reference" else "oracle", os.path.join(PKG, "gpuq_tables.bin")), kind
 
 
+def cpu_model():
+    """the host CPU's model name (/proc/cpuinfo), recorded beside every CPU figure"""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def cpu_baseline(types, raw, im):
     """the reference's own block functions on this host's cores on whole 2048 x 7168 MXFP4 experts (raw [E, ...],
     im [E, 7168]: a slice of the GPU's own workload, decoded outside the timed region) -> each type. Returns the
@@ -162,7 +174,8 @@ def cpu_baseline(types, raw, im):
             outs[name].append(chk.quantize(TYPES[name], x, im[e:e + 1], threads=threads))
         dt += time.perf_counter() - t0
     n = len(types) * experts * ROWS * COLS
-    cb = {"value": n / dt / 1e9, "unit": "Gweights/s", "cores": threads, "kind": kind,
+    cb = {"value": n / dt / 1e9, "unit": "Gweights/s", "cores": threads, "kind": kind, "cpu_model": cpu_model(),
+          "nproc": os.cpu_count(),
           "sample": "%d of the shard's experts (%d x %d, MXFP4 -> %s), %.1f s of quantization" % (
               experts, ROWS, COLS, "+".join(types), dt)}
     return cb, {t: np.concatenate(v) for t, v in outs.items()}
@@ -450,7 +463,8 @@ def run_config(args):
         parity[name] = {"blocks": n, "identical": same, "sample": "%d x %d x %d" % (nmat, nrow, npr)}
     parity["blocks"] = sum(v["blocks"] for v in parity.values() if isinstance(v, dict))
     parity["identical"] = sum(v["identical"] for v in parity.values() if isinstance(v, dict))
-    cb = {"value": cpu_w / cpu_s / 1e9, "unit": "Gweights/s", "cores": threads,
+    cb = {"value": cpu_w / cpu_s / 1e9, "unit": "Gweights/s", "cores": threads, "cpu_model": cpu_model(),
+          "nproc": os.cpu_count(),
           "kind": "reference" if kind == "reference" else "port",
           "sample": "each type's parity sample (%.1f M weights, %.1f s)" % (cpu_w / 1e6, cpu_s)}
     line = {"metric": "Gweights/s quantized, config %d" % cfg, "value": total_w / (total_ms / 1e3) / 1e9,
@@ -649,7 +663,7 @@ def run_ldlq(args, g, dev, stream, fp32, rank=0, world=1, dist=None):
             "parity": parity, "clocks": clk.summary()}
     if parity:   # the CPU path beside it: the reference's loop on this host's cores for the rows the parity checked
         line["cpu_baseline"] = {"value": parity["rows_checked"] * ne0 / parity["cpu_s"] / 1e9, "unit": "Gweights/s",
-                                "kind": "port", "cores": os.cpu_count() or 1,
+                                "kind": "port", "cores": os.cpu_count() or 1, "cpu_model": cpu_model(),
                                 "sample": "expert 0's first %d rows: the reference's loop (tools/ldlq.py, restated in "
                                           "numpy, float64) with %s, the float64 factor included" % (
                                               parity["rows_checked"], parity["checker"].split(" with ", 1)[-1])}
