@@ -624,6 +624,13 @@ def run_ldlq(args, g, dev, stream, fp32, rank=0, world=1, dist=None):
         im0 = ims[0][0].cpu().numpy()
         t0 = time.perf_counter()
         quant, dequant, tsize = LO.checker_quant(chk, lt, threads=os.cpu_count() or 1)
+        dq_chk = chk
+        if 10 <= lt <= 14 and kind == "reference":
+            # (the reference leaves the k-quants' to_float to ggml: its host build has none; the restatement's, pinned
+            # to gguf-py's dequantizers, stands in - the quantizer stays the reference's own)
+            import oracle as orc
+            dq_chk = orc.Checker("oracle", os.path.join(PKG, "gpuq_tables.bin"))
+            dequant = LO.checker_quant(dq_chk, lt)[1]
         U, perm, _, _ = LO.prepare_hessian(H0, n, damp=0.01)
         got = outs[0].cpu().numpy()[0]
         if args.ldlq_sub:   # (rows are independent given U: the first 256 rows, the restatement being numpy-vectorised)
@@ -635,7 +642,7 @@ def run_ldlq(args, g, dev, stream, fp32, rank=0, world=1, dist=None):
             want, deq_w = LO.quantize_matrix(W0, quant, dequant, tsize, U=U, perm=perm, imatrix=im0, feedback=True)
         cpu_s = time.perf_counter() - t0
         same, nb = block_parity(got, want, tsize)
-        deq = chk.dequantize(lt, got).reshape(rows_checked, ne0)
+        deq = dq_chk.dequantize(lt, got).reshape(rows_checked, ne0)
         lw, lg = LO.proxy_loss(W0, deq_w, H0, n), LO.proxy_loss(W0, deq, H0, n)
         parity = {"blocks": nb, "identical": same, "share": same / nb, "proxy_loss_rel_diff": abs(lg - lw) / lw,
                   "rows_checked": rows_checked,
