@@ -53,6 +53,29 @@ def test_layer_dump_routing_is_the_references(tmp_path, hg):
     assert len(d.rows(3)[0]) == 0 and len(d.rows(99)[0]) == 0
 
 
+def test_dense_map_and_dump_variants(tmp_path, hg):
+    """DenseHessians' weight -> input file map as the reference reads it (dense.txt entries, the shared experts' and
+    the router's implicit MoE input, names it does not know); a dump without the down input or routing weights"""
+    pytest.importorskip("torch")
+    import hessian_gpu
+    ddir = _dump(tmp_path, hg)
+    dn = hessian_gpu.DenseHessians(ddir, "cpu")
+    name = "blk.%d.attn_output_a.weight" % MG.L
+    assert dn.has(name) and dn.groups(name) == MG.DENSE_GROUPS and dn.file(name) == "blk.%d.din.attn_out.bf16" % MG.L
+    for implicit in ("ffn_gate_shexp", "ffn_up_shexp", "ffn_gate_inp"):
+        nm = "blk.%d.%s.weight" % (MG.L, implicit)
+        assert dn.has(nm) and dn.groups(nm) == 1 and dn.file(nm) == "blk.%d.x.bf16" % MG.L
+    assert not dn.has("blk.%d.ffn_down_shexp.weight" % MG.L) and not dn.has("blk.%d.ffn_up_shexp.weight" % (MG.L + 1))
+    for f in ("a.bf16", "w_scaled.f32"):
+        os.remove(os.path.join(ddir, "blk.%d.%s" % (MG.L, f)))
+    d = hessian_gpu.LayerDump(ddir, MG.L)
+    assert d.a is None and d.w is None
+    dh = hessian_gpu.DumpHessians(ddir, "cpu")
+    assert dh.has(MG.L) and not dh.has(MG.L + 1)
+    with pytest.raises(ValueError):
+        dh.hessian_mid(MG.L, 0)                         # no down input dumped and no gate/up weights given
+
+
 def test_three_part_split_is_exact():
     """the kernel's split of a float32 value into three bf16 parts (h = bf16(x), m = bf16(x - h), l = bf16(x - h - m),
     round to nearest even) loses nothing while the parts stay normal numbers: h + m + l == x for |x| >= 2^-100; below

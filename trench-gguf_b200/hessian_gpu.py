@@ -144,8 +144,15 @@ class DumpHessians:
     def __init__(self, ddir, device="cuda", chunk=8192, recompute=False, gq=None):
         self.torch = _torch()
         self.ddir, self.device, self.chunk, self.recompute = ddir, self.torch.device(device), chunk, recompute
-        self.xtx = Xtx(gq, self.device)
+        self._gq, self._xtx = gq, None
         self.layers = {}
+
+    @property
+    def xtx(self):
+        """the GPU kernel's handle, made on first use (the dump's reading needs no GPU)"""
+        if self._xtx is None:
+            self._xtx = Xtx(self._gq, self.device)
+        return self._xtx
 
     def layer(self, L):
         if L not in self.layers:
@@ -214,7 +221,7 @@ class DenseHessians:
     def __init__(self, ddir, device="cuda", chunk=8192, max_rows=0, gq=None):
         self.torch = _torch()
         self.ddir, self.device, self.chunk, self.max_rows = ddir, self.torch.device(device), chunk, max_rows
-        self.xtx = Xtx(gq, self.device)
+        self._gq, self._xtx = gq, None
         self.map = {}
         p = os.path.join(ddir, "dense.txt")
         if os.path.exists(p):
@@ -226,6 +233,13 @@ class DenseHessians:
                     self.map[w] = (fname, int(ne0), int(groups))
         self.n_embd = int(read_info(ddir).get("n_embd", "0")) if os.path.exists(os.path.join(ddir, "info.txt")) else 0
         self.cache_file, self.cache = None, None
+
+    @property
+    def xtx(self):
+        """the GPU kernel's handle, made on first use"""
+        if self._xtx is None:
+            self._xtx = Xtx(self._gq, self.device)
+        return self._xtx
 
     def _entry(self, name):
         if name in self.map:
