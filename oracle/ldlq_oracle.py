@@ -42,10 +42,12 @@ def prepare_hessian(H, n, damp=0.01, order="seq", bs=QK):
     return U, perm, d[perm], dead
 
 
-def quantize_matrix(W, quant, dequant, tsize, U=None, perm=None, imatrix=None, feedback=True, bs=QK):
+def quantize_matrix(W, quant, dequant, tsize, U=None, perm=None, imatrix=None, feedback=True, bs=QK, weights="imatrix",
+                    diag_n=None):
     """W [ne1, ne0] f32; quant(block [ne1, bs], qw [bs]) -> uint8 [ne1, tsize]; dequant(bytes) -> f32 [ne1, bs].
-    Importance weights: the imatrix entries of the block's (permuted) columns. Returns (bytes [ne1, nblk*tsize],
-    dequantized [ne1, ne0])."""
+    Importance weights (tools/ldlq.py:86-94): 'imatrix' the imatrix entries of the block's (permuted) columns, 'diag'
+    diag(H)/n of them (diag_n, already in the permuted order), 'schur' diag((U_kk^T U_kk)^-1) of the block.
+    Returns (bytes [ne1, nblk*tsize], dequantized [ne1, ne0])."""
     ne1, ne0 = W.shape
     nblk = ne0 // bs
     if perm is None:
@@ -56,7 +58,15 @@ def quantize_matrix(W, quant, dequant, tsize, U=None, perm=None, imatrix=None, f
     blk_order = perm.reshape(nblk, bs)[:, 0] // bs
     for k in range(nblk):
         cols = slice(k * bs, (k + 1) * bs)
-        qw = np.ascontiguousarray(imatrix[perm[cols]], dtype=np.float32)
+        if weights == "imatrix":
+            qw = np.ascontiguousarray(imatrix[perm[cols]], dtype=np.float32)
+        elif weights == "diag":
+            qw = np.ascontiguousarray(diag_n[cols], dtype=np.float32)
+        elif weights == "schur":
+            Ubb = U[cols, cols]
+            qw = np.ascontiguousarray(np.diag(np.linalg.inv(Ubb.T @ Ubb)), dtype=np.float32)
+        else:
+            raise ValueError(weights)
         blk = np.ascontiguousarray(Wp[:, cols])
         raw = quant(blk, qw)
         q = dequant(raw)

@@ -467,6 +467,32 @@ def test_gpu_ldlq_other_types_against_reference_loop(tables, oracle, name):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("weights", ["diag", "schur"])
+def test_gpu_ldlq_importance_modes_against_restatement(tables, oracle, weights):
+    """the loop's other importance weights (tools/ldlq.py:86-94, :414-417): diag(H)/n in the factor's column order,
+    and diag((U_kk^T U_kk)^-1) of each block, against the restatement's loop with the same U; act order"""
+    torch, G, ldlq_gpu, g = _gpu_setup(tables)
+    dev = torch.device("cuda")
+    ne1, ne0, n = 64, 1024, 4096
+    H, im = LO.synthetic_hessian(ne0, n, seed=71)
+    W = (np.random.default_rng(72).standard_t(5, (ne1, ne0)) * 0.02).astype(np.float32)
+    U, perm, diag_n, _ = LO.prepare_hessian(H, n, damp=0.01, order="act")
+    typ = G.TYPES["IQ2_XXS"]
+    gqt = ldlq_gpu.GpuQuant(g, typ)
+    out = ldlq_gpu.quantize_matrix_torch(torch.from_numpy(W[None].copy()).to(dev), gqt, U=torch.from_numpy(U).to(dev),
+                                         perm=torch.from_numpy(perm).to(dev), diag_n=torch.from_numpy(diag_n).to(dev),
+                                         imatrix=torch.from_numpy(im[None].copy()).to(dev), weights=weights
+                                         ).cpu().numpy()[0]
+    quant, dequant, tsize = LO.checker_quant(oracle, typ)
+    want, deq_w = LO.quantize_matrix(W, quant, dequant, tsize, U=U, perm=perm, imatrix=im, weights=weights,
+                                     diag_n=diag_n)
+    same = (out.reshape(ne1, -1, tsize) == want.reshape(ne1, -1, tsize)).all(-1).mean()
+    assert same >= IDENTICAL_MIN, same
+    lw = LO.proxy_loss(W, deq_w, H, n)
+    assert abs(LO.proxy_loss(W, oracle.dequantize(typ, out).reshape(ne1, ne0), H, n) - lw) <= LOSS_RTOL * lw
+
+
+@pytest.mark.gpu
 def test_gpu_experts_in_lockstep(tables):
     """ldlq_experts (every expert's factor, then one loop over all experts, one launch of each kernel a block) gives
     every expert the bytes of prepare_hessian_torch + quantize_matrix_torch run for it alone"""
