@@ -73,6 +73,28 @@ def test_prepare_hessian_dead_columns_and_act_order():
     assert np.allclose(U, np.triu(U))
 
 
+def test_ridge_ladder_matches_restatement():
+    """a normalised Hessian with an eigenvalue of -0.05 x mean(diag): the reference's first ridge (0.01 x mean) does
+    not make it positive-definite, the second (10 x more on top) does; ldlq_gpu's factorisation takes the same step
+    as the restatement of the reference's preparation (tools/ldlq.py:58-62, :313-318) and gives its U"""
+    pytest.importorskip("torch")
+    import ldlq_gpu
+    rng = np.random.default_rng(8)
+    m, n = 512, 1000
+    Q, _ = np.linalg.qr(rng.standard_normal((m, m)))
+    lam = np.ones(m)
+    lam[0] = -0.05
+    H = (Q * lam) @ Q.T * n
+    H = 0.5 * (H + H.T)
+    Hn = H / n
+    with pytest.raises(np.linalg.LinAlgError):
+        np.linalg.cholesky(Hn + 0.01 * np.mean(np.diag(Hn)) * np.eye(m))
+    U0, p0, d0, _ = LO.prepare_hessian(H, n, damp=0.01)
+    U1, p1, d1, _ = ldlq_gpu.prepare_hessian_torch(H, n, damp=0.01, device="cpu")
+    assert np.array_equal(p0, p1) and np.allclose(d0, d1, rtol=1e-12)
+    assert np.abs(U1 - U0).max() <= 1e-9 * np.abs(U0).max()
+
+
 def test_prepare_hessian_torch_equals_restatement():
     """ldlq_gpu's factorisation (one Cholesky of the order-reversed matrix and a triangular inverse by halves) gives
     the restatement's U = cholesky(inverse(cholesky(Hp)))^T in float64, with dead columns and act order"""
