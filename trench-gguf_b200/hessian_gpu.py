@@ -87,9 +87,15 @@ class Xtx:
 
 
 def _bf16_rows(u16, device):
-    """bf16 rows as stored (uint16 numpy) -> a bfloat16 tensor on the device, the bits unchanged"""
+    """bf16 rows as stored (uint16 numpy) -> a bfloat16 tensor on the device, the bits unchanged. A slice of a
+    read-only memory map is wrapped without a host copy (torch warns about its read-only buffer; the tensor is only
+    read, by the copy to the device)"""
+    import warnings
     torch = _torch()
-    return torch.from_numpy(np.ascontiguousarray(u16).view(np.int16)).to(device).view(torch.bfloat16)
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore", UserWarning)
+        host = torch.from_numpy(np.ascontiguousarray(u16).view(np.int16))
+    return host.to(device).view(torch.bfloat16)
 
 
 def read_info(ddir):
