@@ -112,8 +112,9 @@ int gpuq_device_count(void);
  * d_dst, matrix m weighted by d_imatrix row m (nmat x n_per_row floats, device; NULL for the no-imatrix types).
  * Decodes inside the quantize kernel, so the sources are the five it reads (F32, F16, BF16, Q8_0, MXFP4; others:
  * gpuq_dequantize_src_dev first); on `stream`, no synchronisation, no library scratch. d_dst must hold
- * nmat * nrow * n_per_row / block_len * gpuq_block_bytes(type) bytes, block_len being 32 for Q8_0 and IQ4_NL and
- * 256 for every other type: the kernel writes them all and cannot see the allocation. */
+ * nmat * nrow * n_per_row / block_len * gpuq_block_bytes(type) bytes, block_len being 1 for F16, 32 for Q8_0,
+ * IQ4_NL, Q4_0, Q5_0 and Q5_1, and 256 for every other type: the kernel writes them all and cannot see the
+ * allocation. The value count is a multiple of 32, except for the F16 target from an F32, F16 or BF16 source. */
 size_t gpuq_requantize_dev(int src, const void * d_raw, int type, void * d_dst, int64_t nmat, int64_t nrow,
                            int64_t n_per_row, const float * d_imatrix, void * stream);
 
