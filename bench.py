@@ -69,9 +69,6 @@ def parse():
                     help="--config 1/3/4: measure only the jobs of these types (comma list, e.g. Q8_0): profiling runs")
     ap.add_argument("--gate", action="store_true",
                     help="the 384-expert IQ2_XXS tensor, host to host, one process over every visible GPU")
-    ap.add_argument("--ldlq-streams", type=int, default=4,
-                    help="config 5: CUDA streams the experts alternate over (the next expert's factorisation runs "
-                         "beside this one's loop); 1 = one expert after another on one stream")
     ap.add_argument("--ldlq-type", default="iq2_xxs",
                     help="config 5: the target type (the reference's LDLQ_TYPES: i-quants, Q4_K, Q5_K, Q6_K, IQ4_XS)")
     ap.add_argument("--ldlq-sub", type=int, default=0, choices=[0, 32, 8],
