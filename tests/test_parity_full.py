@@ -8,7 +8,8 @@ own self-test does (gpuq/test_gpuq.py:93-124: block-wise equality per type and m
   config 1  all 229,376 IQ2_XXS blocks of the dense 4096 x 14336 f32 tensor;
   config 2  two whole 2048 x 7168 MXFP4 experts -> IQ1_S, IQ1_M, IQ2_XXS;
   config 3  two whole BF16 experts -> IQ2_XS, IQ2_S, in the gate/up shape 2048 x 7168 and the down shape 7168 x 2048;
-  config 4  64 full 28,672-wide BF16 rows -> Q2_K..Q6_K with and without an imatrix, and Q8_0.
+  config 4  64 full 28,672-wide BF16 rows -> Q2_K..Q6_K with and without an imatrix, and Q8_0; the fallback
+            targets Q4_0, Q5_0, Q5_1 (both modes) and F16 on the same rows, against the C restatement.
 """
 import os
 
@@ -101,4 +102,21 @@ def test_config4_full_rows(gpuq, checker, config4_rows, name, mode):
     want = checker.quantize(t, x, imx, threads=THREADS)
     same, n = same_blocks(got, want, gpuq.block_bytes(t))
     assert n == 64 * 28672 // (32 if name == "Q8_0" else 256)
+    assert same == n, "%s mode %d: %d of %d blocks differ" % (name, mode, n - same, n)
+
+
+@pytest.mark.parametrize("name,mode", [(n, m) for n in ("Q4_0", "Q5_0", "Q5_1") for m in (1, 0)] + [("F16", 0)])
+def test_config4_full_rows_fallback_types(gpuq, tables, config4_rows, name, mode):
+    """the fallback targets on the same 64 full 28,672-wide BF16 rows: Q4_0, Q5_0, Q5_1 with and without an imatrix,
+    and F16. The reference's host build has none of them (the reference leaves them to ggml), so the checker is the C
+    restatement, pinned to gguf-py's Q4_0/Q5_0/Q5_1 quantizers and to IEEE half rounding by the CPU tests"""
+    raw, im, x = config4_rows
+    t = orc.LEGACY[name] if name in orc.LEGACY else orc.F16
+    o = orc.Checker("oracle", tables)
+    imx = im[None] if mode else None
+    got = gpuq.requantize(30, raw, t, x.shape, imx)
+    want = o.quantize(t, x, imx)
+    bl = 1 if name == "F16" else 32
+    same, n = same_blocks(got, want, o.block_bytes(t))
+    assert n == 64 * 28672 // bl
     assert same == n, "%s mode %d: %d of %d blocks differ" % (name, mode, n - same, n)
