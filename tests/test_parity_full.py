@@ -9,7 +9,8 @@ own self-test does (gpuq/test_gpuq.py:93-124: block-wise equality per type and m
   config 2  two whole 2048 x 7168 MXFP4 experts -> IQ1_S, IQ1_M, IQ2_XXS;
   config 3  two whole BF16 experts -> IQ2_XS, IQ2_S, in the gate/up shape 2048 x 7168 and the down shape 7168 x 2048;
   config 4  64 full 28,672-wide BF16 rows -> Q2_K..Q6_K with and without an imatrix, and Q8_0; the fallback
-            targets Q4_0, Q5_0, Q5_1 (both modes) and F16 on the same rows, against the C restatement.
+            targets Q4_0, Q5_0, Q5_1 (both modes) and F16 on the same rows, against the C restatement;
+  staged    a whole 2048 x 7168 expert of NVFP4, MXFP8 rows and Q4_K -> IQ2_XXS.
 """
 import os
 
@@ -120,3 +121,24 @@ def test_config4_full_rows_fallback_types(gpuq, tables, config4_rows, name, mode
     same, n = same_blocks(got, want, o.block_bytes(t))
     assert n == 64 * 28672 // bl
     assert same == n, "%s mode %d: %d of %d blocks differ" % (name, mode, n - same, n)
+
+
+@pytest.mark.parametrize("src", ["NVFP4", "MXFP8", "Q4_K"])
+def test_staged_source_whole_expert(gpuq, tables, checker, src):
+    """a whole 2048 x 7168 expert of a staged source (NVFP4; unsloth's MXFP8 rows; a k-quant source: the reference
+    decodes these on the CPU) -> IQ2_XXS with an imatrix: every block equals the checker's on the restatement's
+    decode (pinned to gguf-py's dequantizers and, for MXFP8, the reference's own E4M3 table)"""
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    from test_gpu_quant import staged_source
+    o = orc.Checker("oracle", tables)
+    s = orc.SOURCES[src] if src in orc.SOURCES else orc.TYPES[src]
+    raw = staged_source(o, s, 1, 2048, 7168, seed=107)
+    im = np.random.default_rng(108).lognormal(0.0, 1.5, (1, 7168)).astype(np.float32)
+    x = o.decode(s, raw, 2048 * 7168).reshape(1, 2048, 7168)
+    t = orc.TYPES["IQ2_XXS"]
+    got = gpuq.requantize(s, raw, t, x.shape, im)
+    want = checker.quantize(t, x, im, threads=THREADS)
+    same, n = same_blocks(got, want, gpuq.block_bytes(t))
+    assert n == 2048 * 28
+    assert same == n, "%s: %d of %d blocks differ" % (src, n - same, n)
