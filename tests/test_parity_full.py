@@ -10,7 +10,8 @@ own self-test does (gpuq/test_gpuq.py:93-124: block-wise equality per type and m
   config 3  two whole BF16 experts -> IQ2_XS, IQ2_S, in the gate/up shape 2048 x 7168 and the down shape 7168 x 2048;
   config 4  64 full 28,672-wide BF16 rows -> Q2_K..Q6_K with and without an imatrix, and Q8_0; the fallback
             targets Q4_0, Q5_0, Q5_1 (both modes) and F16 on the same rows, against the C restatement;
-  staged    a whole 2048 x 7168 expert of NVFP4, MXFP8 rows and Q4_K -> IQ2_XXS.
+  staged    a whole 2048 x 7168 expert of NVFP4, MXFP8 rows and Q4_K -> IQ2_XXS;
+  others    config 2's two experts -> IQ3_XXS, IQ3_S, IQ2_XS, IQ2_S, IQ4_XS and IQ4_NL (both modes).
 """
 import os
 
@@ -142,3 +143,18 @@ def test_staged_source_whole_expert(gpuq, tables, checker, src):
     same, n = same_blocks(got, want, gpuq.block_bytes(t))
     assert n == 2048 * 28
     assert same == n, "%s: %d of %d blocks differ" % (src, n - same, n)
+
+
+@pytest.mark.parametrize("name,mode", [("IQ3_XXS", 1), ("IQ3_S", 1), ("IQ2_XS", 1), ("IQ2_S", 1), ("IQ4_XS", 1),
+                                       ("IQ4_XS", 0), ("IQ4_NL", 1), ("IQ4_NL", 0)])
+def test_other_types_whole_experts(gpuq, checker, config2_experts, name, mode):
+    """the types no benchmark configuration names (the 3-bit grids, IQ4_XS / IQ4_NL in both modes) on config 2's two
+    whole MXFP4 experts: every block equals the reference's"""
+    raw, im, x = config2_experts
+    t = orc.TYPES[name]
+    imx = im if mode else None
+    got = gpuq.requantize(39, raw, t, x.shape, imx)
+    want = checker.quantize(t, x, imx, threads=THREADS)
+    same, n = same_blocks(got, want, gpuq.block_bytes(t))
+    assert n == 2 * 2048 * 7168 // (32 if name == "IQ4_NL" else 256)
+    assert same == n, "%s mode %d: %d of %d blocks differ" % (name, mode, n - same, n)
